@@ -1,0 +1,124 @@
+/*
+ * oxicuda.h -- C ABI of the B200 (sm_100a) backend for oxitorch's
+ * memory-bound layer path.
+ *
+ * Every entry point is what oxitorch's Rust tensor crate (oxi-tensor) would
+ * bind through `extern "C"` to run the named reference function on device
+ * memory.  Conventions:
+ *   - all tensors are float32 in device memory unless stated;
+ *   - every call is asynchronous on `stream` (a cudaStream_t passed as
+ *     void*; NULL = legacy default stream) and never allocates: scratch comes
+ *     from a caller-provided workspace whose size is returned by the matching
+ *     *_workspace_size function;
+ *   - a call returns an oxc_status; on failure, oxc_last_error() gives the
+ *     message (thread-local), worded like the reference's error messages;
+ *   - no call panics, traps or aborts; device-side index faults are reported
+ *     through an int32 error flag that the caller reads after the stream
+ *     synchronises (oxc_check_error_flag).
+ *
+ * Reference citations are path:line within SirBlocky7747/oxitorch.
+ */
+#ifndef OXICUDA_H
+#define OXICUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------
+ * 1..5 map one-to-one onto OxitorchError (crates/oxi-core/src/lib.rs:186-208)
+ * and from there onto Python exceptions (crates/oxi-bindings/src/error.rs:22-32):
+ * 1,2 -> ValueError, 3 -> NotImplementedError, 4,5,6 -> RuntimeError.      */
+typedef int32_t oxc_status;
+#define OXC_OK 0
+#define OXC_ERR_INVALID_ARGUMENT 1
+#define OXC_ERR_SHAPE_MISMATCH 2
+#define OXC_ERR_NOT_IMPLEMENTED 3
+#define OXC_ERR_OUT_OF_BOUNDS 4
+#define OXC_ERR_OTHER 5
+#define OXC_ERR_TIMEOUT 6
+
+#define OXC_MAX_DIMS 8
+
+/* A strided view: the device counterpart of oxi-tensor's Tensor
+ * {storage, offset, View{shape, strides}} (crates/oxi-tensor/src/lib.rs:24-58).
+ * `data` points at element (0,...,0), i.e. the storage offset is applied;
+ * strides are in elements and may be 0 (broadcast dims, layout.rs:97-114). */
+typedef struct oxc_view {
+  float* data;
+  int32_t ndim;
+  int64_t shape[OXC_MAX_DIMS];
+  int64_t strides[OXC_MAX_DIMS];
+} oxc_view;
+
+/* Backward semantics of the fused norm VJPs.
+ * OXC_GRAD_REF: the reference's graph, where `.apply("rsqrt")` is not in the
+ *   differentiable whitelist (crates/oxi-bindings/src/lib.rs:682-697) and the
+ *   rsqrt factor is a detached constant.
+ * OXC_GRAD_EXACT: the full mathematical gradient (what torch computes). */
+#define OXC_GRAD_REF 0
+#define OXC_GRAD_EXACT 1
+
+/* Activation fused after a layer norm. */
+#define OXC_ACT_NONE 0
+#define OXC_ACT_GELU_TANH 1 /* python/oxitorch/nn/functional.py:194-199 */
+
+/* ---- library ---------------------------------------------------------- */
+int32_t oxc_abi_version(void);
+/* Message of the last failing call on this thread ("" if none). */
+const char* oxc_last_error(void);
+/* Number of visible CUDA devices; replaces the constant 1 of
+ * crates/oxi-bindings/src/lib.rs:781-785. */
+int32_t oxc_device_count(void);
+/* Waits for `stream` with a deadline; OXC_ERR_TIMEOUT if it has not drained
+ * after timeout_ms (negative = wait forever).  Host-side poll, never spins
+ * on the device. */
+oxc_status oxc_stream_sync(void* stream, int64_t timeout_ms);
+/* Synchronises `stream` and reads a device int32 error flag written by a
+ * kernel; returns OXC_ERR_OUT_OF_BOUNDS with the reference's message when it
+ * holds a recorded bad index (flag[0] = 1, flag[1..2] = index value as two
+ * int32 halves, flag[3] = dim size), and clears it. */
+oxc_status oxc_check_error_flag(int32_t* flag_dev, void* stream, int64_t timeout_ms);
+
+/* ---- registry ids: the order of the reference registry tables ---------
+ * binary: add,sub,mul,div,pow,min,max          (crates/oxi-tensor/src/ops.rs:55-91)
+ * cmp:    eq,ne,lt,le,gt,ge                    (ops.rs:96-121)
+ * unary:  neg,abs,sqrt,rsqrt,exp,log,log2,log10,sin,cos,tanh,relu,sigmoid,
+ *         floor,ceil,round,sign,square,reciprocal (ops.rs:125-202)
+ * reduce: sum,mean,max,min,argmax,argmin,norm  (ReduceKind, ops.rs:224-239)
+ * Lookups return -1 for unknown names (replace find_*_op, ops.rs:206-220). */
+int32_t oxc_binary_op_id(const char* name);
+int32_t oxc_cmp_op_id(const char* name);
+int32_t oxc_unary_op_id(const char* name);
+int32_t oxc_reduce_kind_id(const char* name);
+
+/* ---- RMSNorm: F.rms_norm (python/oxitorch/nn/functional.py:236-240) -------
+ * x, y, dy, dx: [rows, cols] row-major; w, dw: [cols]; rstd: [rows]
+ * (saved 1/sqrt(mean(x^2)+eps) per row). */
+oxc_status oxc_rms_norm_fwd(const float* x, const float* w, float* y, float* rstd, int64_t rows,
+                            int64_t cols, float eps, void* stream);
+size_t oxc_rms_norm_bwd_workspace_size(int64_t rows, int64_t cols);
+oxc_status oxc_rms_norm_bwd(const float* x, const float* w, const float* rstd, const float* dy,
+                            float* dx, float* dw, int64_t rows, int64_t cols, int32_t grad_mode,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- LayerNorm (+ fused activation): F.layer_norm then F.gelu -------------
+ * (functional.py:227-233, 194-199).  y is the activation output (or the
+ * layer-norm output for OXC_ACT_NONE); mean/rstd: [rows]. */
+oxc_status oxc_layer_norm_fwd(const float* x, const float* w, const float* b, float* y,
+                              float* mean, float* rstd, int64_t rows, int64_t cols, float eps,
+                              int32_t act, void* stream);
+size_t oxc_layer_norm_bwd_workspace_size(int64_t rows, int64_t cols);
+oxc_status oxc_layer_norm_bwd(const float* x, const float* w, const float* b, const float* mean,
+                              const float* rstd, const float* dy, float* dx, float* dw, float* db,
+                              int64_t rows, int64_t cols, int32_t act, int32_t grad_mode,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OXICUDA_H */

@@ -1,0 +1,803 @@
+"""CPU ORACLE (test infrastructure only) -- a restatement of oxitorch's CPU path.
+
+This module re-states, in numpy + the plain-C kernels of ``oxiref.c``, the
+parts of the reference that the memory-bound layer path runs through:
+
+* ``crates/oxi-tensor``: registry ops, broadcasting, dim/keepdim reductions,
+  ``index_select`` (values computed by ``oxiref.c`` with sequential f32 folds);
+* ``crates/oxi-autograd/src/graph.rs``: the ``Var`` DAG, its iterative DFS
+  topological order, gradient accumulation and ``unbroadcast``;
+* ``crates/oxi-autograd/src/ops.rs``: every VJP closure on the path;
+* ``crates/oxi-bindings/src/lib.rs``: the Python ``Tensor`` surface, including
+  scalar promotion to full-shape constants and the ``apply`` whitelist that
+  leaves ``rsqrt`` detached;
+* ``python/oxitorch/nn/functional.py``: the ``F.*`` compositions.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline legs of
+``bench.py`` use it, and only as the checker.  The product never imports it.
+
+Parity status: the Rust reference cannot be compiled here (no cargo), so this
+oracle is pinned against the reference's own known-answer tests
+(``tests/golden/reference_kats.json``) and against the reference's own
+``functional.py`` source executed on top of this restatement
+(``tests/golden/make_golden.py``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "liboxiref.so")
+_lib = None
+
+F32P = ctypes.POINTER(ctypes.c_float)
+I64P = ctypes.POINTER(ctypes.c_int64)
+F64P = ctypes.POINTER(ctypes.c_double)
+
+
+def build(force: bool = False) -> str:
+    """Compiles ``oxiref.c`` into ``liboxiref.so`` next to this file."""
+    src = os.path.join(_HERE, "oxiref.c")
+    if force or not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src):
+        subprocess.check_call(
+            ["gcc", "-O2", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-shared",
+             "-o", _LIB_PATH, src, "-lm"])
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        L = ctypes.CDLL(_LIB_PATH)
+        L.oxr_unary.argtypes = [ctypes.c_int, F32P, F32P, ctypes.c_int64]
+        L.oxr_binary.argtypes = [ctypes.c_int, F32P, F32P, F32P, ctypes.c_int64]
+        L.oxr_cmp.argtypes = [ctypes.c_int, F32P, F32P, F32P, ctypes.c_int64]
+        L.oxr_reduce_strips.argtypes = [ctypes.c_int, F32P, I64P, ctypes.c_int64, ctypes.c_int64,
+                                        ctypes.c_int64, F32P]
+        L.oxr_sum_all_f32.argtypes = [F32P, ctypes.c_int64]
+        L.oxr_sum_all_f32.restype = ctypes.c_float
+        L.oxr_sum_all_f64.argtypes = [F32P, ctypes.c_int64]
+        L.oxr_sum_all_f64.restype = ctypes.c_double
+        L.oxr_sumsq_all_f64.argtypes = [F32P, ctypes.c_int64]
+        L.oxr_sumsq_all_f64.restype = ctypes.c_double
+        L.oxr_colsum_abs_prod_f64.argtypes = [F32P, F32P, ctypes.c_int64, ctypes.c_int64, F64P]
+        L.oxr_index_select.argtypes = [F32P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, I64P,
+                                       ctypes.c_int64, F32P]
+        L.oxr_index_select.restype = ctypes.c_int64
+        L.oxr_scatter_index_select.argtypes = [F32P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                               I64P, ctypes.c_int64, F32P]
+        _lib = L
+    return _lib
+
+
+def _fp(a):
+    return a.ctypes.data_as(F32P)
+
+
+def _ip(a):
+    return a.ctypes.data_as(I64P)
+
+
+# ---- registry (ops.rs:55-202, order = op id) ---------------------------------
+
+BINARY_OPS = ["add", "sub", "mul", "div", "pow", "min", "max"]
+CMP_OPS = ["eq", "ne", "lt", "le", "gt", "ge"]
+UNARY_OPS = ["neg", "abs", "sqrt", "rsqrt", "exp", "log", "log2", "log10", "sin", "cos", "tanh",
+             "relu", "sigmoid", "floor", "ceil", "round", "sign", "square", "reciprocal"]
+REDUCE_KINDS = ["sum", "mean", "max", "min", "argmax", "argmin", "norm"]
+
+
+class OxiError(Exception):
+    """Mirror of OxitorchError (crates/oxi-core/src/lib.rs:186-208)."""
+
+    kind = "Other"
+
+
+class ShapeMismatch(OxiError, ValueError):
+    kind = "ShapeMismatch"
+
+
+class InvalidArgument(OxiError, ValueError):
+    kind = "InvalidArgument"
+
+
+class NotImplementedOxi(OxiError, NotImplementedError):
+    kind = "NotImplemented"
+
+
+class OutOfBounds(OxiError, RuntimeError):
+    kind = "OutOfBounds"
+
+
+# ---- layout (crates/oxi-tensor/src/layout.rs) ----------------------------------
+
+def broadcast_shapes(a, b):
+    """layout.rs:67-88."""
+    rank = max(len(a), len(b))
+    out = []
+    for i in range(rank):
+        ia = len(a) - rank + i
+        ib = len(b) - rank + i
+        da = a[ia] if ia >= 0 else 1
+        db = b[ib] if ib >= 0 else 1
+        if da != db and da != 1 and db != 1:
+            raise ShapeMismatch(f"shape mismatch: {list(a)} vs {list(b)}")
+        out.append(max(da, db))
+    return tuple(out)
+
+
+def normalize_dim(dim, ndim):
+    """layout.rs:162-179."""
+    if dim < 0:
+        d = ndim + dim
+        if d < 0:
+            raise InvalidArgument(f"invalid argument: dim {dim} out of range for {ndim}-D tensor")
+        return d
+    if dim < ndim:
+        return dim
+    raise InvalidArgument(f"invalid argument: dim {dim} out of range for {ndim}-D tensor")
+
+
+def f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+# ---- oxi-tensor Tensor methods (values only) -----------------------------------
+
+def t_binary(name, a, b):
+    """Tensor::binary_op (lib.rs:263-282, 332-336): broadcast then map."""
+    op = BINARY_OPS.index(name)
+    shape = broadcast_shapes(a.shape, b.shape)
+    aa = f32(np.broadcast_to(a, shape))
+    bb = f32(np.broadcast_to(b, shape))
+    out = np.empty(shape, np.float32)
+    lib().oxr_binary(op, _fp(aa), _fp(bb), _fp(out), out.size)
+    return out
+
+
+def t_cmp(name, a, b):
+    """Tensor::cmp_op (lib.rs:284-304, 342-347): bool results as 0.0/1.0."""
+    op = CMP_OPS.index(name)
+    shape = broadcast_shapes(a.shape, b.shape)
+    aa = f32(np.broadcast_to(a, shape))
+    bb = f32(np.broadcast_to(b, shape))
+    out = np.empty(shape, np.float32)
+    lib().oxr_cmp(op, _fp(aa), _fp(bb), _fp(out), out.size)
+    return out
+
+
+def t_unary(name, a):
+    """Tensor::unary_op (lib.rs:306-325, 353-357)."""
+    if name not in UNARY_OPS:
+        raise InvalidArgument(f'invalid argument: unknown unary op "{name}"')
+    aa = f32(a)
+    out = np.empty(aa.shape, np.float32)
+    lib().oxr_unary(UNARY_OPS.index(name), _fp(aa), _fp(out), out.size)
+    return out
+
+
+def t_reduce(kind, a, dim, keepdim):
+    """Tensor::reduce (lib.rs:519-576) over the row-major materialisation."""
+    k = REDUCE_KINDS.index(kind)
+    d = normalize_dim(dim, a.ndim)
+    strip = a.shape[d]
+    if strip == 0 and kind in ("argmax", "argmin"):
+        raise InvalidArgument("invalid argument: cannot compute argmax/argmin over a zero-length dim")
+    if strip == 0 and kind in ("max", "min"):
+        raise InvalidArgument("invalid argument: cannot compute max/min over a zero-length dim")
+    flat = f32(a)
+    outer = int(np.prod(a.shape[:d], dtype=np.int64))
+    inner = int(np.prod(a.shape[d + 1:], dtype=np.int64))
+    # strip (o, i) starts at (o*strip)*inner + i and walks with stride inner
+    offs = ((np.arange(outer, dtype=np.int64) * strip * inner)[:, None]
+            + np.arange(inner, dtype=np.int64)[None, :]).reshape(-1)
+    offs = np.ascontiguousarray(offs)
+    res = np.empty(outer * inner, np.float32)
+    rc = lib().oxr_reduce_strips(k, _fp(flat), _ip(offs), outer * inner, strip, inner, _fp(res))
+    if rc:
+        raise InvalidArgument("invalid argument: cannot compute min/max/argmax/argmin over an empty reduction")
+    shape = list(a.shape)
+    if keepdim:
+        shape[d] = 1
+    else:
+        shape.pop(d)
+    return res.reshape(shape)
+
+
+def t_reduce_strip_all(kind, a):
+    """ReduceKind::reduce_strip over every element (bindings lib.rs:138-142)."""
+    flat = f32(a).reshape(-1)
+    if flat.size == 0:
+        if kind in ("sum", "mean", "norm"):
+            return np.float32(0.0)
+        raise InvalidArgument("invalid argument: cannot compute min/max/argmax/argmin over an empty reduction")
+    res = np.empty(1, np.float32)
+    offs = np.zeros(1, np.int64)
+    lib().oxr_reduce_strips(REDUCE_KINDS.index(kind), _fp(flat), _ip(offs), 1, flat.size, 1, _fp(res))
+    return res[0]
+
+
+def t_index_select(a, dim, ids):
+    """Tensor::index_select (lib.rs:665-703)."""
+    d = normalize_dim(dim, a.ndim)
+    length = a.shape[d]
+    ids = np.ascontiguousarray(np.asarray(ids, dtype=np.int64).reshape(-1))
+    flat = f32(a)
+    outer = int(np.prod(a.shape[:d], dtype=np.int64))
+    inner = int(np.prod(a.shape[d + 1:], dtype=np.int64))
+    shape = list(a.shape)
+    shape[d] = ids.size
+    out = np.empty(shape, np.float32)
+    bad = lib().oxr_index_select(_fp(flat), outer, length, inner, _ip(ids), ids.size, _fp(out))
+    if bad:
+        i = int(ids[bad - 1])
+        raise OutOfBounds(f"out of bounds: index {i} out of range for dim {d} of size {length}")
+    return out
+
+
+def scatter_index_select(g, dim, idx, full_shape):
+    """crates/oxi-autograd/src/ops.rs:741-769 (position-order accumulation)."""
+    outer = int(np.prod(full_shape[:dim], dtype=np.int64))
+    inner = int(np.prod(full_shape[dim + 1:], dtype=np.int64))
+    out = np.empty(full_shape, np.float32)
+    gg = f32(g)
+    ids = np.ascontiguousarray(np.asarray(idx, dtype=np.int64))
+    lib().oxr_scatter_index_select(_fp(gg), outer, full_shape[dim], inner, _ip(ids), ids.size, _fp(out))
+    return out
+
+
+def full(shape, c):
+    return np.full(shape, np.float32(c), np.float32)
+
+
+# ---- Var graph (crates/oxi-autograd/src/graph.rs) -------------------------------
+
+_GRAD_ENABLED = [True]
+
+
+class Var:
+    """graph.rs:115-177: value, op name, inputs, VJP closure, grad slot."""
+
+    __slots__ = ("value", "op", "inputs", "vjp", "grad", "requires_grad")
+
+    def __init__(self, value, op, inputs, vjp, requires_grad):
+        self.value = value
+        self.op = op
+        self.inputs = inputs
+        self.vjp = vjp
+        self.grad = None
+        self.requires_grad = requires_grad
+
+    @staticmethod
+    def leaf(value, requires_grad=False):
+        return Var(value, None, [], None, requires_grad)
+
+    @staticmethod
+    def make(value, op, inputs, vjp):
+        if not _GRAD_ENABLED[0]:
+            return Var.leaf(value, False)
+        return Var(value, op, list(inputs), vjp, any(i.requires_grad for i in inputs))
+
+    def accumulate_grad(self, g):
+        """graph.rs:235-242: existing.add(g)."""
+        self.grad = g if self.grad is None else t_binary("add", self.grad, g)
+
+
+def unbroadcast(g, shape):
+    """graph.rs:274-313."""
+    shape = tuple(shape)
+    if g.ndim < len(shape):
+        raise ShapeMismatch(f"shape mismatch: {list(g.shape)} vs {list(shape)}")
+    extra = g.ndim - len(shape)
+    for i, s in enumerate(shape):
+        if g.shape[extra + i] != s and s != 1:
+            raise ShapeMismatch(f"shape mismatch: {list(g.shape)} vs {list(shape)}")
+    t = g
+    for i in range(extra):
+        t = t_reduce("sum", t, i, True)
+    for i, s in enumerate(shape):
+        if s == 1 and t.shape[i] != 1:
+            t = t_reduce("sum", t, i, True)
+    if tuple(t.shape) != shape:
+        t = t.reshape(shape)
+    return t
+
+
+def topo_order(root):
+    """graph.rs:324-348: iterative DFS with Enter/Exit frames."""
+    order, visited = [], set()
+    stack = [("enter", root)]
+    while stack:
+        kind, v = stack.pop()
+        if kind == "enter":
+            if id(v) in visited:
+                continue
+            visited.add(id(v))
+            stack.append(("exit", v))
+            for inp in v.inputs:
+                if id(inp) not in visited:
+                    stack.append(("enter", inp))
+        else:
+            order.append(v)
+    return order
+
+
+def backward(root, seed=None):
+    """graph.rs:373-438 (retain_graph = false)."""
+    if not root.requires_grad:
+        raise InvalidArgument("invalid argument: element 0 of tensors does not require grad and does not have a grad_fn")
+    if seed is None:
+        if root.value.size != 1:
+            raise InvalidArgument("invalid argument: grad can be implicitly created only for scalar outputs; pass a seed tensor")
+        seed = np.ones(root.value.shape, np.float32)
+    order = topo_order(root)
+    for node in order:
+        if node.op is not None:
+            node.grad = None
+    root.accumulate_grad(f32(seed))
+    for node in reversed(order):
+        if node.op is None:
+            continue
+        if node.grad is None:
+            raise InvalidArgument("invalid argument: internal: node reached in backward without a gradient")
+        if node.vjp is None:
+            raise InvalidArgument("invalid argument: trying to backward through the graph a second time")
+        f, node.vjp = node.vjp, None
+        grads = f(node.grad)
+        for inp, g in zip(node.inputs, grads):
+            if not inp.requires_grad:
+                continue
+            inp.accumulate_grad(unbroadcast(g, inp.value.shape))
+
+
+# ---- differentiable ops (crates/oxi-autograd/src/ops.rs) --------------------------
+
+def grad_for(g, x):
+    """ops.rs:20-24."""
+    return unbroadcast(g, x.value.shape)
+
+
+def a_add(a, b):
+    out = t_binary("add", a.value, b.value)
+    return Var.make(out, "add", [a, b], lambda g: [grad_for(g, a), grad_for(g, b)])
+
+
+def a_sub(a, b):
+    out = t_binary("sub", a.value, b.value)
+
+    def vjp(g):
+        gb = t_unary("neg", g)
+        return [grad_for(g, a), grad_for(gb, b)]
+    return Var.make(out, "sub", [a, b], vjp)
+
+
+def a_mul(a, b):
+    out = t_binary("mul", a.value, b.value)
+
+    def vjp(g):
+        ga = t_binary("mul", g, b.value)
+        gb = t_binary("mul", g, a.value)
+        return [grad_for(ga, a), grad_for(gb, b)]
+    return Var.make(out, "mul", [a, b], vjp)
+
+
+def a_div(a, b):
+    out = t_binary("div", a.value, b.value)
+
+    def vjp(g):
+        ga = t_binary("div", g, b.value)
+        b2 = t_binary("mul", b.value, b.value)
+        gb = t_unary("neg", t_binary("div", t_binary("mul", g, a.value), b2))
+        return [grad_for(ga, a), grad_for(gb, b)]
+    return Var.make(out, "div", [a, b], vjp)
+
+
+def a_pow(a, b):
+    out = t_binary("pow", a.value, b.value)
+
+    def vjp(g):
+        bm1 = t_binary("add", b.value, np.array(-1.0, np.float32))
+        apow = t_binary("pow", a.value, bm1)
+        ga = t_binary("mul", t_binary("mul", g, b.value), apow)
+        out_t = t_binary("pow", a.value, b.value)
+        loga = t_unary("log", a.value)
+        gb = t_binary("mul", t_binary("mul", g, out_t), loga)
+        return [grad_for(ga, a), grad_for(gb, b)]
+    return Var.make(out, "pow", [a, b], vjp)
+
+
+def _unary_generic(x, name, dfdx):
+    """ops.rs:132-145."""
+    out = t_unary(name, x.value)
+
+    def vjp(g):
+        gx = t_binary("mul", g, dfdx(x.value))
+        return [grad_for(gx, x)]
+    return Var.make(out, name, [x], vjp)
+
+
+def a_neg(x):
+    out = t_unary("neg", x.value)
+    return Var.make(out, "neg", [x], lambda g: [grad_for(t_unary("neg", g), x)])
+
+
+def a_abs(x):
+    return _unary_generic(x, "abs", lambda t: t_unary("sign", t))
+
+
+def a_exp(x):
+    return _unary_generic(x, "exp", lambda t: t_unary("exp", t))
+
+
+def a_log(x):
+    return _unary_generic(x, "log", lambda t: t_binary("div", np.ones(t.shape, np.float32), t))
+
+
+def a_sqrt(x):
+    def d(t):
+        denom = t_binary("mul", t_unary("sqrt", t), full(t.shape, 2.0))
+        return t_binary("div", np.ones(t.shape, np.float32), denom)
+    return _unary_generic(x, "sqrt", d)
+
+
+def a_tanh(x):
+    def d(t):
+        th = t_unary("tanh", t)
+        th2 = t_binary("mul", th, th)
+        return t_binary("sub", np.ones(t.shape, np.float32), th2)
+    return _unary_generic(x, "tanh", d)
+
+
+def a_sigmoid(x):
+    def d(t):
+        s = t_unary("sigmoid", t)
+        return t_binary("mul", s, t_binary("sub", np.ones(t.shape, np.float32), s))
+    return _unary_generic(x, "sigmoid", d)
+
+
+def a_relu(x):
+    """ops.rs:254-268."""
+    out = t_unary("relu", x.value)
+    mask = t_cmp("gt", x.value, np.zeros(x.value.shape, np.float32))
+    return Var.make(out, "relu", [x], lambda g: [grad_for(t_binary("mul", g, mask), x)])
+
+
+def _normalize_reduce_grad(g, x_shape, dim):
+    """ops.rs:679-690."""
+    if tuple(g.shape) == tuple(x_shape):
+        return g
+    padded = list(g.shape)
+    if g.ndim + 1 == len(x_shape):
+        padded.insert(min(dim, len(padded)), 1)
+    return g.reshape(padded)
+
+
+def _expand_to(t, shape):
+    """ops.rs:693-705."""
+    padded = [1] * len(shape)
+    tail = len(shape) - t.ndim
+    for i in range(len(shape)):
+        if i >= tail:
+            padded[i] = t.shape[i - tail]
+    return np.broadcast_to(t.reshape(padded), shape)
+
+
+def _scatter_along_dim(up, dim, positions, full_shape):
+    """ops.rs:710-737."""
+    data = np.zeros(full_shape, np.float32)
+    inner = int(np.prod(full_shape[dim + 1:], dtype=np.int64)) or 1
+    outer = int(np.prod(full_shape[:dim], dtype=np.int64)) or 1
+    dl = full_shape[dim]
+    flat = data.reshape(-1)
+    upf = f32(up).reshape(-1)
+    pos = np.asarray(positions, np.int64).reshape(outer, inner)
+    o = np.arange(outer)[:, None]
+    i = np.arange(inner)[None, :]
+    p = np.where(pos < 0, dl + pos, pos)
+    flat[((o * dl + p) * inner + i).reshape(-1)] = upf
+    return data
+
+
+def a_reduce(x, kind, dim, keepdim):
+    """ops.rs:327-388."""
+    out = t_reduce(kind, x.value, dim, keepdim)
+    d = normalize_dim(dim, x.value.ndim)
+    xs = x.value.shape
+    if kind == "sum":
+        def vjp(g):
+            up = _expand_to(_normalize_reduce_grad(g, xs, d), xs)
+            return [grad_for(f32(up), x)]
+        return Var.make(out, "sum", [x], vjp)
+    if kind == "mean":
+        n = np.float32(xs[d])
+
+        def vjp(g):
+            up = _expand_to(_normalize_reduce_grad(g, xs, d), xs)
+            scaled = t_binary("mul", f32(up), np.array(np.float32(1.0) / n, np.float32))
+            return [grad_for(scaled, x)]
+        return Var.make(out, "mean", [x], vjp)
+    if kind in ("max", "min"):
+        arg = t_reduce("argmax" if kind == "max" else "argmin", x.value, d, True)
+
+        def vjp(g):
+            up = _normalize_reduce_grad(g, xs, d)
+            idx = arg.reshape(-1).astype(np.int64)
+            return [grad_for(_scatter_along_dim(up, d, idx, xs), x)]
+        return Var.make(out, "maxmin", [x], vjp)
+    if kind == "norm":
+        def vjp(g):
+            up = _expand_to(_normalize_reduce_grad(g, xs, d), xs)
+            n = t_reduce("norm", x.value, d, True)
+            safe = t_binary("add", n, np.array(np.float32(1e-12), np.float32))
+            ratio = t_binary("div", x.value, safe)
+            return [grad_for(t_binary("mul", f32(up), ratio), x)]
+        return Var.make(out, "norm", [x], vjp)
+    raise NotImplementedOxi("not implemented: argmax/argmin are integer outputs and have no gradient")
+
+
+def a_reshape(x, shape):
+    out = x.value.reshape(shape)
+    orig = x.value.shape
+    return Var.make(out, "reshape", [x], lambda g: [grad_for(g.reshape(orig), x)])
+
+
+def a_index_select(x, dim, indices):
+    """ops.rs:498-517."""
+    out = t_index_select(x.value, dim, indices)
+    d = normalize_dim(dim, x.value.ndim)
+    ln = x.value.shape[d]
+    idx = [(ln + i) if i < 0 else i for i in indices]
+    return Var.make(out, "index_select", [x],
+                    lambda g: [grad_for(scatter_index_select(g, d, idx, x.value.shape), x)])
+
+
+# ---- Python Tensor surface (crates/oxi-bindings/src/lib.rs) -------------------------
+
+class Tensor:
+    """PyTensor mirror: wraps a Var; scalars become full-shape constants."""
+
+    def __init__(self, var):
+        self._v = var
+
+    # construction ----------------------------------------------------------
+    @staticmethod
+    def from_numpy(arr, requires_grad=False):
+        return Tensor(Var.leaf(np.array(arr, dtype=np.float32, copy=True), requires_grad))
+
+    # accessors ---------------------------------------------------------------
+    @property
+    def shape(self):
+        return list(self._v.value.shape)
+
+    @property
+    def ndim(self):
+        return self._v.value.ndim
+
+    @property
+    def requires_grad(self):
+        return self._v.requires_grad
+
+    @property
+    def grad(self):
+        g = self._v.grad
+        return None if g is None else Tensor(Var.leaf(g, False))
+
+    def numpy(self):
+        return np.array(self._v.value, dtype=np.float32, copy=True)
+
+    def detach(self):
+        return Tensor(Var.leaf(self._v.value, False))
+
+    def item(self):
+        return float(self._v.value.reshape(-1)[0])
+
+    def __float__(self):
+        return self.item()
+
+    def backward(self, seed=None):
+        backward(self._v, None if seed is None else f32(seed.numpy() if isinstance(seed, Tensor) else seed))
+
+    # helpers -------------------------------------------------------------------
+    def _const_full(self, c):
+        """bindings lib.rs:86-89."""
+        return Var.leaf(full(self._v.value.shape, np.float32(c)), False)
+
+    def _operand(self, other):
+        if isinstance(other, Tensor):
+            return other._v
+        if isinstance(other, (int, float, np.floating, np.integer)):
+            return self._const_full(float(other))
+        raise TypeError("operands must be oxitorch.Tensor or a Python number")
+
+    # dunders (lib.rs:213-327) ----------------------------------------------------
+    def __add__(self, o):
+        return Tensor(a_add(self._v, self._operand(o)))
+
+    __radd__ = __add__
+
+    def __sub__(self, o):
+        return Tensor(a_sub(self._v, self._operand(o)))
+
+    def __rsub__(self, o):
+        if isinstance(o, Tensor):
+            return Tensor(a_sub(o._v, self._v))
+        return Tensor(a_add(a_neg(self._v), self._const_full(o)))
+
+    def __mul__(self, o):
+        return Tensor(a_mul(self._v, self._operand(o)))
+
+    __rmul__ = __mul__
+
+    def __truediv__(self, o):
+        return Tensor(a_div(self._v, self._operand(o)))
+
+    def __rtruediv__(self, o):
+        if isinstance(o, Tensor):
+            return Tensor(a_div(o._v, self._v))
+        inv = a_pow(self._v, self._const_full(-1.0))
+        return Tensor(a_mul(inv, self._const_full(o)))
+
+    def __neg__(self):
+        return Tensor(a_neg(self._v))
+
+    def __pow__(self, o):
+        if isinstance(o, Tensor):
+            return Tensor(a_pow(self._v, o._v))
+        if self._v.requires_grad:
+            return Tensor(a_pow(self._v, self._const_full(o)))
+        return Tensor(Var.leaf(t_binary("pow", self._v.value, self._const_full(o).value), False))
+
+    # reductions (lib.rs:126-143, 454-515) ----------------------------------------
+    def _reduce_all(self, kind):
+        if self._v.requires_grad and kind in ("sum", "mean"):
+            if self.ndim == 0:
+                return Tensor(self._v)
+            v = self._v
+            for d in range(self.ndim):
+                v = a_reduce(v, kind, d, True)
+            return Tensor(a_reshape(v, ()))
+        r = t_reduce_strip_all(kind, self._v.value)
+        return Tensor(Var.leaf(np.array(r, np.float32).reshape(()), False))
+
+    def sum(self, dim=None, keepdim=False):
+        return self._reduce_all("sum") if dim is None else Tensor(a_reduce(self._v, "sum", dim, keepdim))
+
+    def mean(self, dim=None, keepdim=False):
+        return self._reduce_all("mean") if dim is None else Tensor(a_reduce(self._v, "mean", dim, keepdim))
+
+    def max(self, dim=None, keepdim=False):
+        return self._reduce_all("max") if dim is None else Tensor(a_reduce(self._v, "max", dim, keepdim))
+
+    def min(self, dim=None, keepdim=False):
+        return self._reduce_all("min") if dim is None else Tensor(a_reduce(self._v, "min", dim, keepdim))
+
+    def argmax(self, dim, keepdim=False):
+        return Tensor(Var.leaf(t_reduce("argmax", self._v.value, dim, keepdim), False))
+
+    def argmin(self, dim, keepdim=False):
+        return Tensor(Var.leaf(t_reduce("argmin", self._v.value, dim, keepdim), False))
+
+    def norm(self, dim, keepdim=False):
+        return Tensor(a_reduce(self._v, "norm", dim, keepdim))
+
+    # views / indexing ----------------------------------------------------------
+    def reshape(self, shape):
+        return Tensor(a_reshape(self._v, tuple(shape)))
+
+    def index_select(self, dim, indices):
+        if self._v.requires_grad:
+            return Tensor(a_index_select(self._v, dim, list(indices)))
+        return Tensor(Var.leaf(t_index_select(self._v.value, dim, indices), False))
+
+    def gather(self, indices):
+        return self.index_select(0, indices)
+
+    # apply (lib.rs:682-710): only whitelisted unaries stay in the graph ----------
+    _DIFF = {"relu": a_relu, "sigmoid": a_sigmoid, "tanh": a_tanh, "exp": a_exp, "log": a_log,
+             "sqrt": a_sqrt, "neg": a_neg, "abs": a_abs}
+
+    def apply(self, name):
+        if self._v.requires_grad and name in self._DIFF:
+            return Tensor(self._DIFF[name](self._v))
+        return Tensor(Var.leaf(t_unary(name, self._v.value), False))
+
+
+def from_numpy(arr, requires_grad=False):
+    return Tensor.from_numpy(arr, requires_grad)
+
+
+# ---- F.* compositions (python/oxitorch/nn/functional.py:182-293) -----------------------
+
+def gelu(x):
+    """functional.py:194-199 (tanh approximation, composed)."""
+    c = np.sqrt(2.0 / np.pi)
+    x32 = x * x
+    inner = (x + x * x32 * 0.044715) * float(c)
+    return 0.5 * x * (1.0 + inner.apply("tanh"))
+
+
+def silu(x):
+    """functional.py:202-204."""
+    return x * x.apply("sigmoid")
+
+
+def softmax(x, dim=-1):
+    """functional.py:211-215."""
+    m = x.max(dim, True)
+    e = (x - m).apply("exp")
+    return e / e.sum(dim, True)
+
+
+def log_softmax(x, dim=-1):
+    """functional.py:218-222."""
+    m = x.max(dim, True)
+    z = x - m
+    return z - z.apply("exp").sum(dim, True).apply("log")
+
+
+def layer_norm(x, weight, bias, eps=1e-5):
+    """functional.py:227-233 (rsqrt is detached by the apply whitelist)."""
+    mu = x.mean(-1, True)
+    centered = x - mu
+    var = (centered * centered).mean(-1, True)
+    inv = (var + float(eps)).apply("rsqrt")
+    return centered * inv * weight + bias
+
+
+def rms_norm(x, weight, eps=1e-6):
+    """functional.py:236-240."""
+    ms = (x * x).mean(-1, True)
+    inv = (ms + float(eps)).apply("rsqrt")
+    return x * inv * weight
+
+
+def embedding(indices, weight):
+    """functional.py:245-247."""
+    return weight.index_select(0, indices)
+
+
+def cross_entropy(logits, targets):
+    """functional.py:277-293 (dense one-hot pick, mean over the batch)."""
+    ls = log_softmax(logits, -1)
+    n, classes = logits.shape
+    if len(targets) != n:
+        raise ValueError(f"{len(targets)} targets for batch of {n}")
+    onehot = np.zeros((n, classes), dtype=np.float32)
+    onehot[np.arange(n), targets] = 1.0
+    picked = (from_numpy(onehot) * ls).sum(-1)
+    return picked.mean().apply("neg")
+
+
+# ---- whole-tensor yardsticks --------------------------------------------------------------
+
+def sum_all_f32(a):
+    a = f32(a).reshape(-1)
+    return float(lib().oxr_sum_all_f32(_fp(a), a.size))
+
+
+def sum_all_f64(a):
+    a = f32(a).reshape(-1)
+    return float(lib().oxr_sum_all_f64(_fp(a), a.size))
+
+
+def sumsq_all_f64(a):
+    a = f32(a).reshape(-1)
+    return float(lib().oxr_sumsq_all_f64(_fp(a), a.size))
+
+
+def colsum_abs_prod_f64(a, b=None):
+    """Per-column sum over rows of |a*b| (or |a|): the condition number used
+    to scale absolute tolerances of column reductions."""
+    a = f32(a)
+    rows, cols = a.shape
+    out = np.empty(cols, np.float64)
+    bb = None if b is None else f32(np.broadcast_to(b, a.shape))
+    lib().oxr_colsum_abs_prod_f64(_fp(a), None if bb is None else _fp(bb), rows, cols,
+                                  out.ctypes.data_as(F64P))
+    return out

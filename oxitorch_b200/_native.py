@@ -1,0 +1,125 @@
+"""ctypes binding of liboxicuda.so (the C ABI declared in include/oxicuda.h).
+
+The library is loaded from this package directory.  There is no fallback:
+if the shared library is missing or no CUDA device is visible, every entry
+point raises, so a device tensor can never silently run on the CPU.
+
+Status codes map onto Python exceptions the way the reference maps
+OxitorchError (crates/oxi-bindings/src/error.rs:22-32): InvalidArgument and
+ShapeMismatch -> ValueError, NotImplemented -> NotImplementedError, the rest
+-> RuntimeError.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboxicuda.so")
+
+OK = 0
+ERR_INVALID_ARGUMENT = 1
+ERR_SHAPE_MISMATCH = 2
+ERR_NOT_IMPLEMENTED = 3
+ERR_OUT_OF_BOUNDS = 4
+ERR_OTHER = 5
+ERR_TIMEOUT = 6
+
+GRAD_REF = 0
+GRAD_EXACT = 1
+ACT_NONE = 0
+ACT_GELU_TANH = 1
+
+MAX_DIMS = 8
+
+
+class View(ctypes.Structure):
+    """struct oxc_view: data pointer, ndim, shape[8], strides[8] (elements)."""
+
+    _fields_ = [
+        ("data", ctypes.c_void_p),
+        ("ndim", ctypes.c_int32),
+        ("shape", ctypes.c_int64 * MAX_DIMS),
+        ("strides", ctypes.c_int64 * MAX_DIMS),
+    ]
+
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I32 = ctypes.c_int32
+_F32 = ctypes.c_float
+_SZ = ctypes.c_size_t
+_VP = ctypes.POINTER(View)
+
+# name -> (restype, argtypes); one line per entry point of include/oxicuda.h
+SIGNATURES = {
+    "oxc_abi_version": (_I32, []),
+    "oxc_last_error": (ctypes.c_char_p, []),
+    "oxc_device_count": (_I32, []),
+    "oxc_stream_sync": (_I32, [_P, _I64]),
+    "oxc_check_error_flag": (_I32, [_P, _P, _I64]),
+    "oxc_binary_op_id": (_I32, [ctypes.c_char_p]),
+    "oxc_cmp_op_id": (_I32, [ctypes.c_char_p]),
+    "oxc_unary_op_id": (_I32, [ctypes.c_char_p]),
+    "oxc_reduce_kind_id": (_I32, [ctypes.c_char_p]),
+    "oxc_rms_norm_fwd": (_I32, [_P, _P, _P, _P, _I64, _I64, _F32, _P]),
+    "oxc_rms_norm_bwd_workspace_size": (_SZ, [_I64, _I64]),
+    "oxc_rms_norm_bwd": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _P, _SZ, _P]),
+    "oxc_layer_norm_fwd": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _F32, _I32, _P]),
+    "oxc_layer_norm_bwd_workspace_size": (_SZ, [_I64, _I64]),
+    "oxc_layer_norm_bwd": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _I32,
+                                  _P, _SZ, _P]),
+}
+
+_lib = None
+
+
+def load(require_device: bool = True):
+    """Loads the library (once).  Raises if it is missing; with
+    ``require_device`` also raises when no CUDA device is visible."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"oxitorch_b200: {LIB_PATH} is not built; run `python -c "
+                "'import __graft_entry__ as g; g.build()'` (there is no CPU fallback)")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    if require_device and _lib.oxc_device_count() <= 0:
+        raise RuntimeError("oxitorch_b200: no CUDA device is visible (there is no CPU fallback)")
+    return _lib
+
+
+def last_error() -> str:
+    msg = load(False).oxc_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(status: int, what: str = "") -> None:
+    """Raises the reference's exception type for a failing status."""
+    if status == OK:
+        return
+    msg = last_error() or f"{what}: status {status}"
+    if status in (ERR_INVALID_ARGUMENT, ERR_SHAPE_MISMATCH):
+        raise ValueError(msg)
+    if status == ERR_NOT_IMPLEMENTED:
+        raise NotImplementedError(msg)
+    raise RuntimeError(msg)
+
+
+def make_view(t) -> View:
+    """oxc_view of a torch CUDA float32 tensor (any strides, offset applied)."""
+    if t.dim() > MAX_DIMS:
+        raise NotImplementedError(f"not implemented: tensors of rank {t.dim()} > {MAX_DIMS}")
+    v = View()
+    v.data = t.data_ptr()
+    v.ndim = t.dim()
+    for i, (s, st) in enumerate(zip(t.shape, t.stride())):
+        v.shape[i] = s
+        v.strides[i] = st
+    return v

@@ -1,0 +1,77 @@
+"""Builds liboxicuda.so (the C-ABI CUDA library) in-tree for sm_100a.
+
+Each ``csrc/*.cu`` is compiled separately (in parallel) with nvcc and linked
+into ``oxitorch_b200/liboxicuda.so``.  Flags:
+
+* ``-gencode arch=compute_100a,code=sm_100a``: B200 only, no PTX fallback;
+* ``--fmad=false``: no contraction of a*b+c into FMA, because the reference's
+  Rust arithmetic never contracts and the kernels reproduce its rounding
+  sequence (FMAs the kernels want are written explicitly);
+* ``-lineinfo``: source-level attribution in ncu.
+"""
+
+from __future__ import annotations
+
+import concurrent.futures as cf
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+CSRC = os.path.join(HERE, "csrc")
+BUILD = os.path.join(HERE, "_build")
+LIB = os.path.join(HERE, "liboxicuda.so")
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "--fmad=false", "-std=c++17",
+    "-Xcompiler", "-fPIC", "-Xcompiler", "-O2",
+    "-I", os.path.join(ROOT, "include"), "-I", CSRC,
+]
+
+
+def sources():
+    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cu"))
+
+
+def _headers_mtime():
+    hs = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cuh", ".h"))]
+    hs.append(os.path.join(ROOT, "include", "oxicuda.h"))
+    return max(os.path.getmtime(h) for h in hs)
+
+
+def _compile(src, extra, verbose):
+    obj = os.path.join(BUILD, os.path.basename(src)[:-3] + ".o")
+    if (os.path.exists(obj) and os.path.getmtime(obj) >= os.path.getmtime(src)
+            and os.path.getmtime(obj) >= _headers_mtime()):
+        return obj
+    cmd = [NVCC, *NVCC_FLAGS, *extra, "-c", src, "-o", obj]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed for {src}:\n{res.stdout}\n{res.stderr}")
+    if res.stderr.strip() and verbose:
+        print(res.stderr, file=sys.stderr)
+    return obj
+
+
+def build(verbose: bool = False, ptxas_info: bool = False) -> str:
+    os.makedirs(BUILD, exist_ok=True)
+    extra = ["-Xptxas", "-v"] if ptxas_info else []
+    srcs = sources()
+    with cf.ThreadPoolExecutor(max_workers=min(8, len(srcs))) as ex:
+        objs = list(ex.map(lambda s: _compile(s, extra, verbose), srcs))
+    if (not os.path.exists(LIB)
+            or any(os.path.getmtime(o) > os.path.getmtime(LIB) for o in objs)):
+        cmd = [NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", LIB, *objs]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.check_call(cmd)
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(verbose="-v" in sys.argv, ptxas_info="--ptxas" in sys.argv))

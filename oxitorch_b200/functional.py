@@ -1,0 +1,186 @@
+"""Device-side mirror of oxitorch's ``F.*`` layer functions.
+
+Same names, argument meaning and error behaviour as
+``python/oxitorch/nn/functional.py`` for the memory-bound layers; each call is
+one fused CUDA kernel through liboxicuda.so, and its VJP is one fused kernel
+(plus a deterministic column-sum finisher for weight gradients).  Tensors are
+torch CUDA float32 tensors: torch supplies device memory, the stream and the
+autograd graph bookkeeping (``torch.autograd.Function``); all arithmetic on
+the path is ours.
+
+``grad_mode`` selects the backward semantics of the norms:
+``"ref"`` (default) reproduces the reference graph, where ``rsqrt`` is
+detached (crates/oxi-bindings/src/lib.rs:682-697); ``"exact"`` is the full
+mathematical gradient.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _native as N
+
+_MODES = {"ref": N.GRAD_REF, "exact": N.GRAD_EXACT}
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _require_cuda_f32(name, t):
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch CUDA tensor")
+    if not t.is_cuda:
+        raise ValueError(f"invalid argument: {name} must live on a CUDA device "
+                         "(oxitorch_b200 has no CPU path)")
+    if t.dtype != torch.float32:
+        raise ValueError(f"invalid argument: {name} must be float32, got {t.dtype}")
+
+
+def _rows_cols(x):
+    if x.dim() == 0:
+        raise ValueError("invalid argument: dim -1 out of range for 0-D tensor")
+    cols = x.shape[-1]
+    rows = x.numel() // cols if cols else 0
+    return rows, cols
+
+
+def _row_major(name, t):
+    if not t.is_contiguous():
+        raise ValueError(f"invalid argument: {name} must be contiguous for the fused row kernels")
+    return t
+
+
+def _vector(name, t, cols):
+    """A [cols] parameter; a broadcast view with zero row strides is accepted
+    and read through its first row (no copy)."""
+    if t.dim() >= 1 and t.shape[-1] == cols and all(s == 0 for s in t.stride()[:-1]):
+        t = t.reshape(-1)[:cols] if t.dim() == 1 else t.select(0, 0) if t.dim() == 2 else t
+    if t.dim() != 1 or t.shape[0] != cols:
+        raise ValueError(f"shape mismatch: {list(t.shape)} vs [{cols}]")
+    if t.stride(0) != 1:
+        raise ValueError(f"invalid argument: {name} must be contiguous")
+    return t
+
+
+def _workspace(nbytes, device):
+    return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=device)
+
+
+# ---- RMSNorm ---------------------------------------------------------------------
+
+def rms_norm_fwd(x, weight, eps=1e-6):
+    """Returns (y, rstd) for x [..., cols]."""
+    _require_cuda_f32("x", x)
+    _require_cuda_f32("weight", weight)
+    x = _row_major("x", x)
+    rows, cols = _rows_cols(x)
+    weight = _vector("weight", weight, cols)
+    y = torch.empty_like(x)
+    rstd = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device)
+    L = N.load()
+    N.check(L.oxc_rms_norm_fwd(x.data_ptr(), weight.data_ptr(), y.data_ptr(), rstd.data_ptr(),
+                               rows, cols, float(eps), _stream()), "rms_norm")
+    return y, rstd
+
+
+def rms_norm_bwd(x, weight, rstd, dy, grad_mode="ref"):
+    """Returns (dx, dweight)."""
+    rows, cols = _rows_cols(x)
+    weight = _vector("weight", weight, cols)
+    dy = _row_major("dy", dy)
+    dx = torch.empty_like(x)
+    dw = torch.empty(cols, dtype=torch.float32, device=x.device)
+    L = N.load()
+    ws_bytes = L.oxc_rms_norm_bwd_workspace_size(rows, cols)
+    ws = _workspace(ws_bytes, x.device)
+    N.check(L.oxc_rms_norm_bwd(x.data_ptr(), weight.data_ptr(), rstd.data_ptr(), dy.data_ptr(),
+                               dx.data_ptr(), dw.data_ptr(), rows, cols, _MODES[grad_mode],
+                               ws.data_ptr(), ws.numel(), _stream()), "rms_norm backward")
+    return dx, dw
+
+
+class _RMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, eps, grad_mode):
+        y, rstd = rms_norm_fwd(x, weight, eps)
+        ctx.save_for_backward(x, weight, rstd)
+        ctx.grad_mode = grad_mode
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, weight, rstd = ctx.saved_tensors
+        dx, dw = rms_norm_bwd(x, weight, rstd, dy.contiguous(), ctx.grad_mode)
+        return dx, dw.reshape(weight.shape), None, None
+
+
+def rms_norm(x, weight, eps=1e-6, grad_mode="ref"):
+    """F.rms_norm (python/oxitorch/nn/functional.py:236-240): x / rms(x) * weight."""
+    return _RMSNorm.apply(x, weight, eps, grad_mode)
+
+
+# ---- LayerNorm (+ GELU) --------------------------------------------------------------
+
+def layer_norm_fwd(x, weight, bias, eps=1e-5, act=N.ACT_NONE):
+    """Returns (y, mean, rstd); y = act(layer_norm(x))."""
+    _require_cuda_f32("x", x)
+    _require_cuda_f32("weight", weight)
+    _require_cuda_f32("bias", bias)
+    x = _row_major("x", x)
+    rows, cols = _rows_cols(x)
+    weight = _vector("weight", weight, cols)
+    bias = _vector("bias", bias, cols)
+    y = torch.empty_like(x)
+    mean = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device)
+    rstd = torch.empty_like(mean)
+    L = N.load()
+    N.check(L.oxc_layer_norm_fwd(x.data_ptr(), weight.data_ptr(), bias.data_ptr(), y.data_ptr(),
+                                 mean.data_ptr(), rstd.data_ptr(), rows, cols, float(eps), act,
+                                 _stream()), "layer_norm")
+    return y, mean, rstd
+
+
+def layer_norm_bwd(x, weight, bias, mean, rstd, dy, act=N.ACT_NONE, grad_mode="ref"):
+    """Returns (dx, dweight, dbias)."""
+    rows, cols = _rows_cols(x)
+    weight = _vector("weight", weight, cols)
+    bias = _vector("bias", bias, cols)
+    dy = _row_major("dy", dy)
+    dx = torch.empty_like(x)
+    dw = torch.empty(cols, dtype=torch.float32, device=x.device)
+    db = torch.empty_like(dw)
+    L = N.load()
+    ws = _workspace(L.oxc_layer_norm_bwd_workspace_size(rows, cols), x.device)
+    N.check(L.oxc_layer_norm_bwd(x.data_ptr(), weight.data_ptr(), bias.data_ptr(), mean.data_ptr(),
+                                 rstd.data_ptr(), dy.data_ptr(), dx.data_ptr(), dw.data_ptr(),
+                                 db.data_ptr(), rows, cols, act, _MODES[grad_mode], ws.data_ptr(),
+                                 ws.numel(), _stream()), "layer_norm backward")
+    return dx, dw, db
+
+
+class _LayerNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias, eps, act, grad_mode):
+        y, mean, rstd = layer_norm_fwd(x, weight, bias, eps, act)
+        ctx.save_for_backward(x, weight, bias, mean, rstd)
+        ctx.act, ctx.grad_mode = act, grad_mode
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, weight, bias, mean, rstd = ctx.saved_tensors
+        dx, dw, db = layer_norm_bwd(x, weight, bias, mean, rstd, dy.contiguous(), ctx.act,
+                                    ctx.grad_mode)
+        return dx, dw.reshape(weight.shape), db.reshape(bias.shape), None, None, None
+
+
+def layer_norm(x, weight, bias, eps=1e-5, grad_mode="ref"):
+    """F.layer_norm (functional.py:227-233) over the last dim with affine weight/bias."""
+    return _LayerNorm.apply(x, weight, bias, eps, N.ACT_NONE, grad_mode)
+
+
+def layer_norm_gelu(x, weight, bias, eps=1e-5, grad_mode="ref"):
+    """F.gelu(F.layer_norm(x, weight, bias, eps)) as one fused kernel each way
+    (functional.py:227-233 then 194-199)."""
+    return _LayerNorm.apply(x, weight, bias, eps, N.ACT_GELU_TANH, grad_mode)

@@ -1,0 +1,53 @@
+"""Comparison helpers for the parity tests.
+
+Tolerances (from the project's parity contract):
+* integer, index and copy results: bit-exact;
+* fp32 results: |got - want| <= atol + rtol * |want| with rtol 1e-5, atol 1e-6;
+* reductions over >= 32k elements and duplicate-id gradient accumulation:
+  rtol 1e-4;
+* outputs that are sums (column sums such as dweight/dbias, row sums): the
+  reference folds left to right in f32 while the kernels use fixed-order
+  trees, so the absolute term is scaled by the sum's condition number:
+  atol = 1e-6 * sum(|terms|) (each test states the terms).
+"""
+
+import numpy as np
+
+RTOL = 1e-5
+ATOL = 1e-6
+RTOL_BIG = 1e-4
+
+
+def assert_close(got, want, rtol=RTOL, atol=ATOL, what=""):
+    got = np.asarray(got, dtype=np.float64)
+    want = np.asarray(want, dtype=np.float64)
+    assert got.shape == want.shape, f"{what}: shape {got.shape} != {want.shape}"
+    atol = np.broadcast_to(np.asarray(atol, dtype=np.float64), want.shape)
+    nan_ok = np.isnan(got) == np.isnan(want)
+    assert nan_ok.all(), f"{what}: NaN pattern differs"
+    fin = ~np.isnan(want)
+    err = np.abs(got - want)
+    lim = atol + rtol * np.abs(want)
+    bad = fin & ~(err <= lim)
+    if bad.any():
+        i = np.unravel_index(np.argmax(np.where(fin, err - lim, -np.inf)), want.shape)
+        raise AssertionError(
+            f"{what}: {int(bad.sum())}/{want.size} elements out of tolerance "
+            f"(rtol={rtol}); worst at {i}: got {got[i]!r} want {want[i]!r} "
+            f"err {err[i]:.3e} limit {lim[i]:.3e}")
+
+
+def assert_bitexact(got, want, what=""):
+    got = np.asarray(got)
+    want = np.asarray(want)
+    assert got.shape == want.shape, f"{what}: shape {got.shape} != {want.shape}"
+    if got.dtype.kind == "f":
+        same = (got.view(np.uint32 if got.dtype == np.float32 else np.uint64)
+                == want.astype(got.dtype).view(np.uint32 if got.dtype == np.float32 else np.uint64))
+        same |= np.isnan(got) & np.isnan(want)
+    else:
+        same = got == want
+    if not same.all():
+        i = np.unravel_index(np.argmin(same), same.shape)
+        raise AssertionError(f"{what}: {int((~same).sum())}/{same.size} elements differ; "
+                             f"first at {i}: got {got[i]!r} want {want[i]!r}")

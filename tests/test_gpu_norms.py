@@ -1,0 +1,216 @@
+"""RMSNorm and LayerNorm(+GELU) kernels vs the oracle and the golden fixtures.
+
+Tolerances: see tests/parity.py.  dweight/dbias are column sums over rows, so
+their absolute tolerance is 1e-6 * sum_rows |term| (the term each test names).
+"""
+
+import numpy as np
+import pytest
+
+from parity import RTOL, ATOL, assert_close, assert_bitexact
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _host(t):
+    return t.detach().cpu().numpy()
+
+
+def _rms_case(seed, m, n):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((m, n), dtype=np.float32)
+    w = rng.uniform(0.5, 1.5, n).astype(np.float32)
+    dy = rng.standard_normal((m, n), dtype=np.float32)
+    return x, w, dy
+
+
+def _oracle_rms(oracle, x, w, dy, eps=1e-6):
+    xt, wt = oracle.from_numpy(x, True), oracle.from_numpy(w, True)
+    y = oracle.rms_norm(xt, wt, eps)
+    y.backward(dy)
+    return y.numpy(), xt.grad.numpy(), wt.grad.numpy()
+
+
+def _check_rms(x, w, dy, y, dx, dw, y_ref, dx_ref, dw_ref, rstd):
+    assert_close(y, y_ref, what="y")
+    assert_close(dx, dx_ref, what="dx")
+    t1 = x * rstd[:, None]
+    scale = np.abs(dy.astype(np.float64) * t1).sum(0)
+    assert_close(dw, dw_ref, atol=ATOL * np.maximum(scale, 1.0), what="dw")
+
+
+@pytest.mark.parametrize("name", ["rms_4x4096", "rms_7x1001", "rms_3x4"])
+def test_rms_norm_golden(golden, name):
+    from oxitorch_b200 import functional as F
+    g = {k.split(".", 1)[1]: v for k, v in golden.items() if k.startswith(name + ".")}
+    y, rstd = F.rms_norm_fwd(_dev(g["x"]), _dev(g["w"]), 1e-6)
+    dx, dw = F.rms_norm_bwd(_dev(g["x"]), _dev(g["w"]), rstd, _dev(g["dy"]))
+    _check_rms(g["x"], g["w"], g["dy"], _host(y), _host(dx), _host(dw), g["y"], g["dx"], g["dw"],
+               _host(rstd))
+
+
+@pytest.mark.parametrize("m,n", [(256, 4096), (33, 4095), (5, 32768), (64, 11008), (1, 1), (2, 17)])
+def test_rms_norm_vs_oracle(oracle, m, n):
+    from oxitorch_b200 import functional as F
+    x, w, dy = _rms_case(m * 7 + n, m, n)
+    y_ref, dx_ref, dw_ref = _oracle_rms(oracle, x, w, dy)
+    y, rstd = F.rms_norm_fwd(_dev(x), _dev(w), 1e-6)
+    dx, dw = F.rms_norm_bwd(_dev(x), _dev(w), rstd, _dev(dy))
+    _check_rms(x, w, dy, _host(y), _host(dx), _host(dw), y_ref, dx_ref, dw_ref, _host(rstd))
+
+
+def test_rms_norm_config1_full_size(oracle):
+    """x [4096, 4096] ~ N(0,1), w ~ U(0.5,1.5), eps 1e-6."""
+    from oxitorch_b200 import functional as F
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((4096, 4096), dtype=np.float32)
+    w = rng.uniform(0.5, 1.5, 4096).astype(np.float32)
+    dy = rng.standard_normal((4096, 4096), dtype=np.float32)
+    y_ref, dx_ref, dw_ref = _oracle_rms(oracle, x, w, dy)
+    y, rstd = F.rms_norm_fwd(_dev(x), _dev(w), 1e-6)
+    dx, dw = F.rms_norm_bwd(_dev(x), _dev(w), rstd, _dev(dy))
+    _check_rms(x, w, dy, _host(y), _host(dx), _host(dw), y_ref, dx_ref, dw_ref, _host(rstd))
+
+
+def test_rms_norm_exact_mode_vs_torch_autograd():
+    """OXC_GRAD_EXACT is the full gradient: compare with torch fp64 autograd."""
+    import torch
+    from oxitorch_b200 import functional as F
+    x, w, dy = _rms_case(9, 64, 1024)
+    xd = torch.from_numpy(x).double().requires_grad_()
+    wd = torch.from_numpy(w).double().requires_grad_()
+    yd = xd * torch.rsqrt((xd * xd).mean(-1, keepdim=True) + 1e-6) * wd
+    yd.backward(torch.from_numpy(dy).double())
+    xg, wg = _dev(x).requires_grad_(), _dev(w).requires_grad_()
+    y = F.rms_norm(xg, wg, 1e-6, grad_mode="exact")
+    y.backward(_dev(dy))
+    assert_close(_host(y), yd.detach().numpy(), what="y")
+    assert_close(_host(xg.grad), xd.grad.numpy(), rtol=1e-4, atol=1e-5, what="dx exact")
+    assert_close(_host(wg.grad), wd.grad.numpy(), rtol=1e-4, atol=1e-4, what="dw exact")
+
+
+def test_rms_norm_autograd_and_determinism():
+    from oxitorch_b200 import functional as F
+    x, w, dy = _rms_case(11, 300, 4096)
+    outs = []
+    for _ in range(2):
+        xg, wg = _dev(x).requires_grad_(), _dev(w).requires_grad_()
+        F.rms_norm(xg, wg).backward(_dev(dy))
+        outs.append((_host(xg.grad), _host(wg.grad)))
+    assert_bitexact(outs[0][0], outs[1][0], "dx run-to-run")
+    assert_bitexact(outs[0][1], outs[1][1], "dw run-to-run")
+
+
+def _ln_case(seed, m, n):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((m, n), dtype=np.float32)
+    w = rng.uniform(0.5, 1.5, n).astype(np.float32)
+    b = (rng.standard_normal(n, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
+    dy = rng.standard_normal((m, n), dtype=np.float32)
+    return x, w, b, dy
+
+
+def _oracle_ln(oracle, x, w, b, dy, gelu):
+    xt, wt, bt = oracle.from_numpy(x, True), oracle.from_numpy(w, True), oracle.from_numpy(b, True)
+    y = oracle.layer_norm(xt, wt, bt, 1e-5)
+    if gelu:
+        y = oracle.gelu(y)
+    y.backward(dy)
+    return y.numpy(), xt.grad.numpy(), wt.grad.numpy(), bt.grad.numpy()
+
+
+def _ln_dev(x, w, b, dy, gelu, mode="ref"):
+    from oxitorch_b200 import functional as F
+    from oxitorch_b200 import _native as N
+    act = N.ACT_GELU_TANH if gelu else N.ACT_NONE
+    y, mean, rstd = F.layer_norm_fwd(_dev(x), _dev(w), _dev(b), 1e-5, act)
+    dx, dw, db = F.layer_norm_bwd(_dev(x), _dev(w), _dev(b), mean, rstd, _dev(dy), act, mode)
+    return _host(y), _host(dx), _host(dw), _host(db), _host(mean), _host(rstd)
+
+
+def _check_ln(x, dy, got, ref, gelu):
+    y, dx, dw, db, mean, rstd = got
+    y_ref, dx_ref, dw_ref, db_ref = ref
+    assert_close(y, y_ref, what="y")
+    assert_close(dx, dx_ref, what="dx")
+    # dweight terms: g * xhat; dbias terms: g, with |g| <= ~1.2 |dy| for GELU
+    t1 = (x - mean[:, None]) * rstd[:, None]
+    g_scale = np.abs(dy.astype(np.float64)) * (1.2 if gelu else 1.0)
+    assert_close(dw, dw_ref, atol=ATOL * np.maximum((g_scale * np.abs(t1)).sum(0), 1.0), what="dw")
+    assert_close(db, db_ref, atol=ATOL * np.maximum(g_scale.sum(0), 1.0), what="db")
+
+
+@pytest.mark.parametrize("name,gelu", [("lngelu_4x4096", True), ("lngelu_5x777", True),
+                                       ("ln_6x512", False)])
+def test_layer_norm_golden(golden, name, gelu):
+    g = {k.split(".", 1)[1]: v for k, v in golden.items() if k.startswith(name + ".")}
+    got = _ln_dev(g["x"], g["w"], g["b"], g["dy"], gelu)
+    _check_ln(g["x"], g["dy"], got, (g["y"], g["dx"], g["dw"], g["db"]), gelu)
+
+
+@pytest.mark.parametrize("m,n,gelu", [(128, 4096, True), (40, 4095, True), (3, 32768, True),
+                                      (50, 11008, False), (1, 1, True), (9, 33, False)])
+def test_layer_norm_vs_oracle(oracle, m, n, gelu):
+    x, w, b, dy = _ln_case(m * 13 + n, m, n)
+    ref = _oracle_ln(oracle, x, w, b, dy, gelu)
+    _check_ln(x, dy, _ln_dev(x, w, b, dy, gelu), ref, gelu)
+
+
+def test_layer_norm_gelu_config2_rows(oracle):
+    """BASELINE config 2 shapes (cols 4096, eps 1e-5, seed 2) on 2048 of the
+    16384 rows (the composed oracle takes ~1 s per 1M elements)."""
+    rng = np.random.default_rng(2)
+    m, n = 2048, 4096
+    x = rng.standard_normal((m, n), dtype=np.float32)
+    w = rng.uniform(0.5, 1.5, n).astype(np.float32)
+    b = (rng.standard_normal(n, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
+    dy = rng.standard_normal((m, n), dtype=np.float32)
+    ref = _oracle_ln(oracle, x, w, b, dy, True)
+    _check_ln(x, dy, _ln_dev(x, w, b, dy, True), ref, True)
+
+
+def test_layer_norm_exact_mode_vs_torch_autograd():
+    import torch
+    x, w, b, dy = _ln_case(21, 64, 1024)
+    xd = torch.from_numpy(x).double().requires_grad_()
+    wd = torch.from_numpy(w).double().requires_grad_()
+    bd = torch.from_numpy(b).double().requires_grad_()
+    yd = torch.nn.functional.gelu(
+        torch.nn.functional.layer_norm(xd, (1024,), wd, bd, 1e-5), approximate="tanh")
+    yd.backward(torch.from_numpy(dy).double())
+    y, dx, dw, db, _, _ = _ln_dev(x, w, b, dy, True, mode="exact")
+    assert_close(y, yd.detach().numpy(), rtol=1e-5, atol=1e-6, what="y")
+    assert_close(dx, xd.grad.numpy(), rtol=1e-4, atol=1e-5, what="dx exact")
+    assert_close(dw, wd.grad.numpy(), rtol=1e-4, atol=1e-4, what="dw exact")
+    assert_close(db, bd.grad.numpy(), rtol=1e-4, atol=1e-4, what="db exact")
+
+
+def test_layer_norm_autograd_function():
+    from oxitorch_b200 import functional as F
+    x, w, b, dy = _ln_case(5, 32, 4096)
+    xg, wg, bg = _dev(x).requires_grad_(), _dev(w).requires_grad_(), _dev(b).requires_grad_()
+    F.layer_norm_gelu(xg, wg, bg).backward(_dev(dy))
+    got = _ln_dev(x, w, b, dy, True)
+    assert_bitexact(_host(xg.grad), got[1], "dx")
+    assert_bitexact(_host(wg.grad), got[2], "dw")
+    assert_bitexact(_host(bg.grad), got[3], "db")
+
+
+def test_workspace_too_small_is_a_value_error():
+    import torch
+    from oxitorch_b200 import _native as N
+    L = N.load()
+    x = torch.zeros(64, 256, device="cuda")
+    w = torch.ones(256, device="cuda")
+    rstd = torch.ones(64, device="cuda")
+    ws = torch.empty(16, dtype=torch.uint8, device="cuda")
+    st = L.oxc_rms_norm_bwd(x.data_ptr(), w.data_ptr(), rstd.data_ptr(), x.data_ptr(),
+                            x.data_ptr(), w.data_ptr(), 64, 256, 0, ws.data_ptr(), 16,
+                            torch.cuda.current_stream().cuda_stream)
+    with pytest.raises(ValueError, match="workspace"):
+        N.check(st)
