@@ -172,6 +172,21 @@ def t_cmp(name, a, b):
     return out
 
 
+# Test hook: {unary op name: k} shifts that op's results by k ulps, so a test
+# can measure how far a few-ulp difference between two libms (glibc on the
+# reference's host, CUDA's on the device) propagates to an output.
+PERTURB_ULPS = {}
+
+
+def shift_ulps(a, k):
+    """Moves every float32 in `a` by k units in the last place."""
+    out = np.array(a, dtype=np.float32, copy=True)
+    step = np.float32(np.inf if k > 0 else -np.inf)
+    for _ in range(abs(int(k))):
+        out = np.nextafter(out, step).astype(np.float32)
+    return out
+
+
 def t_unary(name, a):
     """Tensor::unary_op (lib.rs:306-325, 353-357)."""
     if name not in UNARY_OPS:
@@ -179,6 +194,8 @@ def t_unary(name, a):
     aa = f32(a)
     out = np.empty(aa.shape, np.float32)
     lib().oxr_unary(UNARY_OPS.index(name), _fp(aa), _fp(out), out.size)
+    if name in PERTURB_ULPS:
+        out = shift_ulps(out, PERTURB_ULPS[name])
     return out
 
 

@@ -7,7 +7,7 @@ their absolute tolerance is 1e-6 * sum_rows |term| (the term each test names).
 import numpy as np
 import pytest
 
-from parity import RTOL, ATOL, assert_close, assert_bitexact
+from parity import RTOL, RTOL_BIG, ATOL, assert_close, assert_bitexact, libm_budget
 
 pytestmark = pytest.mark.gpu
 
@@ -37,11 +37,19 @@ def _oracle_rms(oracle, x, w, dy, eps=1e-6):
 
 
 def _check_rms(x, w, dy, y, dx, dw, y_ref, dx_ref, dw_ref, rstd):
-    assert_close(y, y_ref, what="y")
-    assert_close(dx, dx_ref, what="dx")
+    n = x.shape[1]
+    # inv comes from a row reduction over n elements: rtol 1e-4 once n >= 32k
+    rtol, k = (RTOL, ATOL) if n < 32768 else (RTOL_BIG, 10 * ATOL)
+    assert_close(y, y_ref, rtol=rtol, what="y")
+    assert_close(dx, dx_ref, rtol=rtol, what="dx")
     t1 = x * rstd[:, None]
     scale = np.abs(dy.astype(np.float64) * t1).sum(0)
-    assert_close(dw, dw_ref, atol=ATOL * np.maximum(scale, 1.0), what="dw")
+    assert_close(dw, dw_ref, rtol=rtol, atol=k * np.maximum(scale, 1.0), what="dw")
+    # f64 yardstick: the kernel's dw is within 1e-6 * sum|terms| of the exact value
+    x64 = x.astype(np.float64)
+    inv64 = 1.0 / np.sqrt((x64 * x64).mean(1) + 1e-6)
+    dw64 = (dy.astype(np.float64) * x64 * inv64[:, None]).sum(0)
+    assert_close(dw, dw64, rtol=RTOL, atol=ATOL * np.maximum(scale, 1.0), what="dw vs f64")
 
 
 @pytest.mark.parametrize("name", ["rms_4x4096", "rms_7x1001", "rms_3x4"])
@@ -116,12 +124,20 @@ def _ln_case(seed, m, n):
 
 
 def _oracle_ln(oracle, x, w, b, dy, gelu):
-    xt, wt, bt = oracle.from_numpy(x, True), oracle.from_numpy(w, True), oracle.from_numpy(b, True)
-    y = oracle.layer_norm(xt, wt, bt, 1e-5)
-    if gelu:
-        y = oracle.gelu(y)
-    y.backward(dy)
-    return y.numpy(), xt.grad.numpy(), wt.grad.numpy(), bt.grad.numpy()
+    """(outputs, libm budgets): y, dx, dw, db of the composed reference path and
+    the per-element effect of a 4-ulp tanh difference on each."""
+    def run():
+        xt, wt, bt = (oracle.from_numpy(x, True), oracle.from_numpy(w, True),
+                      oracle.from_numpy(b, True))
+        y = oracle.layer_norm(xt, wt, bt, 1e-5)
+        if gelu:
+            y = oracle.gelu(y)
+        y.backward(dy)
+        return y.numpy(), xt.grad.numpy(), wt.grad.numpy(), bt.grad.numpy()
+    if not gelu:
+        out = run()
+        return out, [np.zeros(o.shape) for o in out]
+    return libm_budget(oracle, run)
 
 
 def _ln_dev(x, w, b, dy, gelu, mode="ref"):
@@ -135,22 +151,24 @@ def _ln_dev(x, w, b, dy, gelu, mode="ref"):
 
 def _check_ln(x, dy, got, ref, gelu):
     y, dx, dw, db, mean, rstd = got
-    y_ref, dx_ref, dw_ref, db_ref = ref
-    assert_close(y, y_ref, what="y")
-    assert_close(dx, dx_ref, what="dx")
+    (y_ref, dx_ref, dw_ref, db_ref), (by, bdx, bdw, bdb) = ref
+    assert_close(y, y_ref, atol=ATOL + by, what="y")
+    assert_close(dx, dx_ref, atol=ATOL + bdx, what="dx")
     # dweight terms: g * xhat; dbias terms: g, with |g| <= ~1.2 |dy| for GELU
     t1 = (x - mean[:, None]) * rstd[:, None]
     g_scale = np.abs(dy.astype(np.float64)) * (1.2 if gelu else 1.0)
-    assert_close(dw, dw_ref, atol=ATOL * np.maximum((g_scale * np.abs(t1)).sum(0), 1.0), what="dw")
-    assert_close(db, db_ref, atol=ATOL * np.maximum(g_scale.sum(0), 1.0), what="db")
+    assert_close(dw, dw_ref, atol=ATOL * np.maximum((g_scale * np.abs(t1)).sum(0), 1.0) + bdw,
+                 what="dw")
+    assert_close(db, db_ref, atol=ATOL * np.maximum(g_scale.sum(0), 1.0) + bdb, what="db")
 
 
 @pytest.mark.parametrize("name,gelu", [("lngelu_4x4096", True), ("lngelu_5x777", True),
                                        ("ln_6x512", False)])
-def test_layer_norm_golden(golden, name, gelu):
+def test_layer_norm_golden(oracle, golden, name, gelu):
     g = {k.split(".", 1)[1]: v for k, v in golden.items() if k.startswith(name + ".")}
     got = _ln_dev(g["x"], g["w"], g["b"], g["dy"], gelu)
-    _check_ln(g["x"], g["dy"], got, (g["y"], g["dx"], g["dw"], g["db"]), gelu)
+    _, budget = _oracle_ln(oracle, g["x"], g["w"], g["b"], g["dy"], gelu)
+    _check_ln(g["x"], g["dy"], got, ((g["y"], g["dx"], g["dw"], g["db"]), budget), gelu)
 
 
 @pytest.mark.parametrize("m,n,gelu", [(128, 4096, True), (40, 4095, True), (3, 32768, True),
@@ -162,10 +180,10 @@ def test_layer_norm_vs_oracle(oracle, m, n, gelu):
 
 
 def test_layer_norm_gelu_config2_rows(oracle):
-    """BASELINE config 2 shapes (cols 4096, eps 1e-5, seed 2) on 2048 of the
-    16384 rows (the composed oracle takes ~1 s per 1M elements)."""
+    """BASELINE config 2 shapes (cols 4096, eps 1e-5, seed 2) on 1024 of the
+    16384 rows (the composed oracle runs three times for the libm budget)."""
     rng = np.random.default_rng(2)
-    m, n = 2048, 4096
+    m, n = 1024, 4096
     x = rng.standard_normal((m, n), dtype=np.float32)
     w = rng.uniform(0.5, 1.5, n).astype(np.float32)
     b = (rng.standard_normal(n, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
