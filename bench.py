@@ -196,6 +196,8 @@ def run_reference(args, rank, world):
 # ---- GPU arm -----------------------------------------------------------------------------
 
 def run_ours(args, rank, world, local_rank):
+    global ROWS
+    ROWS = args.rows
     import torch
     import torch.distributed as dist
     from oxitorch_b200 import _native as N
@@ -283,7 +285,7 @@ def run_ours(args, rank, world, local_rank):
     peak, peak_kind = measured_peak()
 
     # ---- e2e: host buffers through the C ABI --------------------------------------------
-    e2e_steps = max(1, min(args.steps, 5))
+    e2e_steps = 0 if args.skip_e2e else max(1, min(args.steps, 5))
     hx = torch.empty(ROWS, COLS, pin_memory=True)
     hdy = torch.empty(ROWS, COLS, pin_memory=True)
     hx.copy_(x)
@@ -304,7 +306,8 @@ def run_ours(args, rank, world, local_rank):
         hdx.copy_(dx, non_blocking=True)
         hdwdb.copy_(dwdb, non_blocking=True)
 
-    e2e_step()
+    if e2e_steps:
+        e2e_step()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
@@ -320,7 +323,8 @@ def run_ours(args, rank, world, local_rank):
         t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    e2e_value = world * (fwd_bytes + bwd_bytes) / (e2e_ms / e2e_steps * 1e-3) / 1e9
+    e2e_value = (world * (fwd_bytes + bwd_bytes) / (e2e_ms / e2e_steps * 1e-3) / 1e9
+                 if e2e_steps else None)
     h2d = 2 * ROWS * COLS * F32
     d2h = 2 * ROWS * COLS * F32 + 2 * COLS * F32
 
@@ -365,7 +369,7 @@ def run_ours(args, rank, world, local_rank):
             "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
         },
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / e2e_steps,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / e2e_steps if e2e_steps else None,
                 "path": "pinned host -> oxc_layer_norm_fwd/bwd (C ABI) -> pinned host"},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
@@ -392,6 +396,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=100)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rows", type=int, default=ROWS,
+                    help="rows per GPU (default: config 2's 16384; smaller only for profiling)")
+    ap.add_argument("--skip-e2e", action="store_true", help="profiling runs: no host-buffer leg")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

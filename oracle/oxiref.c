@@ -188,6 +188,29 @@ OXR_API int oxr_reduce_strips(int kind, const float* data, const int64_t* s_off,
   return 0;
 }
 
+/* The same strips folded in f64 and rounded once to f32 (sum, mean, norm
+ * only): the reference's composition with exact-as-possible sums, used by the
+ * tests to measure how much of a result is the reference's own left-to-right
+ * f32 rounding. */
+OXR_API int oxr_reduce_strips_f64acc(int kind, const float* data, const int64_t* s_off,
+                                     int64_t strips, int64_t len, int64_t es, float* out) {
+  if (kind != R_SUM && kind != R_MEAN && kind != R_NORM)
+    return oxr_reduce_strips(kind, data, s_off, strips, len, es, out);
+  for (int64_t s = 0; s < strips; ++s) {
+    const float* d = data + s_off[s];
+    double acc = 0.0;
+    for (int64_t i = 0; i < len; ++i) {
+      double v = (double)d[i * es];
+      acc += kind == R_NORM ? (double)(float)(d[i * es] * d[i * es]) : v;
+    }
+    float r = (float)acc;
+    if (kind == R_MEAN) r = len ? r / (float)len : 0.0f;
+    if (kind == R_NORM) r = sqrtf(r);
+    out[s] = len ? r : 0.0f;
+  }
+  return 0;
+}
+
 /* Whole-buffer sequential f32 sum and sum of squares (sum_all, norm over a
  * flattened tensor: lib.rs:582-604), plus exact-as-possible f64 versions
  * used as the accuracy yardstick for large reductions. */

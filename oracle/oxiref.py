@@ -60,6 +60,7 @@ def lib():
         L.oxr_cmp.argtypes = [ctypes.c_int, F32P, F32P, F32P, ctypes.c_int64]
         L.oxr_reduce_strips.argtypes = [ctypes.c_int, F32P, I64P, ctypes.c_int64, ctypes.c_int64,
                                         ctypes.c_int64, F32P]
+        L.oxr_reduce_strips_f64acc.argtypes = L.oxr_reduce_strips.argtypes
         L.oxr_sum_all_f32.argtypes = [F32P, ctypes.c_int64]
         L.oxr_sum_all_f32.restype = ctypes.c_float
         L.oxr_sum_all_f64.argtypes = [F32P, ctypes.c_int64]
@@ -172,6 +173,11 @@ def t_cmp(name, a, b):
     return out
 
 
+# Test hook: when True, sum/mean/norm reductions fold in f64 and round once,
+# i.e. the same composition without the reference's left-to-right f32
+# rounding.  Tests compare the two runs to measure that rounding.
+PRECISE_SUMS = [False]
+
 # Test hook: {unary op name: k} shifts that op's results by k ulps, so a test
 # can measure how far a few-ulp difference between two libms (glibc on the
 # reference's host, CUDA's on the device) propagates to an output.
@@ -216,7 +222,8 @@ def t_reduce(kind, a, dim, keepdim):
             + np.arange(inner, dtype=np.int64)[None, :]).reshape(-1)
     offs = np.ascontiguousarray(offs)
     res = np.empty(outer * inner, np.float32)
-    rc = lib().oxr_reduce_strips(k, _fp(flat), _ip(offs), outer * inner, strip, inner, _fp(res))
+    fn = lib().oxr_reduce_strips_f64acc if PRECISE_SUMS[0] else lib().oxr_reduce_strips
+    rc = fn(k, _fp(flat), _ip(offs), outer * inner, strip, inner, _fp(res))
     if rc:
         raise InvalidArgument("invalid argument: cannot compute min/max/argmax/argmin over an empty reduction")
     shape = list(a.shape)

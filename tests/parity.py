@@ -10,6 +10,10 @@ Tolerances (from the project's parity contract):
   trees, so the absolute term is scaled by the sum's condition number:
   atol = 1e-6 * sum(|terms|) (each test states the terms); 1e-5 * sum(|terms|)
   when the terms themselves depend on a row reduction over >= 32k elements;
+* every output also carries the reference's own summation-order error:
+  the element-wise difference between the reference composition with its
+  left-to-right f32 folds and the same composition with f64-folded sums
+  (reference_budget); the kernels' fixed-order trees sit between the two;
 * outputs that pass through a transcendental (tanh, exp, log): the reference
   calls the host libm (glibc: tanhf is off by 1-2 ulp from correct rounding on
   ~5% of inputs) and the kernels call CUDA's (tanhf <= 2 ulp), so each element
@@ -34,6 +38,32 @@ def perturbed(oracle, name, k):
     finally:
         oracle.PERTURB_ULPS.clear()
         oracle.PERTURB_ULPS.update(old)
+
+
+@contextlib.contextmanager
+def precise_sums(oracle):
+    oracle.PRECISE_SUMS[0] = True
+    try:
+        yield
+    finally:
+        oracle.PRECISE_SUMS[0] = False
+
+
+def reference_budget(oracle, run, libm=("tanh",), ulps=LIBM_ULPS):
+    """(outputs, budgets) of the oracle run `run` (a callable returning a tuple
+    of arrays).  The budget of each element is what the reference's result is
+    only defined up to:
+      |run() - run() with f64-folded sums|   (its own left-to-right f32 sums)
+    + max over +-ulps of |run() - run() with `libm` results shifted| (libm ulps).
+    """
+    base = run()
+    with precise_sums(oracle):
+        exact = run()
+    budget = [np.abs(np.asarray(e, np.float64) - np.asarray(b, np.float64)) for b, e in zip(base, exact)]
+    if libm:
+        _, lb = libm_budget(oracle, run, libm, ulps)
+        budget = [a + b for a, b in zip(budget, lb)]
+    return base, budget
 
 
 def libm_budget(oracle, run, names=("tanh",), ulps=LIBM_ULPS):

@@ -7,7 +7,7 @@ their absolute tolerance is 1e-6 * sum_rows |term| (the term each test names).
 import numpy as np
 import pytest
 
-from parity import RTOL, RTOL_BIG, ATOL, assert_close, assert_bitexact, libm_budget
+from parity import RTOL, RTOL_BIG, ATOL, assert_close, assert_bitexact, reference_budget
 
 pytestmark = pytest.mark.gpu
 
@@ -30,21 +30,23 @@ def _rms_case(seed, m, n):
 
 
 def _oracle_rms(oracle, x, w, dy, eps=1e-6):
-    xt, wt = oracle.from_numpy(x, True), oracle.from_numpy(w, True)
-    y = oracle.rms_norm(xt, wt, eps)
-    y.backward(dy)
-    return y.numpy(), xt.grad.numpy(), wt.grad.numpy()
+    """(y, dx, dw) of the composed reference path and their budgets (the
+    reference's own summation-order error, tests/parity.py)."""
+    def run():
+        xt, wt = oracle.from_numpy(x, True), oracle.from_numpy(w, True)
+        y = oracle.rms_norm(xt, wt, eps)
+        y.backward(dy)
+        return y.numpy(), xt.grad.numpy(), wt.grad.numpy()
+    return reference_budget(oracle, run, libm=())
 
 
-def _check_rms(x, w, dy, y, dx, dw, y_ref, dx_ref, dw_ref, rstd):
-    n = x.shape[1]
-    # inv comes from a row reduction over n elements: rtol 1e-4 once n >= 32k
-    rtol, k = (RTOL, ATOL) if n < 32768 else (RTOL_BIG, 10 * ATOL)
-    assert_close(y, y_ref, rtol=rtol, what="y")
-    assert_close(dx, dx_ref, rtol=rtol, what="dx")
+def _check_rms(x, w, dy, y, dx, dw, ref, rstd):
+    (y_ref, dx_ref, dw_ref), (by, bdx, bdw) = ref
+    assert_close(y, y_ref, atol=ATOL + by, what="y")
+    assert_close(dx, dx_ref, atol=ATOL + bdx, what="dx")
     t1 = x * rstd[:, None]
     scale = np.abs(dy.astype(np.float64) * t1).sum(0)
-    assert_close(dw, dw_ref, rtol=rtol, atol=k * np.maximum(scale, 1.0), what="dw")
+    assert_close(dw, dw_ref, atol=ATOL * np.maximum(scale, 1.0) + bdw, what="dw")
     # f64 yardstick: the kernel's dw is within 1e-6 * sum|terms| of the exact value
     x64 = x.astype(np.float64)
     inv64 = 1.0 / np.sqrt((x64 * x64).mean(1) + 1e-6)
@@ -53,23 +55,24 @@ def _check_rms(x, w, dy, y, dx, dw, y_ref, dx_ref, dw_ref, rstd):
 
 
 @pytest.mark.parametrize("name", ["rms_4x4096", "rms_7x1001", "rms_3x4"])
-def test_rms_norm_golden(golden, name):
+def test_rms_norm_golden(oracle, golden, name):
     from oxitorch_b200 import functional as F
     g = {k.split(".", 1)[1]: v for k, v in golden.items() if k.startswith(name + ".")}
     y, rstd = F.rms_norm_fwd(_dev(g["x"]), _dev(g["w"]), 1e-6)
     dx, dw = F.rms_norm_bwd(_dev(g["x"]), _dev(g["w"]), rstd, _dev(g["dy"]))
-    _check_rms(g["x"], g["w"], g["dy"], _host(y), _host(dx), _host(dw), g["y"], g["dx"], g["dw"],
-               _host(rstd))
+    _, budget = _oracle_rms(oracle, g["x"], g["w"], g["dy"])
+    _check_rms(g["x"], g["w"], g["dy"], _host(y), _host(dx), _host(dw),
+               ((g["y"], g["dx"], g["dw"]), budget), _host(rstd))
 
 
 @pytest.mark.parametrize("m,n", [(256, 4096), (33, 4095), (5, 32768), (64, 11008), (1, 1), (2, 17)])
 def test_rms_norm_vs_oracle(oracle, m, n):
     from oxitorch_b200 import functional as F
     x, w, dy = _rms_case(m * 7 + n, m, n)
-    y_ref, dx_ref, dw_ref = _oracle_rms(oracle, x, w, dy)
+    ref = _oracle_rms(oracle, x, w, dy)
     y, rstd = F.rms_norm_fwd(_dev(x), _dev(w), 1e-6)
     dx, dw = F.rms_norm_bwd(_dev(x), _dev(w), rstd, _dev(dy))
-    _check_rms(x, w, dy, _host(y), _host(dx), _host(dw), y_ref, dx_ref, dw_ref, _host(rstd))
+    _check_rms(x, w, dy, _host(y), _host(dx), _host(dw), ref, _host(rstd))
 
 
 def test_rms_norm_config1_full_size(oracle):
@@ -79,10 +82,10 @@ def test_rms_norm_config1_full_size(oracle):
     x = rng.standard_normal((4096, 4096), dtype=np.float32)
     w = rng.uniform(0.5, 1.5, 4096).astype(np.float32)
     dy = rng.standard_normal((4096, 4096), dtype=np.float32)
-    y_ref, dx_ref, dw_ref = _oracle_rms(oracle, x, w, dy)
+    ref = _oracle_rms(oracle, x, w, dy)
     y, rstd = F.rms_norm_fwd(_dev(x), _dev(w), 1e-6)
     dx, dw = F.rms_norm_bwd(_dev(x), _dev(w), rstd, _dev(dy))
-    _check_rms(x, w, dy, _host(y), _host(dx), _host(dw), y_ref, dx_ref, dw_ref, _host(rstd))
+    _check_rms(x, w, dy, _host(y), _host(dx), _host(dw), ref, _host(rstd))
 
 
 def test_rms_norm_exact_mode_vs_torch_autograd():
@@ -124,8 +127,9 @@ def _ln_case(seed, m, n):
 
 
 def _oracle_ln(oracle, x, w, b, dy, gelu):
-    """(outputs, libm budgets): y, dx, dw, db of the composed reference path and
-    the per-element effect of a 4-ulp tanh difference on each."""
+    """(outputs, budgets): y, dx, dw, db of the composed reference path and, per
+    element, the reference's own summation-order error plus the effect of a
+    4-ulp tanh difference (see tests/parity.py)."""
     def run():
         xt, wt, bt = (oracle.from_numpy(x, True), oracle.from_numpy(w, True),
                       oracle.from_numpy(b, True))
@@ -134,10 +138,7 @@ def _oracle_ln(oracle, x, w, b, dy, gelu):
             y = oracle.gelu(y)
         y.backward(dy)
         return y.numpy(), xt.grad.numpy(), wt.grad.numpy(), bt.grad.numpy()
-    if not gelu:
-        out = run()
-        return out, [np.zeros(o.shape) for o in out]
-    return libm_budget(oracle, run)
+    return reference_budget(oracle, run, libm=("tanh",) if gelu else ())
 
 
 def _ln_dev(x, w, b, dy, gelu, mode="ref"):
