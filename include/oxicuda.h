@@ -117,6 +117,25 @@ oxc_status oxc_layer_norm_bwd(const float* x, const float* w, const float* b, co
                               int64_t rows, int64_t cols, int32_t act, int32_t grad_mode,
                               void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- LayerNorm backward without a caller workspace ------------------------
+ * No counterpart in the reference: an addition for callers that cannot call
+ * cudaMalloc (a host that owns all device memory through its own pool, or a
+ * latency-critical step that cannot afford cudaMalloc's implicit device
+ * synchronisation).  Same arguments and results as oxc_layer_norm_bwd minus
+ * the workspace: the scratch is a fixed device array of
+ * OXC_NOALLOC_SCRATCH_BYTES inside the library, which every GPU that loads
+ * the library holds until exit.  Sizes whose scratch
+ * (oxc_layer_norm_bwd_workspace_size) exceeds it are rejected with
+ * OXC_ERR_INVALID_ARGUMENT.  The first call on a device looks up the array's
+ * device address (make it before any stream capture); all calls on a device
+ * share the array, so calls that overlap on the GPU race and must be
+ * serialised by the caller.  Allocates nothing. */
+#define OXC_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+oxc_status oxc_layer_norm_bwd_noalloc(const float* x, const float* w, const float* b,
+                                      const float* mean, const float* rstd, const float* dy,
+                                      float* dx, float* dw, float* db, int64_t rows, int64_t cols,
+                                      int32_t act, int32_t grad_mode, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

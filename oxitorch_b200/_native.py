@@ -70,7 +70,11 @@ SIGNATURES = {
     "oxc_layer_norm_bwd_workspace_size": (_SZ, [_I64, _I64]),
     "oxc_layer_norm_bwd": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _I32,
                                   _P, _SZ, _P]),
+    "oxc_layer_norm_bwd_noalloc": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32,
+                                          _I32, _P]),
 }
+
+NOALLOC_SCRATCH_BYTES = 16 * 1024 * 1024
 
 _lib = None
 
