@@ -83,6 +83,13 @@ oxc_status oxc_stream_sync(void* stream, int64_t timeout_ms);
  * int32 halves, flag[3] = dim size), and clears it. */
 oxc_status oxc_check_error_flag(int32_t* flag_dev, void* stream, int64_t timeout_ms);
 
+/* Device-side error bits recorded by kernels since the last clear (synchronous;
+ * call after the stream has drained).  Bit 1: a bounded wait inside a
+ * bulk-copy pipeline ran out (the kernel stopped early, its outputs are not
+ * valid).  clear != 0 resets the bits. */
+#define OXC_KERR_PIPELINE_TIMEOUT 1u
+oxc_status oxc_kernel_error(uint32_t* bits, int32_t clear);
+
 /* ---- registry ids: the order of the reference registry tables ---------
  * binary: add,sub,mul,div,pow,min,max          (crates/oxi-tensor/src/ops.rs:55-91)
  * cmp:    eq,ne,lt,le,gt,ge                    (ops.rs:96-121)

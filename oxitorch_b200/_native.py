@@ -59,6 +59,7 @@ SIGNATURES = {
     "oxc_device_count": (_I32, []),
     "oxc_stream_sync": (_I32, [_P, _I64]),
     "oxc_check_error_flag": (_I32, [_P, _P, _I64]),
+    "oxc_kernel_error": (_I32, [ctypes.POINTER(ctypes.c_uint32), _I32]),
     "oxc_binary_op_id": (_I32, [ctypes.c_char_p]),
     "oxc_cmp_op_id": (_I32, [ctypes.c_char_p]),
     "oxc_unary_op_id": (_I32, [ctypes.c_char_p]),
@@ -114,6 +115,14 @@ def check(status: int, what: str = "") -> None:
     if status == ERR_NOT_IMPLEMENTED:
         raise NotImplementedError(msg)
     raise RuntimeError(msg)
+
+
+def kernel_error_bits(clear: bool = True) -> int:
+    """Device-side error bits recorded by kernels (synchronises nothing: call
+    after the stream drained)."""
+    v = ctypes.c_uint32(0)
+    check(load().oxc_kernel_error(ctypes.byref(v), int(clear)), "oxc_kernel_error")
+    return v.value
 
 
 def make_view(t) -> View:

@@ -5,6 +5,7 @@
 #include <cstdio>
 #include <cstring>
 #include <thread>
+#include <vector>
 
 #include "common.cuh"
 
@@ -32,6 +33,16 @@ oxc_status check_launch(const char* what) {
 }
 
 void clear_error() { g_last_error[0] = 0; }
+
+static std::vector<kernel_error_reader>& kernel_error_readers() {
+  static std::vector<kernel_error_reader> readers;
+  return readers;
+}
+
+int register_kernel_error_reader(kernel_error_reader fn) {
+  kernel_error_readers().push_back(fn);
+  return (int)kernel_error_readers().size();
+}
 
 int sm_count() {
   static int cached[64] = {0};
@@ -156,6 +167,18 @@ oxc_status oxc_check_error_flag(int32_t* flag_dev, void* stream, int64_t timeout
   if (e != cudaSuccess) return cuda_fail(e, "oxc_check_error_flag");
   return fail(OXC_ERR_OUT_OF_BOUNDS, "out of bounds: index %lld out of range for dim 0 of size %d",
               (long long)idx, host[3]);
+}
+
+oxc_status oxc_kernel_error(uint32_t* bits, int32_t clear) {
+  if (!bits) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: null bits pointer");
+  *bits = 0;
+  for (kernel_error_reader fn : kernel_error_readers()) {
+    unsigned int v = 0;
+    cudaError_t e = fn(&v, clear);
+    if (e != cudaSuccess) return cuda_fail(e, "oxc_kernel_error");
+    *bits |= v;
+  }
+  return OXC_OK;
 }
 
 int32_t oxc_binary_op_id(const char* name) { return lookup(kBinary, name); }

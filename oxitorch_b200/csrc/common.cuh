@@ -22,6 +22,12 @@ oxc_status cuda_fail(cudaError_t err, const char* what);
 oxc_status check_launch(const char* what);
 void clear_error();
 
+// ---- device-side error words -------------------------------------------------
+// Each translation unit with bounded-wait kernels owns a device error word and
+// registers a reader for it; oxc_kernel_error() ORs them all.
+typedef cudaError_t (*kernel_error_reader)(unsigned int* value, int clear);
+int register_kernel_error_reader(kernel_error_reader fn);
+
 // ---- device properties -----------------------------------------------------
 // Streaming-multiprocessor count of the current device (148 on B200), cached.
 int sm_count();

@@ -4,66 +4,54 @@
 //   mu = x.mean(-1, True); c = x - mu; var = (c*c).mean(-1, True)
 //   inv = (var + eps).apply("rsqrt")             -- detached (bindings lib.rs:682-697)
 //   yln = c * inv * weight + bias
-//   gelu: x32 = y*y; inner = (y + y*x32*0.044715) * C; out = (y*0.5) * (tanh(inner) + 1)
-//   with C = float(sqrt(2/pi)) computed in f64 and rounded to f32 at the boundary.
-// Every elementwise step below is the same f32 operation in the same order as
-// that composition; only the two row sums use a fixed-order tree.
+//   gelu: out = (y*0.5) * (tanh((y + y*y*y*0.044715) * C) + 1),  C = float(sqrt(2/pi))
 //
-// VJP (OXC_GRAD_REF, the reference graph):
-//   g    = dL/d(yln): the composed GELU VJP; its five contributions are added
-//          in the order the reference's backward visits them (graph.rs:324-438):
-//          (a-path, u, p, x32 first input, x32 second input)
+// VJP (OXC_GRAD_REF, the reference graph, autograd/ops.rs):
+//   g    = dL/d(yln) = dy * gelu'(yln)   (the reference accumulates the same
+//          derivative from five graph contributions; here it is one FMA chain)
 //   dw  += g * (c*inv)     db += g            (unbroadcast sums, graph.rs:274-313)
 //   gc   = (g*w) * inv
-//   dx   = gc + (-(sum_row gc)) * (1/cols)    (sub and mean VJPs, autograd/ops.rs:49-56, 340-349)
+//   dx   = gc - (sum_row gc) / cols            (sub and mean VJPs, ops.rs:49-56, 340-349)
 // OXC_GRAD_EXACT: dx = inv * (gw - mean(gw) - xhat*mean(gw*xhat)), gw = g*w.
+//
+// Two implementations of each direction, same arithmetic:
+//   *_pipe_kernel: rows with cols % 4 == 0 and 16-byte aligned tensors.  One
+//     persistent CTA per SM; a producer warp streams whole rows into a shared-
+//     memory ring with bulk copies (pipeline.cuh) while 16 consumer warps
+//     compute, so HBM stays busy during the arithmetic.
+//   *_kernel: any width up to 32768, register-resident rows, plain loads.
 #include <math.h>
 
+#include <algorithm>
+
+#include "pipeline.cuh"
 #include "rowvec.cuh"
 
 namespace oxc {
 
 struct GeluConst {
-  float k;  // 0.044715 as f32
-  float c;  // sqrt(2/pi) rounded to f32
+  float k;   // 0.044715 as f32
+  float k3;  // 3 * k
+  float c;   // sqrt(2/pi) rounded to f32
 };
 
 __device__ __forceinline__ float gelu_fwd(float y, const GeluConst& gc) {
-  const float x32 = __fmul_rn(y, y);
-  const float p = __fmul_rn(y, x32);
-  const float q = __fmul_rn(p, gc.k);
-  const float u = __fadd_rn(y, q);
-  const float inner = __fmul_rn(u, gc.c);
-  const float th = tanhf(inner);
-  const float a = __fmul_rn(y, 0.5f);
-  const float bb = __fadd_rn(th, 1.0f);
-  return __fmul_rn(a, bb);
+  const float y2 = y * y;
+  const float u = fmaf(gc.k * y2, y, y);  // y + k*y^3
+  const float th = tanhf(u * gc.c);
+  const float h = 0.5f * y;
+  return fmaf(h, th, h);  // 0.5*y*(1 + th)
 }
 
-// d out / d y times g, as the reference's graph computes it.
-__device__ __forceinline__ float gelu_vjp(float y, float g, const GeluConst& gc) {
-  const float x32 = __fmul_rn(y, y);
-  const float p = __fmul_rn(y, x32);
-  const float q = __fmul_rn(p, gc.k);
-  const float u = __fadd_rn(y, q);
-  const float inner = __fmul_rn(u, gc.c);
-  const float th = tanhf(inner);
-  const float a = __fmul_rn(y, 0.5f);
-  const float bb = __fadd_rn(th, 1.0f);
-  const float g_a = __fmul_rn(g, bb);
-  const float g_bb = __fmul_rn(g, a);
-  const float d = __fsub_rn(1.0f, __fmul_rn(th, th));
-  const float g_inner = __fmul_rn(g_bb, d);
-  const float g_u = __fmul_rn(g_inner, gc.c);
-  const float g_p = __fmul_rn(g_u, gc.k);
-  const float g_x32 = __fmul_rn(g_p, y);
-  float r = __fmul_rn(g_a, 0.5f);
-  r = __fadd_rn(r, g_u);
-  r = __fadd_rn(r, __fmul_rn(g_p, x32));
-  const float t = __fmul_rn(g_x32, y);
-  r = __fadd_rn(r, t);
-  r = __fadd_rn(r, t);
-  return r;
+// g * d gelu / d y at y.
+__device__ __forceinline__ float gelu_grad(float y, float g, const GeluConst& gc) {
+  const float y2 = y * y;
+  const float u = fmaf(gc.k * y2, y, y);
+  const float th = tanhf(u * gc.c);
+  const float sech2 = fmaf(-th, th, 1.0f);            // 1 - th^2
+  const float dinner = gc.c * fmaf(gc.k3, y2, 1.0f);  // d(inner)/dy
+  const float gp = fmaf(0.5f * y * sech2, dinner, fmaf(0.5f, th, 0.5f));
+  return g * gp;
 }
 
 template <int VW, int VPT, int MAXT, int ACT>
@@ -115,7 +103,7 @@ __global__ void __launch_bounds__(MAXT) ln_fwd_kernel(
         load_vec<VW>(bv, b + e, false);
 #pragma unroll
         for (int k = 0; k < VW; ++k) {
-          const float yl = __fadd_rn(__fmul_rn(__fmul_rn(v[i][k], inv), wv[k]), bv[k]);
+          const float yl = fmaf(v[i][k] * inv, wv[k], bv[k]);
           o[k] = ACT == OXC_ACT_GELU_TANH ? gelu_fwd(yl, gc) : yl;
         }
         store_vec<VW>(yr + e, o);
@@ -177,12 +165,9 @@ __global__ void __launch_bounds__(MAXT) ln_bwd_kernel(
       const int e = (i * blockDim.x + threadIdx.x) * VW;
 #pragma unroll
       for (int k = 0; k < VW; ++k) {
-        const float t1 = __fmul_rn(__fsub_rn(xv[i][k], mu), inv);  // c*inv
+        const float t1 = (xv[i][k] - mu) * inv;  // c*inv
         float g = gv[i][k];
-        if constexpr (ACT == OXC_ACT_GELU_TANH) {
-          const float yl = __fadd_rn(__fmul_rn(t1, wv[i][k]), bv[i][k]);
-          g = gelu_vjp(yl, g, gc);
-        }
+        if constexpr (ACT == OXC_ACT_GELU_TANH) g = gelu_grad(fmaf(t1, wv[i][k], bv[i][k]), g, gc);
         if (e < cols) {
           adw[i][k] = __fadd_rn(adw[i][k], __fmul_rn(g, t1));
           adb[i][k] = __fadd_rn(adb[i][k], g);
@@ -236,6 +221,295 @@ __global__ void __launch_bounds__(MAXT) ln_bwd_kernel(
   }
 }
 
+
+// ---- bulk-copy pipelined kernels (cols % 4 == 0, aligned) -------------------
+//
+// NG consumer groups of NWG warps each + 1 producer warp.  Group g processes
+// the CTA's rows i = g, g + NG, ... so NG rows are in their arithmetic at the
+// same time (each group's reductions use its own named barrier), while the
+// producer keeps the next rows streaming in.  weight/bias live in shared
+// memory (read once per CTA), leaving registers for the row slices.
+
+// Loads w (and b) into shared memory with every thread of the CTA.
+__device__ __forceinline__ void stage_params(float* ws, const float* w, float* bs, const float* b,
+                                             int cols) {
+  const int nvec = cols >> 2;
+  for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+    reinterpret_cast<float4*>(ws)[v] = ld_keep(reinterpret_cast<const float4*>(w) + v);
+    if (bs) reinterpret_cast<float4*>(bs)[v] = ld_keep(reinterpret_cast<const float4*>(b) + v);
+  }
+}
+
+template <int NG, int NWG, int VPT, int ACT>
+__global__ void __launch_bounds__((NG * NWG + 1) * 32, 1) ln_fwd_pipe_kernel(
+    const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
+    float* __restrict__ y, float* __restrict__ mean_out, float* __restrict__ rstd_out,
+    int64_t rows, int cols, int64_t chunk, int stages, float eps, GeluConst gc) {
+  extern __shared__ unsigned char smem[];
+  float* red;
+  const RowRing<1> ring = make_ring<1, NWG>(smem, stages, cols, &red);
+  float* ws = red + 64;
+  float* bs = ws + cols;
+  stage_params(ws, w, bs, b, cols);
+  __syncthreads();
+  const int64_t r0 = (int64_t)blockIdx.x * chunk;
+  const int64_t r1 = min(rows, r0 + chunk);
+  const int warp = threadIdx.x >> 5;
+  if (warp == NG * NWG) {
+    if ((threadIdx.x & 31) == 0 && r0 < r1) {
+      const float* src[1] = {x};
+      produce_rows<1>(ring, src, r0, r1);
+    }
+    return;
+  }
+  constexpr int T = NWG * 32;
+  const int g = warp / NWG, gt = threadIdx.x - g * T, bar = 1 + g;
+  float* gred = red + g * (NWG + 1);
+  const int nvec = cols >> 2;
+  const float4* w4 = reinterpret_cast<const float4*>(ws);
+  const float4* b4 = reinterpret_cast<const float4*>(bs);
+  for (int64_t i = g; i < r1 - r0; i += NG) {
+    const int64_t row = r0 + i;
+    const bool ok = consumer_acquire<1>(ring, i);
+    const float4* src = reinterpret_cast<const float4*>(ring.row((int)(i % ring.stages), 0));
+    float4 v[VPT];
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int slot = k * T + gt;
+      v[k] = (ok && slot < nvec) ? src[slot] : make_float4(0, 0, 0, 0);
+    }
+    consumer_release<1>(ring, i);
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+    s = group_sum<NWG>(s, gred, bar);
+    const float mu = __fdiv_rn(s, (float)cols);
+    float ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      v[k].x -= mu; v[k].y -= mu; v[k].z -= mu; v[k].w -= mu;
+      const float q = (v[k].x * v[k].x + v[k].y * v[k].y) + (v[k].z * v[k].z + v[k].w * v[k].w);
+      if (k * T + gt < nvec) ss += q;
+    }
+    ss = group_sum<NWG>(ss, gred, bar);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(ss, (float)cols) + eps));
+    float4* yr = reinterpret_cast<float4*>(y + row * (int64_t)cols);
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int slot = k * T + gt;
+      if (ok && slot < nvec) {
+        const float4 wv = w4[slot], bv = b4[slot];
+        float4 o;
+        o.x = fmaf(v[k].x * inv, wv.x, bv.x);
+        o.y = fmaf(v[k].y * inv, wv.y, bv.y);
+        o.z = fmaf(v[k].z * inv, wv.z, bv.z);
+        o.w = fmaf(v[k].w * inv, wv.w, bv.w);
+        if constexpr (ACT == OXC_ACT_GELU_TANH) {
+          o.x = gelu_fwd(o.x, gc); o.y = gelu_fwd(o.y, gc);
+          o.z = gelu_fwd(o.z, gc); o.w = gelu_fwd(o.w, gc);
+        }
+        st_stream(yr + slot, o);
+      }
+    }
+    if (gt == 0 && ok) {
+      mean_out[row] = mu;
+      rstd_out[row] = inv;
+    }
+  }
+}
+
+template <int NG, int NWG, int VPT, int ACT, int MODE>
+__global__ void __launch_bounds__((NG * NWG + 1) * 32, 1) ln_bwd_pipe_kernel(
+    const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
+    const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
+    const float* __restrict__ dy, float* __restrict__ dx, float* __restrict__ parts,
+    int64_t rows, int cols, int64_t chunk, int stages, GeluConst gc) {
+  extern __shared__ unsigned char smem[];
+  float* red;
+  const RowRing<2> ring = make_ring<2, NWG>(smem, stages, cols, &red);
+  float* ws = red + 64;
+  float* bs = ws + cols;
+  stage_params(ws, w, bs, b, cols);
+  __syncthreads();
+  const int64_t r0 = (int64_t)blockIdx.x * chunk;
+  const int64_t r1 = min(rows, r0 + chunk);
+  const int warp = threadIdx.x >> 5;
+  if (warp == NG * NWG) {
+    if ((threadIdx.x & 31) == 0 && r0 < r1) {
+      const float* src[2] = {x, dy};
+      produce_rows<2>(ring, src, r0, r1);
+    }
+    return;
+  }
+  constexpr int T = NWG * 32;
+  const int g = warp / NWG, gt = threadIdx.x - g * T, bar = 1 + g;
+  float* gred = red + g * (NWG + 1);
+  const int nvec = cols >> 2;
+  const float4* w4 = reinterpret_cast<const float4*>(ws);
+  const float4* b4 = reinterpret_cast<const float4*>(bs);
+  float4 adw[VPT], adb[VPT];
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    adw[k] = make_float4(0, 0, 0, 0);
+    adb[k] = make_float4(0, 0, 0, 0);
+  }
+  const float inv_n = __fdiv_rn(1.0f, (float)cols);
+  // Row statistics are prefetched one group-iteration ahead so their global
+  // load latency is not on each row's critical path.
+  float mu_next = 0.0f, inv_next = 0.0f;
+  if (g < r1 - r0) {
+    mu_next = __ldg(mean_in + r0 + g);
+    inv_next = __ldg(rstd_in + r0 + g);
+  }
+  for (int64_t i = g; i < r1 - r0; i += NG) {
+    const int64_t row = r0 + i;
+    const float mu = mu_next, inv = inv_next;
+    if (i + NG < r1 - r0) {
+      mu_next = __ldg(mean_in + row + NG);
+      inv_next = __ldg(rstd_in + row + NG);
+    }
+    const bool ok = consumer_acquire<2>(ring, i);
+    const int stage = (int)(i % ring.stages);
+    const float4* xs = reinterpret_cast<const float4*>(ring.row(stage, 0));
+    const float4* gs = reinterpret_cast<const float4*>(ring.row(stage, 1));
+    float4 xv[VPT], gv[VPT];
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int slot = k * T + gt;
+      const bool valid = ok && slot < nvec;
+      xv[k] = valid ? xs[slot] : make_float4(0, 0, 0, 0);
+      gv[k] = valid ? gs[slot] : make_float4(0, 0, 0, 0);
+    }
+    consumer_release<2>(ring, i);
+    float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int slot = k * T + gt;
+      const float4 wv = slot < nvec ? w4[slot] : make_float4(0, 0, 0, 0);
+      const float4 bv = slot < nvec ? b4[slot] : make_float4(0, 0, 0, 0);
+      float* xe = reinterpret_cast<float*>(&xv[k]);
+      float* ge = reinterpret_cast<float*>(&gv[k]);
+      const float* we = reinterpret_cast<const float*>(&wv);
+      const float* be = reinterpret_cast<const float*>(&bv);
+      float* dwe = reinterpret_cast<float*>(&adw[k]);
+      float* dbe = reinterpret_cast<float*>(&adb[k]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float t1 = (xe[e] - mu) * inv;
+        float gg = ge[e];
+        if constexpr (ACT == OXC_ACT_GELU_TANH) gg = gelu_grad(fmaf(t1, we[e], be[e]), gg, gc);
+        dwe[e] = fmaf(gg, t1, dwe[e]);
+        dbe[e] += gg;
+        const float gw = gg * we[e];
+        if constexpr (MODE == OXC_GRAD_REF) {
+          ge[e] = gw * inv;
+          s1 += ge[e];
+        } else {
+          ge[e] = gw;
+          xe[e] = t1;
+          s1 += gw;
+          s2 = fmaf(gw, t1, s2);
+        }
+      }
+    }
+    s1 = group_sum<NWG>(s1, gred, bar);
+    if constexpr (MODE == OXC_GRAD_EXACT) s2 = group_sum<NWG>(s2, gred, bar);
+    float4* dxr = reinterpret_cast<float4*>(dx + row * (int64_t)cols);
+    const float shift = -s1 * inv_n;
+    const float m1 = s1 * inv_n, m2 = s2 * inv_n;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int slot = k * T + gt;
+      if (ok && slot < nvec) {
+        float4 o;
+        float* oe = reinterpret_cast<float*>(&o);
+        const float* xe = reinterpret_cast<const float*>(&xv[k]);
+        const float* ge = reinterpret_cast<const float*>(&gv[k]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if constexpr (MODE == OXC_GRAD_REF) oe[e] = ge[e] + shift;
+          else oe[e] = inv * ((ge[e] - m1) - xe[e] * m2);
+        }
+        st_stream(dxr + slot, o);
+      }
+    }
+  }
+  // Combine the groups' column partials in group order through shared memory
+  // (the ring is idle: every issued copy was waited for by its consumer).
+  all_consumers_sync<NG * NWG * 32>();
+  float4* comb = reinterpret_cast<float4*>(ring.buf);  // (NG-1) x 2 x cols floats
+  if (g > 0) {
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int slot = k * T + gt;
+      if (slot < nvec) {
+        comb[(size_t)(2 * (g - 1)) * nvec + slot] = adw[k];
+        comb[(size_t)(2 * (g - 1) + 1) * nvec + slot] = adb[k];
+      }
+    }
+  }
+  all_consumers_sync<NG * NWG * 32>();
+  if (g == 0) {
+    float4* pw = reinterpret_cast<float4*>(parts + (int64_t)blockIdx.x * cols);
+    float4* pb = reinterpret_cast<float4*>(parts + ((int64_t)gridDim.x + blockIdx.x) * cols);
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int slot = k * T + gt;
+      if (slot < nvec) {
+        float4 a = adw[k], c = adb[k];
+        for (int h = 1; h < NG; ++h) {
+          const float4 p = comb[(size_t)(2 * (h - 1)) * nvec + slot];
+          const float4 q = comb[(size_t)(2 * (h - 1) + 1) * nvec + slot];
+          a.x += p.x; a.y += p.y; a.z += p.z; a.w += p.w;
+          c.x += q.x; c.y += q.y; c.z += q.z; c.w += q.w;
+        }
+        pw[slot] = a;
+        pb[slot] = c;
+      }
+    }
+  }
+}
+
+// Pipeline geometry: NG groups x NWG warps.
+constexpr int kFwdNG = 4, kFwdNWG = 4;   // 4 rows in flight, 128 threads per row
+constexpr int kBwdNG = 2, kBwdNWG = 8;   // 2 rows in flight, 256 threads per row
+
+// Max dynamic shared memory per block (opt-in) of the current device.
+static size_t max_smem_optin() {
+  static size_t cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 48 * 1024;
+  if (!cached[dev]) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+      v = 48 * 1024;
+    cached[dev] = (size_t)v;
+  }
+  return cached[dev];
+}
+
+// Stages of the ring for `nin` inputs of `cols` floats plus the staged
+// weight/bias (0 = pipeline unusable: fewer than `min_stages` fit).
+static int pipe_stages(int nin, int64_t cols, int max_stages, int min_stages) {
+  const size_t avail = max_smem_optin();
+  int st = max_stages;
+  while (st >= min_stages && ring_smem_bytes(nin, cols, st, 2 * cols) > avail) --st;
+  return st >= min_stages ? st : 0;
+}
+
+// VPT (float4 slots per consumer thread, threads = nwg * 32), or 0.
+static int pipe_vpt(int64_t cols, int nwg, int max_vpt) {
+  const int64_t nvec = cols / 4, T = (int64_t)nwg * 32;
+  for (int v : {1, 2, 4, 8})
+    if (v <= max_vpt && nvec <= v * T) return v;
+  return 0;
+}
+
+template <typename K>
+static void allow_smem(K kernel, size_t bytes) {
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
 static int64_t ln_bwd_ctas(int64_t rows) {
   int64_t g = 2 * (int64_t)sm_count();
   const int64_t by_rows = (rows + 7) / 8;
@@ -246,6 +520,7 @@ static int64_t ln_bwd_ctas(int64_t rows) {
 static GeluConst gelu_const() {
   GeluConst gc;
   gc.k = (float)0.044715;
+  gc.k3 = 3.0f * gc.k;
   gc.c = (float)sqrt(2.0 / M_PI);
   return gc;
 }
@@ -273,9 +548,38 @@ oxc_status oxc_layer_norm_fwd(const float* x, const float* w, const float* b, fl
     return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: layer_norm: null pointer");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool v4 = cols % 4 == 0 && aligned16(x) && aligned16(w) && aligned16(b) && aligned16(y);
+  const GeluConst gc = gelu_const();
+  const int stages = v4 ? pipe_stages(1, cols, 8, kFwdNG + 1) : 0;
+  const int vpt = v4 ? pipe_vpt(cols, kFwdNWG, 8) : 0;
+  if (stages && vpt) {
+    const int64_t ctas = std::min<int64_t>(rows, sm_count());
+    const int64_t chunk = (rows + ctas - 1) / ctas;
+    const size_t smem = ring_smem_bytes(1, cols, stages, 2 * cols);
+    const int block = (kFwdNG * kFwdNWG + 1) * 32;
+#define LAUNCH_P(VPT, ACT)                                                                  \
+  do {                                                                                      \
+    auto k = ln_fwd_pipe_kernel<kFwdNG, kFwdNWG, VPT, ACT>;                                 \
+    allow_smem(k, smem);                                                                    \
+    k<<<(unsigned)ctas, block, smem, s>>>(x, w, b, y, mean, rstd, rows, (int)cols, chunk,   \
+                                          stages, eps, gc);                                 \
+  } while (0)
+#define LAUNCH_A(VPT)                                                                       \
+  do {                                                                                      \
+    if (act == OXC_ACT_GELU_TANH) LAUNCH_P(VPT, OXC_ACT_GELU_TANH);                         \
+    else LAUNCH_P(VPT, OXC_ACT_NONE);                                                       \
+  } while (0)
+    switch (vpt) {
+      case 1: LAUNCH_A(1); break;
+      case 2: LAUNCH_A(2); break;
+      case 4: LAUNCH_A(4); break;
+      default: LAUNCH_A(8); break;
+    }
+#undef LAUNCH_A
+#undef LAUNCH_P
+    return check_launch("oxc_layer_norm_fwd");
+  }
   RowGeom g = row_geom(cols, v4);
   const unsigned grid = (unsigned)(rows < 0x7fffffff ? rows : 0x7fffffff);
-  const GeluConst gc = gelu_const();
 #define LAUNCH(VW, VPT, MAXT)                                                            \
   do {                                                                                   \
     if (act == OXC_ACT_GELU_TANH)                                                        \
@@ -324,11 +628,53 @@ oxc_status oxc_layer_norm_bwd(const float* x, const float* w, const float* b, co
     return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: layer_norm backward: null pointer");
   const bool v4 = cols % 4 == 0 && aligned16(x) && aligned16(w) && aligned16(b) &&
                   aligned16(dy) && aligned16(dx) && aligned16(workspace);
+  float* parts = static_cast<float*>(workspace);
+  const GeluConst gc = gelu_const();
+  const int stages = v4 ? pipe_stages(2, cols, 6, kBwdNG + 1) : 0;
+  const int vpt = v4 ? pipe_vpt(cols, kBwdNWG, 4) : 0;
+  if (stages && vpt) {
+    // At most ln_bwd_ctas(rows) CTAs, the partial slots the workspace holds.
+    const int64_t ctas = std::min<int64_t>(sm_count(), ln_bwd_ctas(rows));
+    if ((size_t)2 * ctas * cols * sizeof(float) > workspace_bytes)
+      return fail(OXC_ERR_OTHER, "internal: layer_norm backward partials exceed the workspace");
+    const int64_t chunk = (rows + ctas - 1) / ctas;
+    const size_t smem = ring_smem_bytes(2, cols, stages, 2 * cols);
+    const int block = (kBwdNG * kBwdNWG + 1) * 32;
+#define LAUNCH_P(VPT, ACT, MODE)                                                              \
+  do {                                                                                        \
+    auto k = ln_bwd_pipe_kernel<kBwdNG, kBwdNWG, VPT, ACT, MODE>;                             \
+    allow_smem(k, smem);                                                                      \
+    k<<<(unsigned)ctas, block, smem, s>>>(x, w, b, mean, rstd, dy, dx, parts, rows, (int)cols, \
+                                          chunk, stages, gc);                                 \
+  } while (0)
+#define LAUNCH_A(VPT)                                                                         \
+  do {                                                                                        \
+    if (act == OXC_ACT_GELU_TANH) {                                                           \
+      if (grad_mode == OXC_GRAD_REF) LAUNCH_P(VPT, OXC_ACT_GELU_TANH, OXC_GRAD_REF);          \
+      else LAUNCH_P(VPT, OXC_ACT_GELU_TANH, OXC_GRAD_EXACT);                                  \
+    } else {                                                                                  \
+      if (grad_mode == OXC_GRAD_REF) LAUNCH_P(VPT, OXC_ACT_NONE, OXC_GRAD_REF);               \
+      else LAUNCH_P(VPT, OXC_ACT_NONE, OXC_GRAD_EXACT);                                       \
+    }                                                                                         \
+  } while (0)
+    switch (vpt) {
+      case 1: LAUNCH_A(1); break;
+      case 2: LAUNCH_A(2); break;
+      default: LAUNCH_A(4); break;
+    }
+#undef LAUNCH_A
+#undef LAUNCH_P
+    oxc_status st = check_launch("oxc_layer_norm_bwd");
+    if (st) return st;
+    launch_colsum_partials(parts, (int)ctas, cols, dw, s);
+    launch_colsum_partials(parts + ctas * cols, (int)ctas, cols, db, s);
+    return check_launch("oxc_layer_norm_bwd (dw, db)");
+  }
   RowGeom g = row_geom(cols, v4, 512);
   const int64_t ctas = ln_bwd_ctas(rows);
   const int64_t chunk = (rows + ctas - 1) / ctas;
-  float* parts = static_cast<float*>(workspace);
-  const GeluConst gc = gelu_const();
+  if ((size_t)2 * ctas * cols * sizeof(float) > workspace_bytes)
+    return fail(OXC_ERR_OTHER, "internal: layer_norm backward partials exceed the workspace");
 #define LAUNCH_M(VW, VPT, MAXT, ACT, MODE)                                              \
   ln_bwd_kernel<VW, VPT, MAXT, ACT, MODE><<<(unsigned)ctas, g.block, 0, s>>>(           \
       x, w, b, mean, rstd, dy, dx, parts, rows, (int)cols, chunk, gc)
