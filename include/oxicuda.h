@@ -124,6 +124,34 @@ oxc_status oxc_layer_norm_bwd(const float* x, const float* w, const float* b, co
                               int64_t rows, int64_t cols, int32_t act, int32_t grad_mode,
                               void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- softmax / log_softmax: F.softmax, F.log_softmax over the last dim -----
+ * (python/oxitorch/nn/functional.py:211-222).  log != 0 selects log_softmax.
+ * x, y, dy, dx: [rows, cols] row-major.  The VJP takes the forward output y. */
+oxc_status oxc_softmax_fwd(const float* x, float* y, int64_t rows, int64_t cols, int32_t log,
+                           void* stream);
+oxc_status oxc_softmax_bwd(const float* y, const float* dy, float* dx, int64_t rows, int64_t cols,
+                           int32_t log, void* stream);
+
+/* ---- cross-entropy, mean reduction: F.cross_entropy --------------------------
+ * (functional.py:277-293).  logits [rows, cols]; targets int64 [rows] (negative
+ * values count from the end, like the reference's numpy one-hot indexing).
+ * Writes loss[0] = -(1/total_rows) * sum_rows log_softmax(logits)[r, t_r] and
+ * the per-row max, sum of exp(x - max) and -log p_target that the VJP reuses.
+ * total_rows = rows on one GPU; with row sharding it is the global row count
+ * (each shard's loss is its share of the global mean).  A target outside
+ * [-cols, cols) is recorded in err_flag (int32[4], may be NULL) and gives a NaN
+ * row; read it with oxc_check_error_flag. */
+oxc_status oxc_cross_entropy_fwd(const float* logits, const int64_t* targets, float* loss,
+                                 float* row_max, float* row_sum, float* row_nll, int64_t rows,
+                                 int64_t cols, int64_t total_rows, int32_t* err_flag,
+                                 void* stream);
+/* dlogits = exp(x - max) * (g/M) / sum - onehot * g/M, g = *grad_loss (device
+ * scalar; NULL = 1.0), M = total_rows. */
+oxc_status oxc_cross_entropy_bwd(const float* logits, const int64_t* targets,
+                                 const float* row_max, const float* row_sum,
+                                 const float* grad_loss, float* dlogits, int64_t rows,
+                                 int64_t cols, int64_t total_rows, void* stream);
+
 /* ---- LayerNorm backward without a caller workspace ------------------------
  * No counterpart in the reference: an addition for callers that cannot call
  * cudaMalloc (a host that owns all device memory through its own pool, or a

@@ -1,0 +1,418 @@
+// softmax.cu -- F.softmax / F.log_softmax forward and VJP, and F.cross_entropy
+// (mean reduction) forward and VJP.
+//
+// Reference (python/oxitorch/nn/functional.py):
+//   softmax      (211-215): m = x.max(-1, True); e = (x - m).exp(); y = e / e.sum(-1, True)
+//   log_softmax  (218-222): z = x - m; y = z - z.exp().sum(-1, True).log()
+//   cross_entropy(277-293): ls = log_softmax(x); picked = (onehot * ls).sum(-1);
+//                           loss = -(picked.mean())
+// VJPs are the ones the reference graph builds (crates/oxi-autograd/src/ops.rs):
+//   softmax:      dx = y * (g - sum_row(g*y))
+//   log_softmax:  dx = g - exp(y) * sum_row(g)
+//   cross_entropy: d[r,c] = exp(x - m) * ((g/M) * (1/s)) - (c == t_r ? g/M : 0)
+//     (log VJP 1/s, exp VJP, sub VJP, the one-hot pick; the mean over M rows)
+// The max node's VJP additionally scatters -sum_row(dz) to the argmax column;
+// that sum is zero in exact arithmetic and only the row's rounding noise in
+// the reference, so the kernels leave it out.
+//
+// Kernels, all HBM-bound (no contraction):
+//   softmax_fwd/bwd: one CTA per row, two passes; pass 1 reads the row with
+//     L2-allocating 128-bit loads (online max + rescaled sum, or plain sums),
+//     pass 2 re-reads it from L2 and writes -- DRAM sees one read + one write.
+//   ce_fwd: one CTA per row, one online pass; writes per-row (max, sum of
+//     exp, -log p_target) and never materialises a full-size tensor.
+//   ce_loss: deterministic f64 tree over the per-row values.
+//   ce_bwd: grid-stride elementwise over [rows, cols] (128-bit when cols % 4
+//     == 0), per-row (max, 1/s, target) read through L1.
+#include <math.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace oxc {
+
+struct MaxSum {
+  float m;
+  float s;
+};
+
+// Online (max, sum exp(x - max)) update with one element.
+__device__ __forceinline__ void ms_push(MaxSum& a, float x) {
+  if (x > a.m) {
+    a.s = a.s * expf(a.m - x) + 1.0f;
+    a.m = x;
+  } else {
+    a.s += expf(x - a.m);
+  }
+}
+
+__device__ __forceinline__ MaxSum ms_merge(MaxSum a, MaxSum b) {
+  const float m = fmaxf(a.m, b.m);
+  if (m == -INFINITY) return {m, a.s + b.s};
+  const float sa = a.m == m ? a.s : a.s * expf(a.m - m);
+  const float sb = b.m == m ? b.s : b.s * expf(b.m - m);
+  return {m, sa + sb};
+}
+
+// Block-wide merge; every thread gets the result.  scratch: 2 x 33 floats.
+__device__ __forceinline__ MaxSum block_maxsum(MaxSum v, float* scratch) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarps = (blockDim.x + 31) >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    MaxSum w{__shfl_xor_sync(0xffffffffu, v.m, o), __shfl_xor_sync(0xffffffffu, v.s, o)};
+    v = ms_merge(v, w);
+  }
+  __syncthreads();
+  if (lane == 0) {
+    scratch[warp] = v.m;
+    scratch[33 + warp] = v.s;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    MaxSum t = lane < nwarps ? MaxSum{scratch[lane], scratch[33 + lane]} : MaxSum{-INFINITY, 0.0f};
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      MaxSum w{__shfl_xor_sync(0xffffffffu, t.m, o), __shfl_xor_sync(0xffffffffu, t.s, o)};
+      t = ms_merge(t, w);
+    }
+    if (lane == 0) {
+      scratch[32] = t.m;
+      scratch[65] = t.s;
+    }
+  }
+  __syncthreads();
+  return {scratch[32], scratch[65]};
+}
+
+// Row statistics (max, sum exp(x - max)) with 128-bit (VW = 4) or scalar
+// loads; `keep` loads allocate in L2 so a second pass hits it.
+template <int VW>
+__device__ __forceinline__ MaxSum row_maxsum(const float* xr, int cols, float* scratch) {
+  MaxSum a{-INFINITY, 0.0f};
+  if constexpr (VW == 4) {
+    const float4* x4 = reinterpret_cast<const float4*>(xr);
+    const int nvec = cols >> 2;
+    int v = threadIdx.x;
+    for (; v + 3 * (int)blockDim.x < nvec; v += 4 * blockDim.x) {
+      float4 q[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) q[u] = ld_keep(x4 + v + u * blockDim.x);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        ms_push(a, q[u].x); ms_push(a, q[u].y); ms_push(a, q[u].z); ms_push(a, q[u].w);
+      }
+    }
+    for (; v < nvec; v += blockDim.x) {
+      const float4 q = ld_keep(x4 + v);
+      ms_push(a, q.x); ms_push(a, q.y); ms_push(a, q.z); ms_push(a, q.w);
+    }
+  } else {
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) ms_push(a, ld_keep(xr + c));
+  }
+  return block_maxsum(a, scratch);
+}
+
+template <int VW, bool LOG>
+__global__ void __launch_bounds__(512) softmax_fwd_kernel(const float* __restrict__ x,
+                                                          float* __restrict__ y, int64_t rows,
+                                                          int cols) {
+  __shared__ float scratch[66];
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float* xr = x + row * (int64_t)cols;
+    float* yr = y + row * (int64_t)cols;
+    const MaxSum st = row_maxsum<VW>(xr, cols, scratch);
+    const float logs = LOG ? logf(st.s) : 0.0f;
+    if constexpr (VW == 4) {
+      const float4* x4 = reinterpret_cast<const float4*>(xr);
+      float4* y4 = reinterpret_cast<float4*>(yr);
+      for (int v = threadIdx.x; v < (cols >> 2); v += blockDim.x) {
+        const float4 q = ld_stream(x4 + v);
+        float4 o;
+        if constexpr (LOG) {
+          o.x = (q.x - st.m) - logs; o.y = (q.y - st.m) - logs;
+          o.z = (q.z - st.m) - logs; o.w = (q.w - st.m) - logs;
+        } else {
+          o.x = __fdiv_rn(expf(q.x - st.m), st.s); o.y = __fdiv_rn(expf(q.y - st.m), st.s);
+          o.z = __fdiv_rn(expf(q.z - st.m), st.s); o.w = __fdiv_rn(expf(q.w - st.m), st.s);
+        }
+        st_stream(y4 + v, o);
+      }
+    } else {
+      for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+        const float q = ld_stream(xr + c);
+        st_stream(yr + c, LOG ? (q - st.m) - logs : __fdiv_rn(expf(q - st.m), st.s));
+      }
+    }
+  }
+}
+
+template <int VW, bool LOG>
+__global__ void __launch_bounds__(512) softmax_bwd_kernel(const float* __restrict__ y,
+                                                          const float* __restrict__ dy,
+                                                          float* __restrict__ dx, int64_t rows,
+                                                          int cols) {
+  __shared__ float scratch[33];
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float* yr = y + row * (int64_t)cols;
+    const float* gr = dy + row * (int64_t)cols;
+    float* dr = dx + row * (int64_t)cols;
+    float acc = 0.0f;
+    if constexpr (VW == 4) {
+      const float4* y4 = reinterpret_cast<const float4*>(yr);
+      const float4* g4 = reinterpret_cast<const float4*>(gr);
+      for (int v = threadIdx.x; v < (cols >> 2); v += blockDim.x) {
+        const float4 g = ld_keep(g4 + v);
+        if constexpr (LOG) {
+          acc += (g.x + g.y) + (g.z + g.w);
+        } else {
+          const float4 q = ld_keep(y4 + v);
+          acc += (g.x * q.x + g.y * q.y) + (g.z * q.z + g.w * q.w);
+        }
+      }
+    } else {
+      for (int c = threadIdx.x; c < cols; c += blockDim.x)
+        acc += LOG ? ld_keep(gr + c) : ld_keep(gr + c) * ld_keep(yr + c);
+    }
+    const float sum = block_sum(acc, scratch);
+    if constexpr (VW == 4) {
+      const float4* y4 = reinterpret_cast<const float4*>(yr);
+      const float4* g4 = reinterpret_cast<const float4*>(gr);
+      float4* d4 = reinterpret_cast<float4*>(dr);
+      for (int v = threadIdx.x; v < (cols >> 2); v += blockDim.x) {
+        const float4 g = ld_stream(g4 + v), q = ld_stream(y4 + v);
+        float4 o;
+        if constexpr (LOG) {
+          o.x = g.x - expf(q.x) * sum; o.y = g.y - expf(q.y) * sum;
+          o.z = g.z - expf(q.z) * sum; o.w = g.w - expf(q.w) * sum;
+        } else {
+          o.x = q.x * (g.x - sum); o.y = q.y * (g.y - sum);
+          o.z = q.z * (g.z - sum); o.w = q.w * (g.w - sum);
+        }
+        st_stream(d4 + v, o);
+      }
+    } else {
+      for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+        const float g = ld_stream(gr + c), q = ld_stream(yr + c);
+        st_stream(dr + c, LOG ? g - expf(q) * sum : q * (g - sum));
+      }
+    }
+  }
+}
+
+// Records the first bad target: flag[0] = 1, flag[1..2] = value, flag[3] = cols.
+__device__ __forceinline__ void record_bad_index(int32_t* flag, int64_t value, int64_t size) {
+  if (flag && atomicCAS(flag, 0, 1) == 0) {
+    flag[1] = (int32_t)(uint32_t)((uint64_t)value & 0xffffffffu);
+    flag[2] = (int32_t)(uint32_t)((uint64_t)value >> 32);
+    flag[3] = (int32_t)size;
+  }
+}
+
+// Resolves a target like numpy fancy indexing does for onehot[i, t]
+// (negative values count from the end); -1 if out of range.
+__device__ __forceinline__ int64_t resolve_target(int64_t t, int64_t cols) {
+  const int64_t r = t < 0 ? t + cols : t;
+  return (r >= 0 && r < cols) ? r : -1;
+}
+
+template <int VW>
+__global__ void __launch_bounds__(512) ce_fwd_kernel(const float* __restrict__ x,
+                                                     const int64_t* __restrict__ targets,
+                                                     float* __restrict__ row_max,
+                                                     float* __restrict__ row_sum,
+                                                     float* __restrict__ row_nll, int64_t rows,
+                                                     int cols, int32_t* err) {
+  __shared__ float scratch[66];
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float* xr = x + row * (int64_t)cols;
+    const MaxSum st = row_maxsum<VW>(xr, cols, scratch);
+    if (threadIdx.x == 0) {
+      const int64_t t = resolve_target(targets[row], cols);
+      float nll = NAN;
+      if (t < 0) {
+        record_bad_index(err, targets[row], cols);
+      } else {
+        // ls_t = (x_t - m) - log(s); the picked value is -ls_t
+        nll = -((xr[t] - st.m) - logf(st.s));
+      }
+      row_max[row] = st.m;
+      row_sum[row] = st.s;
+      row_nll[row] = nll;
+    }
+  }
+}
+
+// loss = -(sum_rows ls) / total_rows, folded in f64 by one CTA in a fixed order.
+__global__ void __launch_bounds__(1024) ce_loss_kernel(const float* __restrict__ row_nll,
+                                                       int64_t rows, int64_t total_rows,
+                                                       float* __restrict__ loss) {
+  __shared__ double scratch[33];
+  double acc = 0.0;
+  for (int64_t r = threadIdx.x; r < rows; r += blockDim.x) acc += (double)row_nll[r];
+  const double sum = block_sum(acc, scratch);
+  if (threadIdx.x == 0) {
+    // reference: mean = sum / M in f32, then neg (of the mean of ls = -nll)
+    const float mean_ls = __fdiv_rn((float)(-sum), (float)total_rows);
+    loss[0] = -mean_ls;
+  }
+}
+
+template <int VW>
+__global__ void __launch_bounds__(256) ce_bwd_kernel(const float* __restrict__ x,
+                                                     const int64_t* __restrict__ targets,
+                                                     const float* __restrict__ row_max,
+                                                     const float* __restrict__ row_sum,
+                                                     const float* __restrict__ grad_loss,
+                                                     float* __restrict__ dx, int64_t rows,
+                                                     int cols, float inv_total) {
+  const float g = grad_loss ? __ldg(grad_loss) : 1.0f;
+  const float gm = g * inv_total;  // mean VJP: g * (1/M)
+  const int64_t nvec = (int64_t)rows * (cols / VW);
+  const int vpr = cols / VW;  // vectors per row
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec;
+       v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = v / vpr;
+    const int c0 = (int)(v - row * vpr) * VW;
+    const float m = __ldg(row_max + row);
+    const float scale = gm * __fdiv_rn(1.0f, __ldg(row_sum + row));  // (g/M) * (1/s)
+    const int64_t t = resolve_target(__ldg(targets + row), cols);
+    if constexpr (VW == 4) {
+      const float4 q = ld_stream(reinterpret_cast<const float4*>(x) + v);
+      float4 o;
+      o.x = scale * expf(q.x - m) + (c0 + 0 == t ? -gm : -0.0f);
+      o.y = scale * expf(q.y - m) + (c0 + 1 == t ? -gm : -0.0f);
+      o.z = scale * expf(q.z - m) + (c0 + 2 == t ? -gm : -0.0f);
+      o.w = scale * expf(q.w - m) + (c0 + 3 == t ? -gm : -0.0f);
+      st_stream(reinterpret_cast<float4*>(dx) + v, o);
+    } else {
+      const float q = ld_stream(x + v);
+      st_stream(dx + v, scale * expf(q - m) + (c0 == t ? -gm : -0.0f));
+    }
+  }
+}
+
+static unsigned row_grid(int64_t rows) {
+  const int64_t cap = (int64_t)sm_count() * 64;
+  return (unsigned)(rows < cap ? rows : cap);
+}
+
+static int row_block(int64_t cols) { return cols >= 8192 ? 512 : cols >= 1024 ? 256 : 128; }
+
+static oxc_status check_shape(const char* fn, int64_t rows, int64_t cols) {
+  if (rows < 0 || cols < 0)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: negative shape", fn);
+  if (cols > 0x7fffffff)
+    return fail(OXC_ERR_NOT_IMPLEMENTED, "not implemented: %s: rows wider than 2^31", fn);
+  return OXC_OK;
+}
+
+}  // namespace oxc
+
+using namespace oxc;
+
+extern "C" {
+
+oxc_status oxc_softmax_fwd(const float* x, float* y, int64_t rows, int64_t cols, int32_t log,
+                           void* stream) {
+  oxc_status st = check_shape(log ? "log_softmax" : "softmax", rows, cols);
+  if (st) return st;
+  if (rows == 0 || cols == 0) return OXC_OK;
+  if (!x || !y) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: softmax: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool v4 = cols % 4 == 0 && aligned16(x) && aligned16(y);
+  const unsigned grid = row_grid(rows);
+  const int block = row_block(cols);
+  if (v4) {
+    if (log) softmax_fwd_kernel<4, true><<<grid, block, 0, s>>>(x, y, rows, (int)cols);
+    else softmax_fwd_kernel<4, false><<<grid, block, 0, s>>>(x, y, rows, (int)cols);
+  } else {
+    if (log) softmax_fwd_kernel<1, true><<<grid, block, 0, s>>>(x, y, rows, (int)cols);
+    else softmax_fwd_kernel<1, false><<<grid, block, 0, s>>>(x, y, rows, (int)cols);
+  }
+  return check_launch("oxc_softmax_fwd");
+}
+
+oxc_status oxc_softmax_bwd(const float* y, const float* dy, float* dx, int64_t rows, int64_t cols,
+                           int32_t log, void* stream) {
+  oxc_status st = check_shape(log ? "log_softmax backward" : "softmax backward", rows, cols);
+  if (st) return st;
+  if (rows == 0 || cols == 0) return OXC_OK;
+  if (!y || !dy || !dx)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: softmax backward: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool v4 = cols % 4 == 0 && aligned16(y) && aligned16(dy) && aligned16(dx);
+  const unsigned grid = row_grid(rows);
+  const int block = row_block(cols);
+  if (v4) {
+    if (log) softmax_bwd_kernel<4, true><<<grid, block, 0, s>>>(y, dy, dx, rows, (int)cols);
+    else softmax_bwd_kernel<4, false><<<grid, block, 0, s>>>(y, dy, dx, rows, (int)cols);
+  } else {
+    if (log) softmax_bwd_kernel<1, true><<<grid, block, 0, s>>>(y, dy, dx, rows, (int)cols);
+    else softmax_bwd_kernel<1, false><<<grid, block, 0, s>>>(y, dy, dx, rows, (int)cols);
+  }
+  return check_launch("oxc_softmax_bwd");
+}
+
+oxc_status oxc_cross_entropy_fwd(const float* logits, const int64_t* targets, float* loss,
+                                 float* row_max, float* row_sum, float* row_nll, int64_t rows,
+                                 int64_t cols, int64_t total_rows, int32_t* err_flag,
+                                 void* stream) {
+  oxc_status st = check_shape("cross_entropy", rows, cols);
+  if (st) return st;
+  if (total_rows < rows || total_rows <= 0)
+    return fail(OXC_ERR_INVALID_ARGUMENT,
+                "invalid argument: cross_entropy: total_rows %lld must cover the %lld local rows",
+                (long long)total_rows, (long long)rows);
+  if (cols == 0)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: cross_entropy over zero classes");
+  if (!logits || !targets || !loss || !row_max || !row_sum || !row_nll)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: cross_entropy: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (rows > 0) {
+    const bool v4 = cols % 4 == 0 && aligned16(logits);
+    const unsigned grid = row_grid(rows);
+    const int block = row_block(cols);
+    if (v4)
+      ce_fwd_kernel<4><<<grid, block, 0, s>>>(logits, targets, row_max, row_sum, row_nll, rows,
+                                              (int)cols, err_flag);
+    else
+      ce_fwd_kernel<1><<<grid, block, 0, s>>>(logits, targets, row_max, row_sum, row_nll, rows,
+                                              (int)cols, err_flag);
+    st = check_launch("oxc_cross_entropy_fwd");
+    if (st) return st;
+  }
+  ce_loss_kernel<<<1, 1024, 0, s>>>(row_nll, rows, total_rows, loss);
+  return check_launch("oxc_cross_entropy_fwd (loss)");
+}
+
+oxc_status oxc_cross_entropy_bwd(const float* logits, const int64_t* targets,
+                                 const float* row_max, const float* row_sum,
+                                 const float* grad_loss, float* dlogits, int64_t rows,
+                                 int64_t cols, int64_t total_rows, void* stream) {
+  oxc_status st = check_shape("cross_entropy backward", rows, cols);
+  if (st) return st;
+  if (total_rows < rows || total_rows <= 0)
+    return fail(OXC_ERR_INVALID_ARGUMENT,
+                "invalid argument: cross_entropy backward: total_rows must cover the local rows");
+  if (rows == 0 || cols == 0) return OXC_OK;
+  if (!logits || !targets || !row_max || !row_sum || !dlogits)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: cross_entropy backward: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool v4 = cols % 4 == 0 && aligned16(logits) && aligned16(dlogits);
+  const float inv_total = 1.0f / (float)total_rows;  // the mean VJP's 1/M (f32)
+  const int block = 256;
+  const int64_t work = rows * (v4 ? cols / 4 : cols);
+  const int64_t cap = (int64_t)sm_count() * 8 * 4;  // 8 CTAs of 256 per SM, 4 waves of ILP
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((work + block - 1) / block, cap));
+  if (v4)
+    ce_bwd_kernel<4><<<grid, block, 0, s>>>(logits, targets, row_max, row_sum, grad_loss, dlogits,
+                                            rows, (int)cols, inv_total);
+  else
+    ce_bwd_kernel<1><<<grid, block, 0, s>>>(logits, targets, row_max, row_sum, grad_loss, dlogits,
+                                            rows, (int)cols, inv_total);
+  return check_launch("oxc_cross_entropy_bwd");
+}
+
+}  // extern "C"

@@ -184,3 +184,124 @@ def layer_norm_gelu(x, weight, bias, eps=1e-5, grad_mode="ref"):
     """F.gelu(F.layer_norm(x, weight, bias, eps)) as one fused kernel each way
     (functional.py:227-233 then 194-199)."""
     return _LayerNorm.apply(x, weight, bias, eps, N.ACT_GELU_TANH, grad_mode)
+
+
+# ---- softmax / log_softmax ----------------------------------------------------------
+
+def _last_dim_only(dim, x):
+    if dim not in (-1, x.dim() - 1):
+        raise NotImplementedError("not implemented: softmax over a dim other than the last")
+
+
+def softmax_fwd(x, log=False):
+    _require_cuda_f32("x", x)
+    x = _row_major("x", x)
+    rows, cols = _rows_cols(x)
+    y = torch.empty_like(x)
+    N.check(N.load().oxc_softmax_fwd(x.data_ptr(), y.data_ptr(), rows, cols, int(log), _stream()),
+            "softmax")
+    return y
+
+
+def softmax_bwd(y, dy, log=False):
+    rows, cols = _rows_cols(y)
+    dy = _row_major("dy", dy)
+    dx = torch.empty_like(y)
+    N.check(N.load().oxc_softmax_bwd(y.data_ptr(), dy.data_ptr(), dx.data_ptr(), rows, cols,
+                                     int(log), _stream()), "softmax backward")
+    return dx
+
+
+class _Softmax(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, log):
+        y = softmax_fwd(x, log)
+        ctx.save_for_backward(y)
+        ctx.log = log
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        (y,) = ctx.saved_tensors
+        return softmax_bwd(y, dy.contiguous(), ctx.log), None
+
+
+def softmax(x, dim=-1):
+    """F.softmax (functional.py:211-215), numerically stable, over the last dim."""
+    _last_dim_only(dim, x)
+    return _Softmax.apply(x, False)
+
+
+def log_softmax(x, dim=-1):
+    """F.log_softmax (functional.py:218-222) over the last dim."""
+    _last_dim_only(dim, x)
+    return _Softmax.apply(x, True)
+
+
+# ---- cross-entropy ----------------------------------------------------------------------
+
+def _targets_tensor(targets, n, classes, device):
+    """The reference takes a Python list and indexes a numpy one-hot with it
+    (functional.py:285-289): the same length check and numpy's index rules."""
+    if isinstance(targets, torch.Tensor):
+        t = targets.to(device=device, dtype=torch.int64).reshape(-1)
+        if t.numel() != n:
+            raise ValueError(f"{t.numel()} targets for batch of {n}")
+        return t.contiguous()
+    if len(targets) != n:
+        raise ValueError(f"{len(targets)} targets for batch of {n}")
+    for v in targets:
+        if not -classes <= int(v) < classes:
+            raise IndexError(f"index {int(v)} is out of bounds for axis 1 with size {classes}")
+    return torch.tensor([int(v) for v in targets], dtype=torch.int64, device=device)
+
+
+def cross_entropy_fwd(logits, targets, total_rows=None):
+    """Returns (loss[1], row_max, row_sum, row_nll)."""
+    _require_cuda_f32("logits", logits)
+    logits = _row_major("logits", logits)
+    if logits.dim() != 2:
+        raise ValueError(f"invalid argument: cross_entropy expects [n, classes] logits, got {list(logits.shape)}")
+    n, classes = logits.shape
+    t = _targets_tensor(targets, n, classes, logits.device)
+    loss = torch.empty(1, dtype=torch.float32, device=logits.device)
+    row_max = torch.empty(n, dtype=torch.float32, device=logits.device)
+    row_sum = torch.empty_like(row_max)
+    row_nll = torch.empty_like(row_max)
+    flag = torch.zeros(4, dtype=torch.int32, device=logits.device)
+    L = N.load()
+    N.check(L.oxc_cross_entropy_fwd(logits.data_ptr(), t.data_ptr(), loss.data_ptr(),
+                                    row_max.data_ptr(), row_sum.data_ptr(), row_nll.data_ptr(), n,
+                                    classes, int(total_rows or n), flag.data_ptr(), _stream()),
+            "cross_entropy")
+    return loss, row_max, row_sum, row_nll, t, flag
+
+
+def cross_entropy_bwd(logits, t, row_max, row_sum, grad_loss=None, total_rows=None):
+    n, classes = logits.shape
+    dlogits = torch.empty_like(logits)
+    N.check(N.load().oxc_cross_entropy_bwd(
+        logits.data_ptr(), t.data_ptr(), row_max.data_ptr(), row_sum.data_ptr(),
+        None if grad_loss is None else grad_loss.data_ptr(), dlogits.data_ptr(), n, classes,
+        int(total_rows or n), _stream()), "cross_entropy backward")
+    return dlogits
+
+
+class _CrossEntropy(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, logits, targets):
+        loss, row_max, row_sum, _, t, _ = cross_entropy_fwd(logits, targets)
+        ctx.save_for_backward(logits, t, row_max, row_sum)
+        return loss.reshape(())
+
+    @staticmethod
+    def backward(ctx, g):
+        logits, t, row_max, row_sum = ctx.saved_tensors
+        g = g.reshape(1).to(torch.float32).contiguous()
+        return cross_entropy_bwd(logits, t, row_max, row_sum, g), None
+
+
+def cross_entropy(logits, targets):
+    """F.cross_entropy (functional.py:277-293): mean over the batch of
+    -log_softmax(logits)[i, targets[i]]."""
+    return _CrossEntropy.apply(logits, targets)

@@ -66,6 +66,19 @@ def reference_budget(oracle, run, libm=("tanh",), ulps=LIBM_ULPS):
     return base, budget
 
 
+def max_vjp_budget(oracle, run):
+    """Per-element |run() - run() without the max node's VJP| (nonzero only on
+    argmax columns): what the kernels' omission of that exact-zero term can
+    change."""
+    base = run()
+    oracle.SKIP_MAX_VJP[0] = True
+    try:
+        alt = run()
+    finally:
+        oracle.SKIP_MAX_VJP[0] = False
+    return [np.abs(np.asarray(a, np.float64) - np.asarray(b, np.float64)) for a, b in zip(alt, base)]
+
+
 def libm_budget(oracle, run, names=("tanh",), ulps=LIBM_ULPS):
     """Per-output elementwise |run() - run() with `names` shifted by +-ulps|,
     maximised over both directions.  `run` returns a tuple of arrays."""
