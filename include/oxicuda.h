@@ -152,6 +152,26 @@ oxc_status oxc_cross_entropy_bwd(const float* logits, const int64_t* targets,
                                  const float* grad_loss, float* dlogits, int64_t rows,
                                  int64_t cols, int64_t total_rows, void* stream);
 
+/* ---- embedding: F.embedding = weight.index_select(0, ids) and its VJP -------
+ * (python/oxitorch/nn/functional.py:245-247; crates/oxi-tensor/src/lib.rs:665-703;
+ * VJP crates/oxi-autograd/src/ops.rs:741-769).  ids int64 [n] (negative ids
+ * count from the end of the whole table); out / dout [n, cols].
+ * The table on this GPU holds rows [vocab_offset, vocab_offset + rows) of a
+ * vocab_total-row table (vocab_offset = 0, rows = vocab_total unsharded).
+ * Forward: ids of other shards give zero rows.  Backward: dtable [rows, cols]
+ * is written in full; row r is the left-to-right sum of dout over r's
+ * occurrences in position order (bit-identical to the reference) when r
+ * occurs at most 128 times, else the sum of 128-occurrence pieces.  Ids out
+ * of range of the whole table are recorded in err_flag (int32[4]). */
+oxc_status oxc_embedding_fwd(const float* table, const int64_t* ids, float* out, int64_t n,
+                             int64_t vocab_total, int64_t vocab_offset, int64_t rows,
+                             int64_t cols, int32_t* err_flag, void* stream);
+size_t oxc_embedding_bwd_workspace_size(int64_t n, int64_t rows, int64_t cols);
+oxc_status oxc_embedding_bwd(const float* dout, const int64_t* ids, float* dtable, int64_t n,
+                             int64_t vocab_total, int64_t vocab_offset, int64_t rows,
+                             int64_t cols, int32_t* err_flag, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
 /* ---- LayerNorm backward without a caller workspace ------------------------
  * No counterpart in the reference: an addition for callers that cannot call
  * cudaMalloc (a host that owns all device memory through its own pool, or a

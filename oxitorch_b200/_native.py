@@ -75,6 +75,9 @@ SIGNATURES = {
     "oxc_softmax_bwd": (_I32, [_P, _P, _P, _I64, _I64, _I32, _P]),
     "oxc_cross_entropy_fwd": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P]),
     "oxc_cross_entropy_bwd": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
+    "oxc_embedding_fwd": (_I32, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P]),
+    "oxc_embedding_bwd_workspace_size": (_SZ, [_I64, _I64, _I64]),
+    "oxc_embedding_bwd": (_I32, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _SZ, _P]),
     "oxc_layer_norm_bwd_noalloc": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32,
                                           _I32, _P]),
 }

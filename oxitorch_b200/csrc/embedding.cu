@@ -1,0 +1,410 @@
+// embedding.cu -- F.embedding forward (Tensor::index_select along dim 0) and
+// its duplicate-id VJP (scatter_index_select).
+//
+// Reference: python/oxitorch/nn/functional.py:245-247 -> weight.index_select(0, ids)
+//   forward  crates/oxi-tensor/src/lib.rs:665-703: ids validated first (negative
+//            ids count from the end; out of range -> OutOfBounds), then a row copy.
+//   VJP      crates/oxi-autograd/src/ops.rs:741-769: dtable = zeros, then
+//            dtable[id_k] += dout[k] for k in position order -- so every table row
+//            is a left-to-right f32 sum, from 0.0, of its occurrences.
+//
+// B200 design:
+//   gather: one CTA per output row (grid-stride), 128-bit copies; table rows
+//     are read with L2-allocating loads (hot ids repeat), outputs streamed.
+//   VJP:
+//     1. prepare: ids -> (key = resolved row, value = position); bad ids
+//        recorded in the error flag and keyed past the table (ignored).
+//     2. stable radix sort of (key, position) pairs (CUB, header-only, part of
+//        the CUDA toolkit): equal keys keep increasing position order.
+//     3. offsets: segment starts read straight off the sorted keys.
+//     4. split pieces: rows occurring more than P times are cut at the fixed
+//        P-position blocks of the sorted array; one CTA per block sums its (at
+//        most two) pieces of such rows into partial rows.
+//     5. rows: one CTA per table row writes zeros (no occurrence), the
+//        left-to-right sum of its <= P occurrences in position order
+//        (bit-identical to the reference), or the sum of its pieces in block
+//        order (deterministic; differs from the reference only by summation
+//        order).
+//   Sharded tables (vocab-parallel): the table holds rows
+//   [vocab_offset, vocab_offset + rows); ids outside are zero rows forward
+//   and contribute nothing backward.
+#include <cub/device/device_radix_sort.cuh>
+
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace oxc {
+
+constexpr int kSplitP = 128;  // occurrences per piece for hot rows
+
+// Resolved row inside this shard, or -1 (outside the shard / out of range).
+// Sets *bad when the id is out of range of the whole table.
+__device__ __forceinline__ int64_t emb_row(int64_t id, int64_t vocab_total, int64_t offset,
+                                           int64_t rows, bool* bad) {
+  const int64_t r = id < 0 ? id + vocab_total : id;
+  if (r < 0 || r >= vocab_total) {
+    *bad = true;
+    return -1;
+  }
+  *bad = false;
+  const int64_t local = r - offset;
+  return (local >= 0 && local < rows) ? local : -1;
+}
+
+__device__ __forceinline__ void emb_record_bad(int32_t* flag, int64_t value, int64_t size) {
+  if (flag && atomicCAS(flag, 0, 1) == 0) {
+    flag[1] = (int32_t)(uint32_t)((uint64_t)value & 0xffffffffu);
+    flag[2] = (int32_t)(uint32_t)((uint64_t)value >> 32);
+    flag[3] = (int32_t)size;
+  }
+}
+
+template <int VW>
+__global__ void __launch_bounds__(256) emb_gather_kernel(
+    const float* __restrict__ table, const int64_t* __restrict__ ids, float* __restrict__ out,
+    int64_t n, int64_t vocab_total, int64_t offset, int64_t rows, int cols, int32_t* err) {
+  const int nvec = cols / VW;
+  for (int64_t k = blockIdx.x; k < n; k += gridDim.x) {
+    const int64_t id = ids[k];
+    bool bad;
+    const int64_t r = emb_row(id, vocab_total, offset, rows, &bad);
+    if (bad && threadIdx.x == 0) emb_record_bad(err, id, vocab_total);
+    float* dst = out + k * (int64_t)cols;
+    if constexpr (VW == 4) {
+      float4* d4 = reinterpret_cast<float4*>(dst);
+      if (r < 0) {
+        for (int v = threadIdx.x; v < nvec; v += blockDim.x) st_stream(d4 + v, make_float4(0, 0, 0, 0));
+      } else {
+        const float4* s4 = reinterpret_cast<const float4*>(table + r * (int64_t)cols);
+        int v = threadIdx.x;
+        for (; v + 3 * (int)blockDim.x < nvec; v += 4 * blockDim.x) {
+          float4 q[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) q[u] = ld_keep(s4 + v + u * blockDim.x);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) st_stream(d4 + v + u * blockDim.x, q[u]);
+        }
+        for (; v < nvec; v += blockDim.x) st_stream(d4 + v, ld_keep(s4 + v));
+      }
+    } else {
+      const float* src = r < 0 ? nullptr : table + r * (int64_t)cols;
+      for (int c = threadIdx.x; c < cols; c += blockDim.x)
+        st_stream(dst + c, src ? ld_keep(src + c) : 0.0f);
+    }
+  }
+}
+
+// keys[k] = row of ids[k] in this shard (rows if outside: sorts after every
+// real row and is ignored); vals[k] = k.
+__global__ void emb_prepare_kernel(const int64_t* __restrict__ ids, int64_t n, int64_t vocab_total,
+                                   int64_t offset, int64_t rows, int32_t* __restrict__ keys,
+                                   int32_t* __restrict__ vals, int32_t* err) {
+  for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n;
+       k += (int64_t)gridDim.x * blockDim.x) {
+    bool bad;
+    const int64_t r = emb_row(ids[k], vocab_total, offset, rows, &bad);
+    if (bad) emb_record_bad(err, ids[k], vocab_total);
+    keys[k] = (int32_t)(r < 0 ? rows : r);
+    vals[k] = (int32_t)k;
+  }
+}
+
+// offsets[r] = first sorted index with key >= r, for r in [0, rows].
+__global__ void emb_offsets_kernel(const int32_t* __restrict__ skeys, int64_t n, int64_t rows,
+                                   int32_t* __restrict__ offsets) {
+  for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p <= n;
+       p += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t prev = p > 0 ? min((int64_t)skeys[p - 1], rows) : -1;
+    const int64_t cur = p < n ? min((int64_t)skeys[p], rows) : rows;
+    for (int64_t r = prev + 1; r <= cur; ++r) offsets[r] = (int32_t)p;
+  }
+}
+
+// Sums dout rows spos[p0..p1) (in order) into acc for this thread's columns.
+template <int VW, int VPT>
+__device__ __forceinline__ void sum_positions(const float* __restrict__ dout,
+                                              const int32_t* __restrict__ spos, int64_t p0,
+                                              int64_t p1, int cols, int c_base,
+                                              float (&acc)[VPT][VW]) {
+  const int nvec = cols / VW;
+  int64_t p = p0;
+  for (; p + 1 < p1; p += 2) {
+    const float* ra = dout + (int64_t)spos[p] * cols;
+    const float* rb = dout + (int64_t)spos[p + 1] * cols;
+    float qa[VPT][VW], qb[VPT][VW];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int v = c_base + i * blockDim.x + threadIdx.x;
+      if (v < nvec) {
+        if constexpr (VW == 4) {
+          const float4 a = ld_stream(reinterpret_cast<const float4*>(ra) + v);
+          const float4 b = ld_stream(reinterpret_cast<const float4*>(rb) + v);
+          qa[i][0] = a.x; qa[i][1] = a.y; qa[i][2] = a.z; qa[i][3] = a.w;
+          qb[i][0] = b.x; qb[i][1] = b.y; qb[i][2] = b.z; qb[i][3] = b.w;
+        } else {
+          qa[i][0] = ld_stream(ra + v);
+          qb[i][0] = ld_stream(rb + v);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < VW; ++e) { qa[i][e] = 0.0f; qb[i][e] = 0.0f; }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < VPT; ++i)
+#pragma unroll
+      for (int e = 0; e < VW; ++e) acc[i][e] = __fadd_rn(__fadd_rn(acc[i][e], qa[i][e]), qb[i][e]);
+  }
+  if (p < p1) {
+    const float* ra = dout + (int64_t)spos[p] * cols;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int v = c_base + i * blockDim.x + threadIdx.x;
+      if (v < nvec) {
+        if constexpr (VW == 4) {
+          const float4 a = ld_stream(reinterpret_cast<const float4*>(ra) + v);
+          acc[i][0] = __fadd_rn(acc[i][0], a.x); acc[i][1] = __fadd_rn(acc[i][1], a.y);
+          acc[i][2] = __fadd_rn(acc[i][2], a.z); acc[i][3] = __fadd_rn(acc[i][3], a.w);
+        } else {
+          acc[i][0] = __fadd_rn(acc[i][0], ld_stream(ra + v));
+        }
+      }
+    }
+  }
+}
+
+template <int VW, int VPT>
+__device__ __forceinline__ void store_acc(float* dst, int cols, int c_base,
+                                          const float (&acc)[VPT][VW], bool streaming) {
+  const int nvec = cols / VW;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int v = c_base + i * blockDim.x + threadIdx.x;
+    if (v < nvec) {
+      if constexpr (VW == 4) {
+        const float4 o = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+        if (streaming) st_stream(reinterpret_cast<float4*>(dst) + v, o);
+        else reinterpret_cast<float4*>(dst)[v] = o;
+      } else {
+        if (streaming) st_stream(dst + v, acc[i][0]);
+        else dst[v] = acc[i][0];
+      }
+    }
+  }
+}
+
+// Block j of the sorted array: partial sums of the (at most two) pieces of
+// rows that occur more than kSplitP times.  Slot 2j: the row covering
+// position j*P (if split); slot 2j+1: a split row that starts inside block j.
+template <int VW, int VPT>
+__global__ void __launch_bounds__(256) emb_split_kernel(
+    const float* __restrict__ dout, const int32_t* __restrict__ skeys,
+    const int32_t* __restrict__ spos, const int32_t* __restrict__ offsets, int64_t n,
+    int64_t rows, int cols, float* __restrict__ parts) {
+  const int64_t j = blockIdx.x;
+  const int64_t b0 = j * kSplitP, b1 = min(n, b0 + kSplitP);
+  if (b0 >= n) return;
+  const int64_t keys2[2] = {skeys[b0], skeys[b1 - 1]};
+  const int nvec = cols / VW;
+  for (int side = 0; side < 2; ++side) {
+    const int64_t r = keys2[side];
+    if (r >= rows) continue;
+    if (side == 1 && r == keys2[0]) continue;
+    const int64_t s0 = offsets[r], s1 = offsets[r + 1];
+    if (s1 - s0 <= kSplitP) continue;
+    const int64_t p0 = max(s0, b0), p1 = min(s1, b1);
+    float* dst = parts + (2 * j + side) * (int64_t)cols;
+    for (int c_base = 0; c_base < nvec; c_base += VPT * blockDim.x) {
+      float acc[VPT][VW];
+#pragma unroll
+      for (int i = 0; i < VPT; ++i)
+#pragma unroll
+        for (int e = 0; e < VW; ++e) acc[i][e] = 0.0f;
+      sum_positions<VW, VPT>(dout, spos, p0, p1, cols, c_base, acc);
+      store_acc<VW, VPT>(dst, cols, c_base, acc, false);
+    }
+  }
+}
+
+template <int VW, int VPT>
+__global__ void __launch_bounds__(256) emb_rows_kernel(
+    const float* __restrict__ dout, const int32_t* __restrict__ spos,
+    const int32_t* __restrict__ offsets, const float* __restrict__ parts, int64_t rows, int cols,
+    float* __restrict__ dtable) {
+  const int nvec = cols / VW;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int64_t s0 = offsets[r], s1 = offsets[r + 1];
+    float* dst = dtable + r * (int64_t)cols;
+    for (int c_base = 0; c_base < nvec; c_base += VPT * blockDim.x) {
+      float acc[VPT][VW];
+#pragma unroll
+      for (int i = 0; i < VPT; ++i)
+#pragma unroll
+        for (int e = 0; e < VW; ++e) acc[i][e] = 0.0f;
+      if (s1 - s0 <= kSplitP) {
+        sum_positions<VW, VPT>(dout, spos, s0, s1, cols, c_base, acc);
+      } else {
+        const int64_t j0 = s0 / kSplitP, j1 = (s1 - 1) / kSplitP;
+        for (int64_t j = j0; j <= j1; ++j) {
+          const int side = (j == j0 && s0 != j0 * kSplitP) ? 1 : 0;
+          const float* src = parts + (2 * j + side) * (int64_t)cols;
+#pragma unroll
+          for (int i = 0; i < VPT; ++i) {
+            const int v = c_base + i * blockDim.x + threadIdx.x;
+            if (v < nvec) {
+              if constexpr (VW == 4) {
+                const float4 a = reinterpret_cast<const float4*>(src)[v];
+                acc[i][0] = __fadd_rn(acc[i][0], a.x); acc[i][1] = __fadd_rn(acc[i][1], a.y);
+                acc[i][2] = __fadd_rn(acc[i][2], a.z); acc[i][3] = __fadd_rn(acc[i][3], a.w);
+              } else {
+                acc[i][0] = __fadd_rn(acc[i][0], src[v]);
+              }
+            }
+          }
+        }
+      }
+      store_acc<VW, VPT>(dst, cols, c_base, acc, true);
+    }
+  }
+}
+
+struct EmbLayout {
+  size_t keys_in, vals_in, keys_out, vals_out, offsets, parts, cub, total;
+  size_t cub_bytes;
+  int end_bit;
+};
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+static oxc_status emb_layout(int64_t n, int64_t rows, int64_t cols, EmbLayout* L) {
+  int end_bit = 1;
+  while (end_bit < 31 && ((int64_t)1 << end_bit) <= rows) ++end_bit;  // keys in [0, rows]
+  size_t cub_bytes = 0;
+  cudaError_t e = cub::DeviceRadixSort::SortPairs(nullptr, cub_bytes, (const int32_t*)nullptr,
+                                                  (int32_t*)nullptr, (const int32_t*)nullptr,
+                                                  (int32_t*)nullptr, (int)n, 0, end_bit);
+  if (e != cudaSuccess) return cuda_fail(e, "embedding backward (sort workspace size)");
+  const int64_t nblocks = (n + kSplitP - 1) / kSplitP;
+  size_t off = 0;
+  L->keys_in = off; off += align256((size_t)n * 4);
+  L->vals_in = off; off += align256((size_t)n * 4);
+  L->keys_out = off; off += align256((size_t)n * 4);
+  L->vals_out = off; off += align256((size_t)n * 4);
+  L->offsets = off; off += align256((size_t)(rows + 1) * 4);
+  L->parts = off; off += align256((size_t)2 * nblocks * cols * 4);
+  L->cub = off; off += align256(cub_bytes);
+  L->total = off;
+  L->cub_bytes = cub_bytes;
+  L->end_bit = end_bit;
+  return OXC_OK;
+}
+
+static oxc_status emb_check(const char* fn, int64_t n, int64_t vocab_total, int64_t offset,
+                            int64_t rows, int64_t cols) {
+  if (n < 0 || rows < 0 || cols < 0 || vocab_total < 0 || offset < 0)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: negative size", fn);
+  if (offset + rows > vocab_total)
+    return fail(OXC_ERR_INVALID_ARGUMENT,
+                "invalid argument: %s: shard [%lld, %lld) exceeds the table of %lld rows", fn,
+                (long long)offset, (long long)(offset + rows), (long long)vocab_total);
+  if (n > 0x7fffffff || rows >= 0x7fffffff || cols > 0x7fffffff)
+    return fail(OXC_ERR_NOT_IMPLEMENTED, "not implemented: %s: sizes beyond 2^31", fn);
+  return OXC_OK;
+}
+
+}  // namespace oxc
+
+using namespace oxc;
+
+extern "C" {
+
+oxc_status oxc_embedding_fwd(const float* table, const int64_t* ids, float* out, int64_t n,
+                             int64_t vocab_total, int64_t vocab_offset, int64_t rows,
+                             int64_t cols, int32_t* err_flag, void* stream) {
+  oxc_status st = emb_check("embedding", n, vocab_total, vocab_offset, rows, cols);
+  if (st) return st;
+  if (n == 0 || cols == 0) return OXC_OK;
+  if (!ids || !out || (rows > 0 && !table))
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: embedding: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool v4 = cols % 4 == 0 && aligned16(table) && aligned16(out);
+  const unsigned grid = (unsigned)std::min<int64_t>(n, (int64_t)sm_count() * 16);
+  const int block = v4 ? (int)std::min<int64_t>(256, std::max<int64_t>(32, ((cols / 4 + 31) / 32) * 32))
+                       : (int)std::min<int64_t>(256, std::max<int64_t>(32, ((cols + 31) / 32) * 32));
+  if (v4)
+    emb_gather_kernel<4><<<grid, block, 0, s>>>(table, ids, out, n, vocab_total, vocab_offset,
+                                                rows, (int)cols, err_flag);
+  else
+    emb_gather_kernel<1><<<grid, block, 0, s>>>(table, ids, out, n, vocab_total, vocab_offset,
+                                                rows, (int)cols, err_flag);
+  return check_launch("oxc_embedding_fwd");
+}
+
+size_t oxc_embedding_bwd_workspace_size(int64_t n, int64_t rows, int64_t cols) {
+  if (n <= 0 || rows < 0 || cols <= 0) return 0;
+  EmbLayout L;
+  if (emb_layout(n, rows, cols, &L) != OXC_OK) return 0;
+  return L.total;
+}
+
+oxc_status oxc_embedding_bwd(const float* dout, const int64_t* ids, float* dtable, int64_t n,
+                             int64_t vocab_total, int64_t vocab_offset, int64_t rows,
+                             int64_t cols, int32_t* err_flag, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  oxc_status st = emb_check("embedding backward", n, vocab_total, vocab_offset, rows, cols);
+  if (st) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (rows == 0 || cols == 0) return OXC_OK;
+  if (!dtable) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: embedding backward: null pointer");
+  if (n == 0) {
+    cudaError_t e = cudaMemsetAsync(dtable, 0, (size_t)rows * cols * sizeof(float), s);
+    return e == cudaSuccess ? OXC_OK : cuda_fail(e, "oxc_embedding_bwd");
+  }
+  if (!dout || !ids)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: embedding backward: null pointer");
+  EmbLayout L;
+  st = emb_layout(n, rows, cols, &L);
+  if (st) return st;
+  if (!workspace || workspace_bytes < L.total)
+    return fail(OXC_ERR_INVALID_ARGUMENT,
+                "invalid argument: embedding backward needs a %zu-byte workspace, got %zu",
+                L.total, workspace_bytes);
+  char* ws = static_cast<char*>(workspace);
+  int32_t* keys_in = reinterpret_cast<int32_t*>(ws + L.keys_in);
+  int32_t* vals_in = reinterpret_cast<int32_t*>(ws + L.vals_in);
+  int32_t* keys_out = reinterpret_cast<int32_t*>(ws + L.keys_out);
+  int32_t* vals_out = reinterpret_cast<int32_t*>(ws + L.vals_out);
+  int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
+  float* parts = reinterpret_cast<float*>(ws + L.parts);
+  const unsigned g1 = (unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)sm_count() * 8);
+  emb_prepare_kernel<<<g1, 256, 0, s>>>(ids, n, vocab_total, vocab_offset, rows, keys_in, vals_in,
+                                        err_flag);
+  st = check_launch("oxc_embedding_bwd (prepare)");
+  if (st) return st;
+  size_t cub_bytes = L.cub_bytes;
+  cudaError_t e = cub::DeviceRadixSort::SortPairs(ws + L.cub, cub_bytes, keys_in, keys_out,
+                                                  vals_in, vals_out, (int)n, 0, L.end_bit, s);
+  if (e != cudaSuccess) return cuda_fail(e, "oxc_embedding_bwd (sort)");
+  const unsigned g2 = (unsigned)std::min<int64_t>((n + 1 + 255) / 256, (int64_t)sm_count() * 8);
+  emb_offsets_kernel<<<g2, 256, 0, s>>>(keys_out, n, rows, offsets);
+  st = check_launch("oxc_embedding_bwd (offsets)");
+  if (st) return st;
+  const bool v4 = cols % 4 == 0 && aligned16(dout) && aligned16(dtable);
+  const int64_t nblocks = (n + kSplitP - 1) / kSplitP;
+  const unsigned grows = (unsigned)std::min<int64_t>(rows, (int64_t)sm_count() * 32);
+  if (v4) {
+    emb_split_kernel<4, 4><<<(unsigned)nblocks, 256, 0, s>>>(dout, keys_out, vals_out, offsets, n,
+                                                             rows, (int)cols, parts);
+    emb_rows_kernel<4, 4><<<grows, 256, 0, s>>>(dout, vals_out, offsets, parts, rows, (int)cols,
+                                                dtable);
+  } else {
+    emb_split_kernel<1, 4><<<(unsigned)nblocks, 256, 0, s>>>(dout, keys_out, vals_out, offsets, n,
+                                                             rows, (int)cols, parts);
+    emb_rows_kernel<1, 4><<<grows, 256, 0, s>>>(dout, vals_out, offsets, parts, rows, (int)cols,
+                                                dtable);
+  }
+  return check_launch("oxc_embedding_bwd");
+}
+
+}  // extern "C"

@@ -305,3 +305,71 @@ def cross_entropy(logits, targets):
     """F.cross_entropy (functional.py:277-293): mean over the batch of
     -log_softmax(logits)[i, targets[i]]."""
     return _CrossEntropy.apply(logits, targets)
+
+
+# ---- embedding ----------------------------------------------------------------------------
+
+def _ids_tensor(indices, vocab, device):
+    """The reference validates every id before copying (lib.rs:665-675):
+    negative ids count from the end, anything else out of range raises."""
+    if isinstance(indices, torch.Tensor):
+        return indices.to(device=device, dtype=torch.int64).reshape(-1).contiguous()
+    ids = [int(i) for i in indices]
+    for i in ids:
+        idx = vocab + i if i < 0 else i
+        if idx < 0 or idx >= vocab:
+            raise RuntimeError(f"out of bounds: index {i} out of range for dim 0 of size {vocab}")
+    return torch.tensor(ids, dtype=torch.int64, device=device)
+
+
+def embedding_fwd(ids, weight, vocab_offset=0, vocab_total=None):
+    """out [n, cols] = weight[ids]; weight may be a vocab shard."""
+    _require_cuda_f32("weight", weight)
+    weight = _row_major("weight", weight)
+    rows, cols = weight.shape
+    total = int(vocab_total or rows)
+    out = torch.empty(ids.numel(), cols, dtype=torch.float32, device=weight.device)
+    flag = torch.zeros(4, dtype=torch.int32, device=weight.device)
+    N.check(N.load().oxc_embedding_fwd(weight.data_ptr(), ids.data_ptr(), out.data_ptr(),
+                                       ids.numel(), total, int(vocab_offset), rows, cols,
+                                       flag.data_ptr(), _stream()), "embedding")
+    return out, flag
+
+
+def embedding_bwd(ids, dout, rows, vocab_offset=0, vocab_total=None):
+    """dtable [rows, cols] for dout [n, cols]."""
+    dout = _row_major("dout", dout)
+    n, cols = ids.numel(), dout.shape[-1]
+    total = int(vocab_total or rows)
+    dtable = torch.empty(rows, cols, dtype=torch.float32, device=dout.device)
+    flag = torch.zeros(4, dtype=torch.int32, device=dout.device)
+    L = N.load()
+    ws = _workspace(L.oxc_embedding_bwd_workspace_size(n, rows, cols), dout.device)
+    N.check(L.oxc_embedding_bwd(dout.data_ptr(), ids.data_ptr(), dtable.data_ptr(), n, total,
+                                int(vocab_offset), rows, cols, flag.data_ptr(), ws.data_ptr(),
+                                ws.numel(), _stream()), "embedding backward")
+    return dtable, flag
+
+
+class _Embedding(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, ids, weight):
+        out, _ = embedding_fwd(ids, weight)
+        ctx.save_for_backward(ids)
+        ctx.rows = weight.shape[0]
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        (ids,) = ctx.saved_tensors
+        dtable, _ = embedding_bwd(ids, dout.contiguous(), ctx.rows)
+        return None, dtable
+
+
+def embedding(indices, weight):
+    """F.embedding (functional.py:245-247): weight.index_select(0, indices);
+    indices is a flat list of ints (or an int tensor); the output is
+    [len(indices), dim]."""
+    _require_cuda_f32("weight", weight)
+    ids = _ids_tensor(indices, weight.shape[0], weight.device)
+    return _Embedding.apply(ids, weight)
