@@ -102,6 +102,51 @@ int32_t oxc_cmp_op_id(const char* name);
 int32_t oxc_unary_op_id(const char* name);
 int32_t oxc_reduce_kind_id(const char* name);
 
+/* ---- elementwise registry engine ---------------------------------------
+ * out must be dense row-major with the broadcast shape of the inputs; inputs
+ * are arbitrary strided/broadcast views.  Replaces Tensor::binary_op / cmp_op /
+ * unary_op (crates/oxi-tensor/src/lib.rs:263-357, iterate.rs:21-75) with
+ * NumPy broadcasting (layout.rs:67-114; incompatible shapes ->
+ * OXC_ERR_SHAPE_MISMATCH "shape mismatch: [..] vs [..]").  Comparison results
+ * are 1.0 / 0.0 (lib.rs:302). */
+oxc_status oxc_binary(int32_t op, const oxc_view* a, const oxc_view* b, const oxc_view* out,
+                      void* stream);
+oxc_status oxc_cmp(int32_t op, const oxc_view* a, const oxc_view* b, const oxc_view* out,
+                   void* stream);
+oxc_status oxc_unary(int32_t op, const oxc_view* in, const oxc_view* out, void* stream);
+/* a op scalar with the scalar as a kernel argument instead of a full-shape
+ * constant tensor (replaces const_full, crates/oxi-bindings/src/lib.rs:86-104);
+ * scalar_first != 0 computes (scalar op a).  Same values: a Python scalar is
+ * rounded to f32 and broadcast either way. */
+oxc_status oxc_binary_scalar(int32_t op, const oxc_view* a, float scalar, int32_t scalar_first,
+                             const oxc_view* out, void* stream);
+
+/* ---- reductions ----------------------------------------------------------
+ * Tensor::reduce(kind, dim, keepdim) (crates/oxi-tensor/src/lib.rs:519-576,
+ * ReduceKind::reduce_strip ops.rs:246-285): `out` is dense f32 with the input
+ * shape minus `dim` (or with 1 there when keepdim); argmax/argmin come back as
+ * float indices, the reference's f32 carrier (lib.rs:568-572).  Strips that
+ * are not contiguous are folded left to right per output (the reference's own
+ * order); long strips over few outputs need the workspace that
+ * oxc_reduce_workspace_size reports (0 otherwise). */
+size_t oxc_reduce_workspace_size(int32_t kind, const oxc_view* in, int64_t dim);
+oxc_status oxc_reduce(int32_t kind, const oxc_view* in, int64_t dim, int32_t keepdim,
+                      const oxc_view* out, void* workspace, size_t workspace_bytes, void* stream);
+/* Whole-tensor reduction (reduce_strip over every element, as the Python
+ * t.sum()/t.mean()/... without a dim: crates/oxi-bindings/src/lib.rs:126-143;
+ * sum_all/mean_all/norm, lib.rs:582-604).  Deterministic two-stage reduction
+ * with f64 partials; writes the f32 result to out[0] and, if out_f64 is not
+ * NULL, the f64 value to out_f64[0] (device pointers). */
+size_t oxc_reduce_all_workspace_size(int64_t numel);
+oxc_status oxc_reduce_all(int32_t kind, const oxc_view* in, float* out, double* out_f64,
+                          void* workspace, size_t workspace_bytes, void* stream);
+/* sum over 1..16 tensors of sum(v*v), in f64 (device out[0]): the total norm
+ * of clip_grad_norm_ (python/oxitorch/optim.py:242-263) without a host round
+ * trip per gradient. */
+size_t oxc_sum_squares_workspace_size(const oxc_view* views, int32_t count);
+oxc_status oxc_sum_squares(const oxc_view* views, int32_t count, double* out, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
 /* ---- RMSNorm: F.rms_norm (python/oxitorch/nn/functional.py:236-240) -------
  * x, y, dy, dx: [rows, cols] row-major; w, dw: [cols]; rstd: [rows]
  * (saved 1/sqrt(mean(x^2)+eps) per row). */

@@ -64,6 +64,16 @@ SIGNATURES = {
     "oxc_cmp_op_id": (_I32, [ctypes.c_char_p]),
     "oxc_unary_op_id": (_I32, [ctypes.c_char_p]),
     "oxc_reduce_kind_id": (_I32, [ctypes.c_char_p]),
+    "oxc_binary": (_I32, [_I32, _VP, _VP, _VP, _P]),
+    "oxc_cmp": (_I32, [_I32, _VP, _VP, _VP, _P]),
+    "oxc_unary": (_I32, [_I32, _VP, _VP, _P]),
+    "oxc_binary_scalar": (_I32, [_I32, _VP, _F32, _I32, _VP, _P]),
+    "oxc_reduce_workspace_size": (_SZ, [_I32, _VP, _I64]),
+    "oxc_reduce": (_I32, [_I32, _VP, _I64, _I32, _VP, _P, _SZ, _P]),
+    "oxc_reduce_all_workspace_size": (_SZ, [_I64]),
+    "oxc_reduce_all": (_I32, [_I32, _VP, _P, _P, _P, _SZ, _P]),
+    "oxc_sum_squares_workspace_size": (_SZ, [_VP, _I32]),
+    "oxc_sum_squares": (_I32, [_VP, _I32, _P, _P, _SZ, _P]),
     "oxc_rms_norm_fwd": (_I32, [_P, _P, _P, _P, _I64, _I64, _F32, _P]),
     "oxc_rms_norm_bwd_workspace_size": (_SZ, [_I64, _I64]),
     "oxc_rms_norm_bwd": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _P, _SZ, _P]),

@@ -1,0 +1,407 @@
+// elementwise.cu -- the registry of elementwise ops over strided/broadcast views.
+//
+// Reference: crates/oxi-tensor/src/ops.rs:55-202 (F32_BINARY_OPS, F32_CMP_OPS,
+// F32_UNARY_OPS), dispatched by Tensor::binary_op / cmp_op / unary_op
+// (crates/oxi-tensor/src/lib.rs:263-357) over iterate::map_n (iterate.rs:21-75)
+// with NumPy broadcasting (layout.rs:67-114).  Every op is the same IEEE f32
+// operation: + - * / sqrt are correctly rounded on both sides (bit-identical),
+// min/max ignore NaN like f32::min/max, sign follows f32::signum (never 0),
+// round is half away from zero; exp/log/log2/log10/sin/cos/tanh/pow call
+// CUDA's libm (a few ulp from glibc's).
+//
+// The host side broadcasts (ShapeMismatch on incompatible shapes), turns every
+// operand into strides over the output grid (0 on broadcast dims), drops
+// size-1 dims and merges dims that are contiguous for every operand.  Then:
+//   contiguous: every operand dense (or a scalar): 128-bit grid-stride loop;
+//   tiled:      a 2-D problem where an operand is column-major (a transposed
+//               view): 32x32 tiles through shared memory, so both the
+//               column-major read and the row-major write are coalesced;
+//   general:    any strides, index arithmetic per element (up to 8 dims).
+// Outputs are always dense row-major, like the reference's from_results.
+#include <math.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+
+namespace oxc {
+
+enum ElemKind { EK_UNARY = 0, EK_BINARY = 1, EK_CMP = 2 };
+
+__device__ __forceinline__ float rust_signum(float a) {
+  return isnan(a) ? a : (signbit(a) ? -1.0f : 1.0f);
+}
+
+__device__ __forceinline__ float unary_op(int op, float a) {
+  switch (op) {
+    case 0: return -a;
+    case 1: return fabsf(a);
+    case 2: return __fsqrt_rn(a);
+    case 3: return __fdiv_rn(1.0f, __fsqrt_rn(a));
+    case 4: return expf(a);
+    case 5: return logf(a);
+    case 6: return log2f(a);
+    case 7: return log10f(a);
+    case 8: return sinf(a);
+    case 9: return cosf(a);
+    case 10: return tanhf(a);
+    case 11: return fmaxf(a, 0.0f);
+    case 12: return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-a)));
+    case 13: return floorf(a);
+    case 14: return ceilf(a);
+    case 15: return roundf(a);
+    case 16: return rust_signum(a);
+    case 17: return __fmul_rn(a, a);
+    default: return __fdiv_rn(1.0f, a);
+  }
+}
+
+__device__ __forceinline__ float binary_op(int op, float a, float b) {
+  switch (op) {
+    case 0: return __fadd_rn(a, b);
+    case 1: return __fsub_rn(a, b);
+    case 2: return __fmul_rn(a, b);
+    case 3: return __fdiv_rn(a, b);
+    case 4: return powf(a, b);
+    case 5: return fminf(a, b);
+    default: return fmaxf(a, b);
+  }
+}
+
+__device__ __forceinline__ float cmp_op(int op, float a, float b) {
+  bool r;
+  switch (op) {
+    case 0: r = a == b; break;
+    case 1: r = a != b; break;
+    case 2: r = a < b; break;
+    case 3: r = a <= b; break;
+    case 4: r = a > b; break;
+    default: r = a >= b; break;
+  }
+  return r ? 1.0f : 0.0f;
+}
+
+__device__ __forceinline__ float apply(int kind, int op, float a, float b) {
+  return kind == EK_UNARY ? unary_op(op, a) : kind == EK_BINARY ? binary_op(op, a, b)
+                                                                : cmp_op(op, a, b);
+}
+
+struct Grid {
+  int nd;
+  int64_t n[OXC_MAX_DIMS];
+  int64_t st[2][OXC_MAX_DIMS];  // per input, in elements (0 = broadcast)
+};
+
+// One input: a tensor (p, strides in Grid), or a single value broadcast
+// everywhere -- read from device memory at p (a zero-stride view) or the
+// host-provided v when p is null.
+struct Operand {
+  const float* p;
+  float v;
+  int scalar;
+};
+
+__device__ __forceinline__ float scalar_value(const Operand& o) { return o.p ? __ldg(o.p) : o.v; }
+
+// Contiguous path: every tensor operand dense.  VW = 4 needs them 16-byte
+// aligned.
+template <int VW>
+__global__ void __launch_bounds__(256) elem_dense_kernel(int kind, int op, Operand a, Operand b,
+                                                         float* __restrict__ out, int64_t n) {
+  const float sa = a.scalar ? scalar_value(a) : 0.0f;
+  const float sb = (kind != EK_UNARY && b.scalar) ? scalar_value(b) : 0.0f;
+  const int64_t nv = n / VW;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += stride) {
+    if constexpr (VW == 4) {
+      const float4 x = a.scalar ? make_float4(sa, sa, sa, sa)
+                                : ld_stream(reinterpret_cast<const float4*>(a.p) + v);
+      float4 y = make_float4(sb, sb, sb, sb);
+      if (kind != EK_UNARY && !b.scalar) y = ld_stream(reinterpret_cast<const float4*>(b.p) + v);
+      float4 o;
+      o.x = apply(kind, op, x.x, y.x);
+      o.y = apply(kind, op, x.y, y.y);
+      o.z = apply(kind, op, x.z, y.z);
+      o.w = apply(kind, op, x.w, y.w);
+      st_stream(reinterpret_cast<float4*>(out) + v, o);
+    } else {
+      const float x = a.scalar ? sa : ld_stream(a.p + v);
+      const float y = (kind == EK_UNARY || b.scalar) ? sb : ld_stream(b.p + v);
+      st_stream(out + v, apply(kind, op, x, y));
+    }
+  }
+  if constexpr (VW == 4) {  // tail
+    for (int64_t i = nv * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+      const float x = a.scalar ? sa : a.p[i];
+      const float y = (kind == EK_UNARY || b.scalar) ? sb : b.p[i];
+      out[i] = apply(kind, op, x, y);
+    }
+  }
+}
+
+// General strided path (index arithmetic per element, innermost dim fastest).
+__global__ void __launch_bounds__(256) elem_strided_kernel(int kind, int op, Operand a, Operand b,
+                                                           Grid g, float* __restrict__ out,
+                                                           int64_t n) {
+  const float sa = a.scalar ? scalar_value(a) : 0.0f;
+  const float sb = (kind != EK_UNARY && b.scalar) ? scalar_value(b) : 0.0f;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    int64_t rem = i, oa = 0, ob = 0;
+    for (int d = g.nd - 1; d >= 0; --d) {
+      const int64_t q = rem / g.n[d];
+      const int64_t idx = rem - q * g.n[d];
+      rem = q;
+      oa += idx * g.st[0][d];
+      ob += idx * g.st[1][d];
+    }
+    const float x = a.scalar ? sa : __ldg(a.p + oa);
+    const float y = (kind == EK_UNARY || b.scalar) ? sb : __ldg(b.p + ob);
+    out[i] = apply(kind, op, x, y);
+  }
+}
+
+// 2-D tiled path: out[r][c] (row-major, cols = g.n[1]); tensor inputs are
+// staged through 32x32 shared tiles; `colmajor` bit k says input k is
+// contiguous along r (a transposed view) and is read along r.
+__global__ void __launch_bounds__(256) elem_tiled_kernel(int kind, int op, Operand a, Operand b,
+                                                         Grid g, int colmajor,
+                                                         float* __restrict__ out) {
+  __shared__ float tiles[2][32][33];
+  const float sa = a.scalar ? scalar_value(a) : 0.0f;
+  const float sb = (kind != EK_UNARY && b.scalar) ? scalar_value(b) : 0.0f;
+  const int64_t R = g.n[0], C = g.n[1];
+  const int64_t tiles_c = (C + 31) / 32;
+  const int64_t ntiles = ((R + 31) / 32) * tiles_c;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+  const Operand ops[2] = {a, b};
+  const int nin = kind == EK_UNARY ? 1 : 2;
+  for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    const int64_t r0 = (t / tiles_c) * 32, c0 = (t % tiles_c) * 32;
+    for (int k = 0; k < nin; ++k) {
+      if (ops[k].scalar) continue;
+      if (colmajor & (1 << k)) {
+        // tiles[k][c][r]: consecutive lanes walk r, the contiguous dim
+        for (int j = ty; j < 32; j += 8) {
+          const int64_t r = r0 + tx, c = c0 + j;
+          tiles[k][j][tx] =
+              (r < R && c < C) ? __ldg(ops[k].p + r * g.st[k][0] + c * g.st[k][1]) : 0.0f;
+        }
+      } else {
+        for (int j = ty; j < 32; j += 8) {
+          const int64_t r = r0 + j, c = c0 + tx;
+          tiles[k][tx][j] =
+              (r < R && c < C) ? __ldg(ops[k].p + r * g.st[k][0] + c * g.st[k][1]) : 0.0f;
+        }
+      }
+    }
+    __syncthreads();
+    for (int j = ty; j < 32; j += 8) {
+      const int64_t r = r0 + j, c = c0 + tx;
+      if (r < R && c < C) {
+        const float x = a.scalar ? sa : tiles[0][tx][j];
+        const float y = (kind == EK_UNARY || b.scalar) ? sb : tiles[1][tx][j];
+        out[r * C + c] = apply(kind, op, x, y);
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ---- host-side view algebra (layout.rs) --------------------------------------
+
+static oxc_status view_ok(const oxc_view* v, const char* what) {
+  if (!v) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: null view", what);
+  if (v->ndim < 0 || v->ndim > OXC_MAX_DIMS)
+    return fail(OXC_ERR_NOT_IMPLEMENTED, "not implemented: %s: rank %d > %d", what, v->ndim,
+                OXC_MAX_DIMS);
+  for (int i = 0; i < v->ndim; ++i)
+    if (v->shape[i] < 0)
+      return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: negative dim", what);
+  return OXC_OK;
+}
+
+static void shape_str(const oxc_view* v, char* buf, size_t cap) {
+  size_t p = 0;
+  p += snprintf(buf + p, cap - p, "[");
+  for (int i = 0; i < v->ndim && p < cap; ++i)
+    p += snprintf(buf + p, cap - p, i ? ", %lld" : "%lld", (long long)v->shape[i]);
+  if (p < cap) snprintf(buf + p, cap - p, "]");
+}
+
+// layout::broadcast_shapes (layout.rs:67-88).
+static oxc_status broadcast(const oxc_view* a, const oxc_view* b, int* nd, int64_t* out) {
+  const int r = std::max(a->ndim, b->ndim);
+  for (int i = 0; i < r; ++i) {
+    const int ia = a->ndim - r + i, ib = b->ndim - r + i;
+    const int64_t da = ia >= 0 ? a->shape[ia] : 1, db = ib >= 0 ? b->shape[ib] : 1;
+    if (da != db && da != 1 && db != 1) {
+      char sa[160], sb[160];
+      shape_str(a, sa, sizeof sa);
+      shape_str(b, sb, sizeof sb);
+      return fail(OXC_ERR_SHAPE_MISMATCH, "shape mismatch: %s vs %s", sa, sb);
+    }
+    out[i] = std::max(da, db);
+  }
+  *nd = r;
+  return OXC_OK;
+}
+
+// layout::broadcast_strides (layout.rs:97-114): 0 on new and size-1 dims.
+static void bstrides(const oxc_view* v, int nd, const int64_t* shape, int64_t* st) {
+  const int off = nd - v->ndim;
+  for (int i = 0; i < nd; ++i) {
+    const int j = i - off;
+    st[i] = (j >= 0 && v->shape[j] != 1) ? v->strides[j] : 0;
+  }
+  (void)shape;
+}
+
+// Drops size-1 dims and merges dim i into i+1 when contiguous for all inputs
+// (the output is dense, so it merges whenever the inputs do).
+static void collapse(Grid* g, int nin) {
+  Grid h;
+  h.nd = 0;
+  for (int d = 0; d < g->nd; ++d) {
+    if (g->n[d] == 1) continue;
+    h.n[h.nd] = g->n[d];
+    for (int k = 0; k < 2; ++k) h.st[k][h.nd] = g->st[k][d];
+    ++h.nd;
+  }
+  Grid m;
+  m.nd = 0;
+  for (int d = 0; d < h.nd; ++d) {
+    if (m.nd > 0) {
+      bool merge = true;
+      for (int k = 0; k < nin; ++k)
+        if (m.st[k][m.nd - 1] != h.st[k][d] * h.n[d]) merge = false;
+      if (merge) {
+        m.n[m.nd - 1] *= h.n[d];
+        for (int k = 0; k < 2; ++k) m.st[k][m.nd - 1] = h.st[k][d];
+        continue;
+      }
+    }
+    m.n[m.nd] = h.n[d];
+    for (int k = 0; k < 2; ++k) m.st[k][m.nd] = h.st[k][d];
+    ++m.nd;
+  }
+  *g = m;
+}
+
+static oxc_status run_elementwise(int kind, int op, const oxc_view* a, const oxc_view* b,
+                                  const float* scalar, int scalar_first, const oxc_view* out,
+                                  cudaStream_t s, const char* fn) {
+  oxc_status st = view_ok(a, fn);
+  if (st) return st;
+  if (b && (st = view_ok(b, fn))) return st;
+  if ((st = view_ok(out, fn))) return st;
+  int nd = a->ndim;
+  int64_t shape[OXC_MAX_DIMS];
+  for (int i = 0; i < nd; ++i) shape[i] = a->shape[i];
+  if (b && (st = broadcast(a, b, &nd, shape))) return st;
+  // the output must be dense row-major with the broadcast shape
+  if (out->ndim != nd)
+    return fail(OXC_ERR_SHAPE_MISMATCH, "shape mismatch: output rank %d vs %d", out->ndim, nd);
+  int64_t total = 1, expect = 1;
+  for (int i = nd - 1; i >= 0; --i) {
+    if (out->shape[i] != shape[i])
+      return fail(OXC_ERR_SHAPE_MISMATCH, "shape mismatch: output dim %d is %lld, expected %lld",
+                  i, (long long)out->shape[i], (long long)shape[i]);
+    if (shape[i] != 1 && out->strides[i] != expect)
+      return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s output must be contiguous", fn);
+    expect *= shape[i];
+  }
+  total = expect;
+  if (total == 0) return OXC_OK;
+  if (!a->data || !out->data || (b && !b->data))
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: null data", fn);
+  Grid g;
+  g.nd = nd;
+  for (int i = 0; i < nd; ++i) g.n[i] = shape[i];
+  bstrides(a, nd, shape, g.st[0]);
+  if (b) bstrides(b, nd, shape, g.st[1]);
+  else for (int i = 0; i < nd; ++i) g.st[1][i] = 0;
+  const int nin = b ? 2 : 1;
+  collapse(&g, nin);
+  Operand oa{a->data, 0.0f, 0}, ob{b ? b->data : nullptr, 0.0f, kind == EK_UNARY ? 1 : 0};
+  if (scalar) {  // one operand is the host scalar argument
+    if (scalar_first) {
+      ob = Operand{a->data, 0.0f, 0};
+      for (int d = 0; d < g.nd; ++d) g.st[1][d] = g.st[0][d];
+      oa = Operand{nullptr, *scalar, 1};
+    } else {
+      ob = Operand{nullptr, *scalar, 1};
+    }
+  }
+  // a tensor operand with all-zero strides is one broadcast value
+  bool zero[2] = {true, true};
+  for (int d = 0; d < g.nd; ++d)
+    for (int k = 0; k < 2; ++k)
+      if (g.st[k][d]) zero[k] = false;
+  if (!oa.scalar && zero[0]) oa.scalar = 1;
+  if (!ob.scalar && zero[1]) ob.scalar = 1;
+  const bool a_dense = oa.scalar || (g.nd == 1 && g.st[0][0] == 1);
+  const bool b_dense = ob.scalar || (g.nd == 1 && g.st[1][0] == 1);
+  const int64_t cap = (int64_t)sm_count() * 8;
+  if (g.nd <= 1 && a_dense && b_dense) {
+    const bool v4 = aligned16(out->data) && (oa.scalar || aligned16(oa.p)) &&
+                    (ob.scalar || aligned16(ob.p));
+    const int64_t work = v4 ? total / 4 : total;
+    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, cap * 4));
+    if (v4) elem_dense_kernel<4><<<grid, 256, 0, s>>>(kind, op, oa, ob, out->data, total);
+    else elem_dense_kernel<1><<<grid, 256, 0, s>>>(kind, op, oa, ob, out->data, total);
+    return check_launch(fn);
+  }
+  int colmajor = 0;
+  if (g.nd == 2) {
+    const Operand* os[2] = {&oa, &ob};
+    for (int k = 0; k < 2; ++k)
+      if (!os[k]->scalar && g.st[k][0] == 1 && g.st[k][1] != 1) colmajor |= 1 << k;
+  }
+  if (colmajor) {
+    const int64_t ntiles = ((g.n[0] + 31) / 32) * ((g.n[1] + 31) / 32);
+    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(ntiles, cap * 2));
+    elem_tiled_kernel<<<grid, 256, 0, s>>>(kind, op, oa, ob, g, colmajor, out->data);
+    return check_launch(fn);
+  }
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, cap * 4));
+  elem_strided_kernel<<<grid, 256, 0, s>>>(kind, op, oa, ob, g, out->data, total);
+  return check_launch(fn);
+}
+
+}  // namespace oxc
+
+using namespace oxc;
+
+extern "C" {
+
+oxc_status oxc_unary(int32_t op, const oxc_view* in, const oxc_view* out, void* stream) {
+  if (op < 0 || op > 18) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: unknown unary op id %d", op);
+  return run_elementwise(EK_UNARY, op, in, nullptr, nullptr, 0, out,
+                         static_cast<cudaStream_t>(stream), "oxc_unary");
+}
+
+oxc_status oxc_binary(int32_t op, const oxc_view* a, const oxc_view* b, const oxc_view* out,
+                      void* stream) {
+  if (op < 0 || op > 6) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: unknown binary op id %d", op);
+  return run_elementwise(EK_BINARY, op, a, b, nullptr, 0, out, static_cast<cudaStream_t>(stream),
+                         "oxc_binary");
+}
+
+oxc_status oxc_cmp(int32_t op, const oxc_view* a, const oxc_view* b, const oxc_view* out,
+                   void* stream) {
+  if (op < 0 || op > 5) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: unknown comparison op id %d", op);
+  return run_elementwise(EK_CMP, op, a, b, nullptr, 0, out, static_cast<cudaStream_t>(stream),
+                         "oxc_cmp");
+}
+
+oxc_status oxc_binary_scalar(int32_t op, const oxc_view* a, float scalar, int32_t scalar_first,
+                             const oxc_view* out, void* stream) {
+  if (op < 0 || op > 6) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: unknown binary op id %d", op);
+  return run_elementwise(EK_BINARY, op, a, a, &scalar, scalar_first, out,
+                         static_cast<cudaStream_t>(stream), "oxc_binary_scalar");
+}
+
+}  // extern "C"

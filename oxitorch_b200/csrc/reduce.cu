@@ -1,0 +1,653 @@
+// reduce.cu -- Tensor::reduce (dim / keepdim) and whole-tensor reductions.
+//
+// Reference: crates/oxi-tensor/src/lib.rs:519-576 (reduce), 582-604 (sum_all,
+// mean_all, norm), ReduceKind::reduce_strip (ops.rs:246-285):
+//   sum   left-to-right f32 fold;           mean = sum / len (f32)
+//   max   fold(-inf, f32::max)  (NaN ignored; all-NaN -> -inf), min likewise
+//   argmax first index of the maximum (`v > best` from data[0]: NaN never wins,
+//          and a NaN at index 0 keeps index 0); argmin likewise
+//   norm  sqrt(sum(v*v))
+// Results are f32; argmax/argmin indices are returned as f32 values, the
+// reference's carrier (lib.rs:568-572).  Empty strips: sum/mean/norm give 0,
+// max/min/arg* are rejected on the host (InvalidArgument), as in the reference.
+//
+// Kernels (HBM-bound):
+//   row:    the reduced dim has stride 1 -- a CTA (long strips) or a warp per
+//           output, 128-bit loads when aligned, fixed-order tree combine;
+//   column: otherwise -- one thread per output, walking the strip in index
+//           order (for sum/mean/norm that is the reference's own left-to-right
+//           fold, bit for bit); threads of a warp own neighbouring outputs so
+//           the loads coalesce; long strips over few outputs are cut into
+//           segments whose partials a finisher combines in segment order;
+//   all:    whole-tensor, two stages with f64 partials for sum/mean/norm.
+#include <math.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace oxc {
+
+enum RKind { RK_SUM = 0, RK_MEAN, RK_MAX, RK_MIN, RK_ARGMAX, RK_ARGMIN, RK_NORM };
+
+// Partial result of a reduction: value (f32 or f64 sum) and index.
+struct RAcc {
+  double s;    // sum / sum of squares (f64 for whole-tensor), or unused
+  float v;     // max/min/arg value; sum for the f32 paths
+  int64_t i;   // arg index; -1 = nothing seen
+};
+
+__device__ __forceinline__ bool better(int kind, float v, int64_t i, float bv, int64_t bi) {
+  if (isnan(v)) return false;
+  if (bi < 0) return true;
+  if (kind == RK_ARGMAX || kind == RK_MAX) return v > bv || (v == bv && i < bi);
+  return v < bv || (v == bv && i < bi);
+}
+
+// ---- row mode ---------------------------------------------------------------------
+
+struct Layout {
+  int nd;                      // non-reduced dims (collapsed)
+  int64_t n[OXC_MAX_DIMS];
+  int64_t st[OXC_MAX_DIMS];
+  int64_t len;                 // strip length
+  int64_t sd;                  // strip stride
+};
+
+__device__ __forceinline__ int64_t base_offset(const Layout& L, int64_t o) {
+  int64_t off = 0;
+  for (int d = L.nd - 1; d >= 0; --d) {
+    const int64_t q = o / L.n[d];
+    off += (o - q * L.n[d]) * L.st[d];
+    o = q;
+  }
+  return off;
+}
+
+__device__ __forceinline__ float finish(int kind, float sum_or_v, int64_t idx, int64_t len) {
+  switch (kind) {
+    case RK_SUM: return sum_or_v;
+    case RK_MEAN: return len ? __fdiv_rn(sum_or_v, (float)len) : 0.0f;
+    case RK_NORM: return __fsqrt_rn(sum_or_v);
+    case RK_ARGMAX: case RK_ARGMIN: return (float)(idx < 0 ? 0 : idx);
+    default: return sum_or_v;
+  }
+}
+
+// One CTA (WARPS = blockDim/32 warps) or one warp per output; strip contiguous.
+template <bool PER_WARP>
+__global__ void __launch_bounds__(256) reduce_row_kernel(int kind, const float* __restrict__ in,
+                                                         Layout L, int64_t nout,
+                                                         float* __restrict__ out) {
+  __shared__ float sv[33];
+  __shared__ long long si[33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int lanes = PER_WARP ? 32 : blockDim.x;
+  const int tid = PER_WARP ? lane : threadIdx.x;
+  const int64_t per_block = PER_WARP ? blockDim.x / 32 : 1;
+  const bool sumlike = kind == RK_SUM || kind == RK_MEAN || kind == RK_NORM;
+  for (int64_t o0 = (int64_t)blockIdx.x * per_block; o0 < nout; o0 += (int64_t)gridDim.x * per_block) {
+    const int64_t o = o0 + (PER_WARP ? warp : 0);
+    float acc = sumlike ? 0.0f : (kind == RK_MAX || kind == RK_ARGMAX ? -INFINITY : INFINITY);
+    int64_t bi = -1;
+    float bv = 0.0f;
+    if (o < nout) {
+      const float* p = in + base_offset(L, o);
+      const bool v4 = L.sd == 1 && (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+      int64_t j0 = 0;
+      if (v4) {
+        const int64_t nv = L.len / 4;
+        for (int64_t v = tid; v < nv; v += lanes) {
+          const float4 q = ld_stream(reinterpret_cast<const float4*>(p) + v);
+          const float e[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float x = e[k];
+            if (kind == RK_NORM) acc = __fadd_rn(acc, __fmul_rn(x, x));
+            else if (sumlike) acc = __fadd_rn(acc, x);
+            else if (kind == RK_MAX) acc = fmaxf(acc, x);
+            else if (kind == RK_MIN) acc = fminf(acc, x);
+            else if (better(kind, x, 4 * v + k, bv, bi)) { bv = x; bi = 4 * v + k; }
+          }
+        }
+        j0 = nv * 4;
+      }
+      for (int64_t j = j0 + tid; j < L.len; j += lanes) {
+        const float x = ld_stream(p + j * L.sd);
+        if (kind == RK_NORM) acc = __fadd_rn(acc, __fmul_rn(x, x));
+        else if (sumlike) acc = __fadd_rn(acc, x);
+        else if (kind == RK_MAX) acc = fmaxf(acc, x);
+        else if (kind == RK_MIN) acc = fminf(acc, x);
+        else if (better(kind, x, j, bv, bi)) { bv = x; bi = j; }
+      }
+    }
+    // warp combine (fixed order)
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float oa = __shfl_xor_sync(0xffffffffu, acc, off);
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const long long oi = __shfl_xor_sync(0xffffffffu, (long long)bi, off);
+      if (sumlike) acc = __fadd_rn(acc, oa);
+      else if (kind == RK_MAX) acc = fmaxf(acc, oa);
+      else if (kind == RK_MIN) acc = fminf(acc, oa);
+      else if (oi >= 0 && better(kind, ov, oi, bv, bi)) { bv = ov; bi = oi; }
+    }
+    if (!PER_WARP) {
+      __syncthreads();
+      if (lane == 0) { sv[warp] = (kind == RK_ARGMAX || kind == RK_ARGMIN) ? bv : acc; si[warp] = bi; }
+      __syncthreads();
+      if (warp == 0) {
+        const int nw = blockDim.x / 32;
+        float a2 = lane < nw ? sv[lane] : (sumlike ? 0.0f : (kind == RK_MAX || kind == RK_ARGMAX ? -INFINITY : INFINITY));
+        long long i2 = lane < nw ? si[lane] : -1;
+        float b2 = a2;
+        if (kind == RK_ARGMAX || kind == RK_ARGMIN) { if (i2 < 0) b2 = 0.0f; }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+          const float oa = __shfl_xor_sync(0xffffffffu, a2, off);
+          const long long oi = __shfl_xor_sync(0xffffffffu, i2, off);
+          if (sumlike) a2 = __fadd_rn(a2, oa);
+          else if (kind == RK_MAX) a2 = fmaxf(a2, oa);
+          else if (kind == RK_MIN) a2 = fminf(a2, oa);
+          else if (oi >= 0 && better(kind, oa, oi, b2, i2)) { b2 = oa; i2 = oi; a2 = oa; }
+        }
+        acc = a2;
+        bi = i2;
+      }
+    }
+    if ((PER_WARP ? lane == 0 : threadIdx.x == 0) && o < nout) {
+      if (kind == RK_ARGMAX || kind == RK_ARGMIN) {
+        // a NaN at index 0 keeps index 0 (the reference starts from data[0])
+        const float first = in[base_offset(L, o)];
+        out[o] = isnan(first) ? 0.0f : finish(kind, 0.0f, bi, L.len);
+      } else {
+        out[o] = finish(kind, acc, -1, L.len);
+      }
+    }
+    if (!PER_WARP) __syncthreads();
+  }
+}
+
+// ---- column mode ------------------------------------------------------------------
+
+// Thread per (output, segment): folds strip elements [seg*seglen, ...) in
+// index order.  nseg == 1 writes the result; else writes partials.
+__global__ void __launch_bounds__(256) reduce_col_kernel(int kind, const float* __restrict__ in,
+                                                         Layout L, int64_t nout, int64_t nseg,
+                                                         int64_t seglen, float* __restrict__ out,
+                                                         float* __restrict__ pv,
+                                                         long long* __restrict__ pi) {
+  const int64_t total = nout * nseg;
+  const bool sumlike = kind == RK_SUM || kind == RK_MEAN || kind == RK_NORM;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t seg = t / nout, o = t - seg * nout;
+    const float* p = in + base_offset(L, o);
+    const int64_t j0 = seg * seglen, j1 = min(L.len, j0 + seglen);
+    float acc = sumlike ? -0.0f : (kind == RK_MAX || kind == RK_ARGMAX ? -INFINITY : INFINITY);
+    float bv = 0.0f;
+    int64_t bi = -1;
+    int64_t j = j0;
+    for (; j + 3 < j1; j += 4) {
+      float x[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) x[k] = __ldg(p + (j + k) * L.sd);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (kind == RK_NORM) acc = __fadd_rn(acc, __fmul_rn(x[k], x[k]));
+        else if (sumlike) acc = __fadd_rn(acc, x[k]);
+        else if (kind == RK_MAX) acc = fmaxf(acc, x[k]);
+        else if (kind == RK_MIN) acc = fminf(acc, x[k]);
+        else if (better(kind, x[k], j + k, bv, bi)) { bv = x[k]; bi = j + k; }
+      }
+    }
+    for (; j < j1; ++j) {
+      const float x = __ldg(p + j * L.sd);
+      if (kind == RK_NORM) acc = __fadd_rn(acc, __fmul_rn(x, x));
+      else if (sumlike) acc = __fadd_rn(acc, x);
+      else if (kind == RK_MAX) acc = fmaxf(acc, x);
+      else if (kind == RK_MIN) acc = fminf(acc, x);
+      else if (better(kind, x, j, bv, bi)) { bv = x; bi = j; }
+    }
+    if (nseg == 1) {
+      if (kind == RK_ARGMAX || kind == RK_ARGMIN)
+        out[o] = (L.len > 0 && isnan(p[0])) ? 0.0f : finish(kind, 0.0f, bi, L.len);
+      else
+        out[o] = finish(kind, acc, -1, L.len);
+    } else {
+      pv[t] = (kind == RK_ARGMAX || kind == RK_ARGMIN) ? bv : acc;
+      pi[t] = bi;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) reduce_col_finish_kernel(int kind, const float* __restrict__ in,
+                                                                Layout L, int64_t nout, int64_t nseg,
+                                                                const float* __restrict__ pv,
+                                                                const long long* __restrict__ pi,
+                                                                float* __restrict__ out) {
+  const bool sumlike = kind == RK_SUM || kind == RK_MEAN || kind == RK_NORM;
+  for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < nout;
+       o += (int64_t)gridDim.x * blockDim.x) {
+    float acc = sumlike ? -0.0f : (kind == RK_MAX || kind == RK_ARGMAX ? -INFINITY : INFINITY);
+    float bv = 0.0f;
+    int64_t bi = -1;
+    for (int64_t seg = 0; seg < nseg; ++seg) {
+      const float v = pv[seg * nout + o];
+      const int64_t i = pi[seg * nout + o];
+      if (sumlike) acc = __fadd_rn(acc, v);
+      else if (kind == RK_MAX) acc = fmaxf(acc, v);
+      else if (kind == RK_MIN) acc = fminf(acc, v);
+      else if (i >= 0 && better(kind, v, i, bv, bi)) { bv = v; bi = i; }
+    }
+    if (kind == RK_ARGMAX || kind == RK_ARGMIN)
+      out[o] = (L.len > 0 && isnan(in[base_offset(L, o)])) ? 0.0f : finish(kind, 0.0f, bi, L.len);
+    else
+      out[o] = finish(kind, acc, -1, L.len);
+  }
+}
+
+// ---- whole tensor ------------------------------------------------------------------
+
+struct Flat {
+  int nd;
+  int64_t n[OXC_MAX_DIMS];
+  int64_t st[OXC_MAX_DIMS];
+};
+
+__device__ __forceinline__ int64_t flat_offset(const Flat& f, int64_t i) {
+  int64_t off = 0;
+  for (int d = f.nd - 1; d >= 0; --d) {
+    const int64_t q = i / f.n[d];
+    off += (i - q * f.n[d]) * f.st[d];
+    i = q;
+  }
+  return off;
+}
+
+// Stage 1: CTA b reduces logical indices [b*chunk, ...) into part[b].
+__global__ void __launch_bounds__(256) reduce_all_stage1(int kind, const float* __restrict__ in,
+                                                         Flat f, int64_t n, int64_t chunk,
+                                                         double* __restrict__ ps,
+                                                         float* __restrict__ pv,
+                                                         long long* __restrict__ pi) {
+  __shared__ double sd[33];
+  __shared__ float sv[33];
+  __shared__ long long si[33];
+  const int64_t i0 = (int64_t)blockIdx.x * chunk, i1 = min(n, i0 + chunk);
+  const bool dense = f.nd == 1 && f.st[0] == 1;
+  const bool sumlike = kind == RK_SUM || kind == RK_MEAN || kind == RK_NORM;
+  double acc = 0.0;
+  float bv = (kind == RK_MAX || kind == RK_ARGMAX) ? -INFINITY : INFINITY;
+  int64_t bi = -1;
+  for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    const float x = dense ? ld_stream(in + i) : __ldg(in + flat_offset(f, i));
+    if (kind == RK_NORM) acc += (double)x * (double)x;
+    else if (sumlike) acc += (double)x;
+    else if (kind == RK_MAX) bv = fmaxf(bv, x);
+    else if (kind == RK_MIN) bv = fminf(bv, x);
+    else if (better(kind, x, i, bv, bi)) { bv = x; bi = i; }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const double oa = __shfl_xor_sync(0xffffffffu, acc, off);
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+    const long long oi = __shfl_xor_sync(0xffffffffu, (long long)bi, off);
+    acc += oa;
+    if (kind == RK_MAX) bv = fmaxf(bv, ov);
+    else if (kind == RK_MIN) bv = fminf(bv, ov);
+    else if ((kind == RK_ARGMAX || kind == RK_ARGMIN) && oi >= 0 && better(kind, ov, oi, bv, bi)) { bv = ov; bi = oi; }
+  }
+  if (lane == 0) { sd[warp] = acc; sv[warp] = bv; si[warp] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double a = 0.0;
+    float v = (kind == RK_MAX || kind == RK_ARGMAX) ? -INFINITY : INFINITY;
+    long long b = -1;
+    for (int w = 0; w < (int)(blockDim.x / 32); ++w) {
+      a += sd[w];
+      if (kind == RK_MAX) v = fmaxf(v, sv[w]);
+      else if (kind == RK_MIN) v = fminf(v, sv[w]);
+      else if ((kind == RK_ARGMAX || kind == RK_ARGMIN) && si[w] >= 0 && better(kind, sv[w], si[w], v, b)) { v = sv[w]; b = si[w]; }
+    }
+    ps[blockIdx.x] = a;
+    pv[blockIdx.x] = v;
+    pi[blockIdx.x] = b;
+  }
+}
+
+__global__ void reduce_all_stage2(int kind, const float* __restrict__ in, Flat f, int64_t n,
+                                  int64_t nparts, const double* __restrict__ ps,
+                                  const float* __restrict__ pv, const long long* __restrict__ pi,
+                                  float* __restrict__ out, double* __restrict__ out64) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  double a = 0.0;
+  float v = (kind == RK_MAX || kind == RK_ARGMAX) ? -INFINITY : INFINITY;
+  long long b = -1;
+  for (int64_t p = 0; p < nparts; ++p) {
+    a += ps[p];
+    if (kind == RK_MAX) v = fmaxf(v, pv[p]);
+    else if (kind == RK_MIN) v = fminf(v, pv[p]);
+    else if ((kind == RK_ARGMAX || kind == RK_ARGMIN) && pi[p] >= 0 && better(kind, pv[p], pi[p], v, b)) { v = pv[p]; b = pi[p]; }
+  }
+  double r64 = a;
+  float r;
+  switch (kind) {
+    case RK_SUM: r = (float)a; break;
+    case RK_MEAN: r64 = n ? a / (double)n : 0.0; r = n ? __fdiv_rn((float)a, (float)n) : 0.0f; break;
+    case RK_NORM: r64 = sqrt(a); r = __fsqrt_rn((float)a); break;
+    case RK_ARGMAX: case RK_ARGMIN:
+      r = (n > 0 && isnan(in[flat_offset(f, 0)])) ? 0.0f : (float)(b < 0 ? 0 : b);
+      r64 = r;
+      break;
+    default: r = v; r64 = v; break;
+  }
+  out[0] = r;
+  if (out64) out64[0] = r64;
+}
+
+// Sum of squares over several tensors (clip_grad_norm_): stage 1 per chunk of
+// each tensor, stage 2 in (tensor, chunk) order.
+struct MultiViews {
+  int count;
+  const float* p[16];
+  Flat f[16];
+  int64_t n[16];
+  int64_t first_part[17];
+  int64_t chunk;
+};
+
+__global__ void __launch_bounds__(256) sumsq_multi_stage1(MultiViews mv, double* __restrict__ ps) {
+  __shared__ double sd[33];
+  const int64_t part = blockIdx.x;
+  int t = 0;
+  while (t + 1 < mv.count && part >= mv.first_part[t + 1]) ++t;
+  const int64_t i0 = (part - mv.first_part[t]) * mv.chunk, i1 = min(mv.n[t], i0 + mv.chunk);
+  const bool dense = mv.f[t].nd == 1 && mv.f[t].st[0] == 1;
+  double acc = 0.0;
+  for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    const float x = dense ? ld_stream(mv.p[t] + i) : __ldg(mv.p[t] + flat_offset(mv.f[t], i));
+    acc += (double)x * (double)x;
+  }
+  const double s = block_sum(acc, sd);
+  if (threadIdx.x == 0) ps[part] = s;
+}
+
+__global__ void sumsq_multi_stage2(int64_t nparts, const double* __restrict__ ps, double* __restrict__ out) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  double a = 0.0;
+  for (int64_t p = 0; p < nparts; ++p) a += ps[p];
+  out[0] = a;
+}
+
+// ---- host helpers --------------------------------------------------------------------
+
+static oxc_status check_view(const oxc_view* v, const char* fn) {
+  if (!v) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: null view", fn);
+  if (v->ndim < 0 || v->ndim > OXC_MAX_DIMS)
+    return fail(OXC_ERR_NOT_IMPLEMENTED, "not implemented: %s: rank %d", fn, v->ndim);
+  for (int i = 0; i < v->ndim; ++i)
+    if (v->shape[i] < 0) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: negative dim", fn);
+  return OXC_OK;
+}
+
+static Flat make_flat(const oxc_view* v, int64_t* n) {
+  Flat f;
+  f.nd = 0;
+  *n = 1;
+  for (int i = 0; i < v->ndim; ++i) *n *= v->shape[i];
+  for (int i = 0; i < v->ndim; ++i) {
+    if (v->shape[i] == 1) continue;
+    if (f.nd > 0 && f.st[f.nd - 1] == v->strides[i] * v->shape[i]) {
+      f.n[f.nd - 1] *= v->shape[i];
+      f.st[f.nd - 1] = v->strides[i];
+    } else {
+      f.n[f.nd] = v->shape[i];
+      f.st[f.nd] = v->strides[i];
+      ++f.nd;
+    }
+  }
+  if (f.nd == 0) { f.nd = 1; f.n[0] = 1; f.st[0] = 1; }
+  return f;
+}
+
+struct ReducePlan {
+  Layout L;
+  int64_t nout;
+  bool row;
+  int64_t nseg, seglen;
+};
+
+static oxc_status plan_reduce(int32_t kind, const oxc_view* in, int64_t dim, int32_t keepdim,
+                              const oxc_view* out, ReducePlan* P) {
+  oxc_status st = check_view(in, "reduce");
+  if (st) return st;
+  const int nd = in->ndim;
+  // layout::normalize_dim (layout.rs:162-179)
+  int64_t d = dim < 0 ? nd + dim : dim;
+  if (d < 0 || d >= nd)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: dim %lld out of range for %d-D tensor",
+                (long long)dim, nd);
+  const int64_t len = in->shape[d];
+  if (len == 0 && (kind == RK_ARGMAX || kind == RK_ARGMIN))
+    return fail(OXC_ERR_INVALID_ARGUMENT,
+                "invalid argument: cannot compute argmax/argmin over a zero-length dim");
+  if (len == 0 && (kind == RK_MAX || kind == RK_MIN))
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: cannot compute max/min over a zero-length dim");
+  // expected output shape, dense row-major
+  if ((st = check_view(out, "reduce output"))) return st;
+  int64_t eshape[OXC_MAX_DIMS];
+  int end = 0;
+  for (int i = 0; i < nd; ++i) {
+    if (i == d) { if (keepdim) eshape[end++] = 1; continue; }
+    eshape[end++] = in->shape[i];
+  }
+  if (out->ndim != end)
+    return fail(OXC_ERR_SHAPE_MISMATCH, "shape mismatch: reduce output rank %d vs %d", out->ndim, end);
+  int64_t expect = 1;
+  for (int i = end - 1; i >= 0; --i) {
+    if (out->shape[i] != eshape[i])
+      return fail(OXC_ERR_SHAPE_MISMATCH, "shape mismatch: reduce output dim %d", i);
+    if (eshape[i] != 1 && out->strides[i] != expect)
+      return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: reduce output must be contiguous");
+    expect *= eshape[i];
+  }
+  P->nout = expect;
+  // non-reduced dims, collapsed
+  Layout& L = P->L;
+  L.nd = 0;
+  for (int i = 0; i < nd; ++i) {
+    if (i == d || in->shape[i] == 1) continue;
+    if (L.nd > 0 && L.st[L.nd - 1] == in->strides[i] * in->shape[i]) {
+      L.n[L.nd - 1] *= in->shape[i];
+      L.st[L.nd - 1] = in->strides[i];
+    } else {
+      L.n[L.nd] = in->shape[i];
+      L.st[L.nd] = in->strides[i];
+      ++L.nd;
+    }
+  }
+  if (L.nd == 0) { L.nd = 1; L.n[0] = 1; L.st[0] = 0; }
+  L.len = len;
+  L.sd = in->strides[d];
+  // row mode when the strip is contiguous or outputs are not contiguous in memory
+  const bool inner_unit = L.st[L.nd - 1] == 1 && L.n[L.nd - 1] > 1;
+  P->row = L.sd == 1 || !inner_unit;
+  P->nseg = 1;
+  P->seglen = len;
+  if (!P->row) {
+    const int64_t want = 64 * 1024;  // threads to keep HBM busy
+    if (P->nout < want && len > 512) {
+      int64_t nseg = std::min<int64_t>((want + P->nout - 1) / P->nout, (len + 255) / 256);
+      nseg = std::max<int64_t>(nseg, 1);
+      P->nseg = nseg;
+      P->seglen = (len + nseg - 1) / nseg;
+      P->nseg = (len + P->seglen - 1) / P->seglen;
+    }
+  }
+  return OXC_OK;
+}
+
+}  // namespace oxc
+
+using namespace oxc;
+
+extern "C" {
+
+size_t oxc_reduce_workspace_size(int32_t kind, const oxc_view* in, int64_t dim) {
+  if (!in || in->ndim <= 0) return 0;
+  // plan against a fake keepdim output
+  oxc_view out;
+  out.data = nullptr;
+  out.ndim = in->ndim;
+  int64_t d = dim < 0 ? in->ndim + dim : dim;
+  if (d < 0 || d >= in->ndim) return 0;
+  int64_t expect = 1;
+  for (int i = in->ndim - 1; i >= 0; --i) {
+    out.shape[i] = i == d ? 1 : in->shape[i];
+    out.strides[i] = expect;
+    expect *= out.shape[i];
+  }
+  ReducePlan P;
+  if (plan_reduce(kind, in, dim, 1, &out, &P) != OXC_OK) { clear_error(); return 0; }
+  if (P.row || P.nseg == 1) return 0;
+  return (size_t)P.nseg * P.nout * (sizeof(float) + sizeof(long long)) + 256;
+}
+
+oxc_status oxc_reduce(int32_t kind, const oxc_view* in, int64_t dim, int32_t keepdim,
+                      const oxc_view* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (kind < 0 || kind > 6)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: unknown reduction kind %d", kind);
+  ReducePlan P;
+  oxc_status st = plan_reduce(kind, in, dim, keepdim, out, &P);
+  if (st) return st;
+  if (P.nout == 0) return OXC_OK;
+  if (!out->data || (P.L.len > 0 && !in->data))
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: reduce: null data");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t cap = (int64_t)sm_count() * 16;
+  if (P.L.len == 0) {  // empty strips: sum/mean/norm -> 0
+    cudaError_t e = cudaMemsetAsync(out->data, 0, (size_t)P.nout * sizeof(float), s);
+    return e == cudaSuccess ? OXC_OK : cuda_fail(e, "oxc_reduce");
+  }
+  if (P.row) {
+    if (P.L.len >= 2048) {
+      reduce_row_kernel<false><<<(unsigned)std::min<int64_t>(P.nout, cap), 256, 0, s>>>(
+          kind, in->data, P.L, P.nout, out->data);
+    } else {
+      const int64_t blocks = (P.nout + 7) / 8;
+      reduce_row_kernel<true><<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(blocks, cap)), 256, 0, s>>>(
+          kind, in->data, P.L, P.nout, out->data);
+    }
+    return check_launch("oxc_reduce");
+  }
+  const int64_t total = P.nout * P.nseg;
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, cap));
+  if (P.nseg == 1) {
+    reduce_col_kernel<<<grid, 256, 0, s>>>(kind, in->data, P.L, P.nout, 1, P.seglen, out->data,
+                                           nullptr, nullptr);
+    return check_launch("oxc_reduce");
+  }
+  const size_t need = (size_t)P.nseg * P.nout * (sizeof(float) + sizeof(long long)) + 256;
+  if (!workspace || workspace_bytes < need)
+    return fail(OXC_ERR_INVALID_ARGUMENT,
+                "invalid argument: reduce needs a %zu-byte workspace (oxc_reduce_workspace_size), got %zu",
+                need, workspace_bytes);
+  long long* pi = reinterpret_cast<long long*>((reinterpret_cast<uintptr_t>(workspace) + 15) & ~uintptr_t(15));
+  float* pv = reinterpret_cast<float*>(pi + total);
+  reduce_col_kernel<<<grid, 256, 0, s>>>(kind, in->data, P.L, P.nout, P.nseg, P.seglen, out->data, pv, pi);
+  st = check_launch("oxc_reduce");
+  if (st) return st;
+  const unsigned g2 = (unsigned)std::max<int64_t>(1, std::min<int64_t>((P.nout + 255) / 256, cap));
+  reduce_col_finish_kernel<<<g2, 256, 0, s>>>(kind, in->data, P.L, P.nout, P.nseg, pv, pi, out->data);
+  return check_launch("oxc_reduce (finish)");
+}
+
+static int64_t all_parts(int64_t n, int64_t* chunk) {
+  const int64_t cap = (int64_t)sm_count() * 4;
+  int64_t parts = std::max<int64_t>(1, std::min<int64_t>(cap, (n + 8191) / 8192));
+  *chunk = (n + parts - 1) / parts;
+  parts = std::max<int64_t>(1, (n + *chunk - 1) / *chunk);
+  return parts;
+}
+
+size_t oxc_reduce_all_workspace_size(int64_t numel) {
+  int64_t chunk;
+  const int64_t parts = all_parts(std::max<int64_t>(numel, 1), &chunk);
+  return (size_t)parts * (sizeof(double) + sizeof(float) + sizeof(long long)) + 256;
+}
+
+oxc_status oxc_reduce_all(int32_t kind, const oxc_view* in, float* out, double* out_f64,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  if (kind < 0 || kind > 6)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: unknown reduction kind %d", kind);
+  oxc_status st = check_view(in, "reduce_all");
+  if (st) return st;
+  int64_t n;
+  Flat f = make_flat(in, &n);
+  if (n == 0 && kind != RK_SUM && kind != RK_MEAN && kind != RK_NORM)
+    return fail(OXC_ERR_INVALID_ARGUMENT,
+                "invalid argument: cannot compute min/max/argmax/argmin over an empty reduction");
+  if (!out) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: reduce_all: null output");
+  int64_t chunk;
+  const int64_t parts = all_parts(std::max<int64_t>(n, 1), &chunk);
+  const size_t need = oxc_reduce_all_workspace_size(n);
+  if (!workspace || workspace_bytes < need)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: reduce_all needs a %zu-byte workspace, got %zu",
+                need, workspace_bytes);
+  double* ps = reinterpret_cast<double*>((reinterpret_cast<uintptr_t>(workspace) + 15) & ~uintptr_t(15));
+  long long* pi = reinterpret_cast<long long*>(ps + parts);
+  float* pv = reinterpret_cast<float*>(pi + parts);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  reduce_all_stage1<<<(unsigned)parts, 256, 0, s>>>(kind, in->data, f, n, chunk, ps, pv, pi);
+  st = check_launch("oxc_reduce_all");
+  if (st) return st;
+  reduce_all_stage2<<<1, 32, 0, s>>>(kind, in->data, f, n, n ? parts : 0, ps, pv, pi, out, out_f64);
+  return check_launch("oxc_reduce_all (finish)");
+}
+
+size_t oxc_sum_squares_workspace_size(const oxc_view* views, int32_t count) {
+  if (!views || count <= 0 || count > 16) return 0;
+  int64_t parts = 0;
+  for (int i = 0; i < count; ++i) {
+    int64_t n = 1;
+    for (int d = 0; d < views[i].ndim; ++d) n *= views[i].shape[d];
+    parts += (n + (1 << 20) - 1) >> 20;
+  }
+  return (size_t)std::max<int64_t>(parts, 1) * sizeof(double) + 256;
+}
+
+oxc_status oxc_sum_squares(const oxc_view* views, int32_t count, double* out, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  if (!views || count <= 0 || count > 16)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: sum_squares takes 1..16 tensors, got %d", count);
+  if (!out) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: sum_squares: null output");
+  MultiViews mv;
+  mv.count = count;
+  mv.chunk = 1 << 20;
+  mv.first_part[0] = 0;
+  for (int i = 0; i < count; ++i) {
+    oxc_status st = check_view(&views[i], "sum_squares");
+    if (st) return st;
+    mv.p[i] = views[i].data;
+    mv.f[i] = make_flat(&views[i], &mv.n[i]);
+    mv.first_part[i + 1] = mv.first_part[i] + (mv.n[i] + mv.chunk - 1) / mv.chunk;
+  }
+  const size_t need = oxc_sum_squares_workspace_size(views, count);
+  if (!workspace || workspace_bytes < need)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: sum_squares needs a %zu-byte workspace, got %zu",
+                need, workspace_bytes);
+  double* ps = reinterpret_cast<double*>((reinterpret_cast<uintptr_t>(workspace) + 15) & ~uintptr_t(15));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t parts = mv.first_part[count];
+  if (parts > 0) {
+    sumsq_multi_stage1<<<(unsigned)parts, 256, 0, s>>>(mv, ps);
+    oxc_status st = check_launch("oxc_sum_squares");
+    if (st) return st;
+  }
+  sumsq_multi_stage2<<<1, 32, 0, s>>>(parts, ps, out);
+  return check_launch("oxc_sum_squares (finish)");
+}
+
+}  // extern "C"
