@@ -197,6 +197,22 @@ oxc_status oxc_cross_entropy_bwd(const float* logits, const int64_t* targets,
                                  const float* grad_loss, float* dlogits, int64_t rows,
                                  int64_t cols, int64_t total_rows, void* stream);
 
+/* ---- SiLU / SwiGLU: F.silu(g) [* u] ----------------------------------------
+ * (python/oxitorch/nn/functional.py:202-204; sigmoid ops.rs:176).  gate and up
+ * are 2-D views [rows, cols] with any strides (a transposed gate is read
+ * along its contiguous dim); up == NULL computes F.silu(gate).  h, dgate, dup
+ * are dense [rows, cols].  Forward optionally writes the dim-1 reductions of
+ * h (row_sum, row_max, row_argmax as float indices; each may be NULL) with the
+ * reference's f32::max / first-occurrence rules.  Backward optionally writes
+ * sum(dgate^2) + sum(dup^2) in f64 to the device scalar `sumsq` (needs the
+ * workspace oxc_swiglu_bwd_workspace_size reports). */
+oxc_status oxc_swiglu_fwd(const oxc_view* gate, const oxc_view* up, float* h, float* row_sum,
+                          float* row_max, float* row_argmax, void* stream);
+size_t oxc_swiglu_bwd_workspace_size(int64_t rows, int64_t cols);
+oxc_status oxc_swiglu_bwd(const oxc_view* gate, const oxc_view* up, const oxc_view* dh,
+                          float* dgate, float* dup, double* sumsq, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
 /* ---- embedding: F.embedding = weight.index_select(0, ids) and its VJP -------
  * (python/oxitorch/nn/functional.py:245-247; crates/oxi-tensor/src/lib.rs:665-703;
  * VJP crates/oxi-autograd/src/ops.rs:741-769).  ids int64 [n] (negative ids

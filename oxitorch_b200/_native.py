@@ -85,6 +85,9 @@ SIGNATURES = {
     "oxc_softmax_bwd": (_I32, [_P, _P, _P, _I64, _I64, _I32, _P]),
     "oxc_cross_entropy_fwd": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P]),
     "oxc_cross_entropy_bwd": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
+    "oxc_swiglu_fwd": (_I32, [_VP, _VP, _P, _P, _P, _P, _P]),
+    "oxc_swiglu_bwd_workspace_size": (_SZ, [_I64, _I64]),
+    "oxc_swiglu_bwd": (_I32, [_VP, _VP, _VP, _P, _P, _P, _P, _SZ, _P]),
     "oxc_embedding_fwd": (_I32, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P]),
     "oxc_embedding_bwd_workspace_size": (_SZ, [_I64, _I64, _I64]),
     "oxc_embedding_bwd": (_I32, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _SZ, _P]),

@@ -18,6 +18,8 @@ from __future__ import annotations
 
 import torch
 
+import ctypes
+
 from . import _native as N
 
 _MODES = {"ref": N.GRAD_REF, "exact": N.GRAD_EXACT}
@@ -373,3 +375,87 @@ def embedding(indices, weight):
     _require_cuda_f32("weight", weight)
     ids = _ids_tensor(indices, weight.shape[0], weight.device)
     return _Embedding.apply(ids, weight)
+
+
+# ---- SiLU / SwiGLU -----------------------------------------------------------------------
+
+def _as2d(name, t):
+    _require_cuda_f32(name, t)
+    if t.dim() == 1:
+        return t.reshape(1, -1)
+    if t.dim() != 2:
+        t = t.reshape(-1, t.shape[-1])
+    return t
+
+
+def swiglu_fwd(gate, up=None, row_stats=False):
+    """h = silu(gate) * up (silu(gate) if up is None) for 2-D views of any
+    strides; with row_stats also the dim-1 sum, max and argmax of h."""
+    g = _as2d("gate", gate)
+    u = None if up is None else _as2d("up", up)
+    R, C = g.shape
+    h = torch.empty(R, C, dtype=torch.float32, device=g.device)
+    stats = [torch.empty(R, dtype=torch.float32, device=g.device) for _ in range(3)] if row_stats else [None] * 3
+    N.check(N.load().oxc_swiglu_fwd(ctypes.byref(N.make_view(g)),
+                                    None if u is None else ctypes.byref(N.make_view(u)),
+                                    h.data_ptr(), *[None if t is None else t.data_ptr() for t in stats],
+                                    _stream()), "swiglu")
+    return (h, *stats) if row_stats else h
+
+
+def swiglu_bwd(gate, up, dh, sumsq=False):
+    """(dgate, dup[, sum of squares of both as a 0-d f64 tensor])."""
+    g = _as2d("gate", gate)
+    u = None if up is None else _as2d("up", up)
+    d = _as2d("dh", dh)
+    R, C = g.shape
+    dg = torch.empty(R, C, dtype=torch.float32, device=g.device)
+    du = None if u is None else torch.empty(R, C, dtype=torch.float32, device=g.device)
+    L = N.load()
+    sq = torch.empty((), dtype=torch.float64, device=g.device) if sumsq else None
+    ws = _workspace(L.oxc_swiglu_bwd_workspace_size(R, C) if sumsq else 0, g.device)
+    N.check(L.oxc_swiglu_bwd(ctypes.byref(N.make_view(g)),
+                             None if u is None else ctypes.byref(N.make_view(u)),
+                             ctypes.byref(N.make_view(d)), dg.data_ptr(),
+                             None if du is None else du.data_ptr(),
+                             None if sq is None else sq.data_ptr(), ws.data_ptr(), ws.numel(),
+                             _stream()), "swiglu backward")
+    return (dg, du, sq) if sumsq else (dg, du)
+
+
+class _SwiGLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, gate, up):
+        ctx.save_for_backward(gate, up)
+        ctx.shape = gate.shape
+        h = swiglu_fwd(gate, up)
+        return h.reshape(gate.shape)
+
+    @staticmethod
+    def backward(ctx, dh):
+        gate, up = ctx.saved_tensors
+        dg, du = swiglu_bwd(gate, up, dh)
+        return dg.reshape(ctx.shape), du.reshape(ctx.shape)
+
+
+class _SiLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x):
+        ctx.save_for_backward(x)
+        return swiglu_fwd(x).reshape(x.shape)
+
+    @staticmethod
+    def backward(ctx, dy):
+        (x,) = ctx.saved_tensors
+        dg, _ = swiglu_bwd(x, None, dy)
+        return dg.reshape(x.shape)
+
+
+def silu(x):
+    """F.silu (functional.py:202-204): x * sigmoid(x)."""
+    return _SiLU.apply(x)
+
+
+def swiglu(gate, up):
+    """silu(gate) * up, the decoder-MLP gate (composed by callers of F.silu)."""
+    return _SwiGLU.apply(gate, up)
