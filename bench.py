@@ -1,24 +1,32 @@
 """Benchmark of the memory-bound layer path on B200.
 
-Workload (the configuration the headline metric is quoted
-on): LayerNorm (affine, eps 1e-5) followed by the reference's tanh-GELU,
+Default workload (the configuration the headline metric is quoted on, BASELINE
+config 2): LayerNorm (affine, eps 1e-5) followed by the reference's tanh-GELU,
 forward + backward, fp32, x [16384, 4096] ~ N(0,1), weight ~ U(0.5,1.5),
 bias ~ N(0,0.1), upstream grad ~ N(0,1).  One step = the fused forward kernel
 + the fused VJP kernel (+ its dweight/dbias finisher); with N GPUs each rank
 owns its own 16384 rows (weak scaling, row sharding) and the step ends with
 the data-parallel exchange of the [4096] dweight/dbias partials (NCCL
-all-reduce).  Inputs are larger than L2 (268 MB per tensor vs 126 MB), so no
-flush is needed between steps.
+all-reduce).
 
-`value` is whole-job algorithmic GB/s: sum over ranks of the bytes each
-kernel must move (each input read once, each output written once) divided by
-the max over ranks of the device-timed step time.  `e2e` is the same metric
-through the C ABI with host buffers: pinned host -> device copies of x and dy
-and device -> host copies of y, dx, dweight and dbias inside the timed region.
+`--workload` measures the other BASELINE configs the same way (they are the
+parity configs; the headline line is config 2):
+  rms        config 1: RMSNorm fwd+VJP, x [4096, 4096] (fits L2: flushed)
+  ce         config 3: cross-entropy fwd+VJP, logits [32768, 32000]
+  embedding  config 4: gather + duplicate-id VJP, table [32000, 4096],
+             ids [64, 2048] Zipf(1.1) clipped
+  mlp_block  config 5: RMSNorm + SwiGLU (transposed gate view) + dim-1
+             sum/max/argmax + whole-tensor L2 of {dx, dg, du}, 65536 tokens
+
+`value` is whole-job algorithmic GB/s: sum over ranks of the bytes each kernel
+must move (each input read once, each output written once) divided by the max
+over ranks of the device-timed step time.  `e2e` is the same metric through
+the C ABI with host buffers: pinned host -> device copies of the step's inputs
+and device -> host copies of its outputs inside the timed region.
 
 `--impl reference` times the reference algorithm on the host cores instead:
 the oracle port of oxitorch's CPU path (the Rust reference cannot be built on
-this image), on a bounded row sample of the same workload.
+this image), on bounded samples of the same workload.
 """
 
 from __future__ import annotations
@@ -35,23 +43,8 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-ROWS, COLS = 16384, 4096
-EPS = 1e-5
 F32 = 4
-# Algorithmic bytes per row: fwd reads x, writes y (+ mean, rstd);
-# VJP reads x, dy (+ mean, rstd), writes dx.  Parameters: w, b read by both,
-# dw, db written by the VJP.
-FWD_BYTES_ROW = 2 * COLS * F32 + 2 * F32
-BWD_BYTES_ROW = 3 * COLS * F32 + 2 * F32
-PARAM_BYTES_FWD = 2 * COLS * F32
-PARAM_BYTES_BWD = 4 * COLS * F32
 METRIC = "HBM GB/s & % of B200 peak, norm/softmax/CE/embed fwd+bwd at 1/2/4/8 GPUs"
-
-
-def algorithmic_bytes(rows):
-    fwd = rows * FWD_BYTES_ROW + PARAM_BYTES_FWD
-    bwd = rows * BWD_BYTES_ROW + PARAM_BYTES_BWD
-    return fwd, bwd
 
 
 def measured_peak():
@@ -119,159 +112,509 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": n}
 
 
-# ---- CPU reference (oracle port) -------------------------------------------------------
+# ---- CPU reference samples (oracle port) ------------------------------------------------
 
-def _oracle_step(rows, seed):
-    """One fwd+bwd of the composed reference path on `rows` rows; returns seconds."""
+def cpu_sample(workload, seed):
+    """One bounded sample of `workload` through the oracle port of the
+    reference CPU path; returns (seconds, algorithmic bytes of the sample)."""
     import numpy as np
     from oracle import oxiref as R
     rng = np.random.default_rng(seed)
-    x = rng.standard_normal((rows, COLS), dtype=np.float32)
-    w = rng.uniform(0.5, 1.5, COLS).astype(np.float32)
-    b = (rng.standard_normal(COLS, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
-    dy = rng.standard_normal((rows, COLS), dtype=np.float32)
-    t0 = time.perf_counter()
-    xt, wt, bt = R.from_numpy(x, True), R.from_numpy(w, True), R.from_numpy(b, True)
-    y = R.gelu(R.layer_norm(xt, wt, bt, EPS))
-    y.backward(dy)
-    return time.perf_counter() - t0
+    if workload in ("ln_gelu", "rms"):
+        rows, cols = 64, 4096
+        x = rng.standard_normal((rows, cols), dtype=np.float32)
+        w = rng.uniform(0.5, 1.5, cols).astype(np.float32)
+        b = (rng.standard_normal(cols, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
+        dy = rng.standard_normal((rows, cols), dtype=np.float32)
+        t0 = time.perf_counter()
+        xt, wt = R.from_numpy(x, True), R.from_numpy(w, True)
+        if workload == "rms":
+            y = R.rms_norm(xt, wt, 1e-6)
+            nbytes = rows * (20 * cols + 8) + 12 * cols
+        else:
+            y = R.gelu(R.layer_norm(xt, wt, R.from_numpy(b, True), 1e-5))
+            nbytes = rows * (20 * cols + 16) + 24 * cols
+        y.backward(dy)
+        return time.perf_counter() - t0, nbytes
+    if workload == "ce":
+        rows, cols = 8, 32000
+        x = (rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(2)).astype(np.float32)
+        x[rng.random((rows, cols)) < 0.01] = 20.0
+        t = [int(v) for v in rng.integers(0, cols, rows)]
+        t0 = time.perf_counter()
+        xt = R.from_numpy(x, True)
+        R.cross_entropy(xt, t).backward()
+        return time.perf_counter() - t0, rows * cols * 12 + rows * 16
+    if workload == "embedding":
+        v, d, n = 32000, 4096, 512
+        table = rng.standard_normal((v, d), dtype=np.float32)
+        ids = np.minimum(rng.zipf(1.1, n) - 1, v - 1).astype(np.int64)
+        dout = rng.standard_normal((n, d), dtype=np.float32)
+        t0 = time.perf_counter()
+        tt = R.from_numpy(table, True)
+        out = R.embedding([int(i) for i in ids], tt)
+        out.backward(dout)
+        return time.perf_counter() - t0, n * 8 * 2 + n * d * 4 * 3 + v * d * 4
+    if workload == "mlp_block":
+        m, dmod, hid = 16, 4096, 11008
+        x = rng.standard_normal((m, dmod), dtype=np.float32)
+        w = rng.uniform(0.5, 1.5, dmod).astype(np.float32)
+        g = rng.standard_normal((m, hid), dtype=np.float32)
+        u = rng.standard_normal((m, hid), dtype=np.float32)
+        dy = rng.standard_normal((m, dmod), dtype=np.float32)
+        dh = rng.standard_normal((m, hid), dtype=np.float32)
+        t0 = time.perf_counter()
+        xt, wt = R.from_numpy(x, True), R.from_numpy(w, True)
+        R.rms_norm(xt, wt, 1e-6).backward(dy)
+        gt, ut = R.from_numpy(g, True), R.from_numpy(u, True)
+        h = R.silu(gt) * ut
+        hv = h.numpy()
+        R.t_reduce("sum", hv, 1, False), R.t_reduce("max", hv, 1, False), R.t_reduce("argmax", hv, 1, False)
+        h.backward(dh)
+        for grad in (xt.grad.numpy(), gt.grad.numpy(), ut.grad.numpy()):
+            R.sumsq_all_f64(grad)
+        return time.perf_counter() - t0, m * (20 * dmod + 32 * hid) + 12 * dmod
+    raise ValueError(workload)
 
 
-def cpu_baseline(budget_s=10.0, rows=128):
-    """Single-threaded oracle port on repeated `rows`-row samples for ~budget_s."""
-    _oracle_step(8, 0)  # build/load the C oracle, warm caches
-    total, reps = 0.0, 0
+def cpu_baseline(workload, budget_s=10.0):
+    """Single-threaded oracle port on repeated samples for ~budget_s."""
+    cpu_sample(workload, 0)  # build/load the C oracle, warm caches
+    total, nbytes, reps = 0.0, 0, 0
     while total < budget_s or reps < 1:
-        total += _oracle_step(rows, 2 + reps)
+        dt, b = cpu_sample(workload, 1 + reps)
+        total += dt
+        nbytes += b
         reps += 1
-    fwd, bwd = algorithmic_bytes(rows)
-    gbs = (fwd + bwd) * reps / total / 1e9
-    return {"value": gbs, "unit": "GB/s", "cores": 1, "kind": "port",
-            "sample": f"{reps} x {rows} rows of [16384, 4096] (oracle port, single thread), "
-                      f"{total:.1f} s"}
+    return {"value": nbytes / total / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"{reps} samples of the {workload} workload (oracle port of the reference "
+                      f"CPU path, single thread), {total:.1f} s"}
 
 
 def _pool_worker(args):
-    rows, seed = args
-    return _oracle_step(rows, seed)
+    return cpu_sample(*args)
 
 
 def run_reference(args, rank, world):
-    """--impl reference: the oracle port on all host cores, row-sharded across a
-    spawn-started process pool; each step is a bounded row sample."""
+    """--impl reference: the oracle port on all host cores (spawn-started
+    process pool, one bounded sample per process per step)."""
     if rank != 0:
         return
     import multiprocessing as mp
     cores = os.cpu_count() or 1
-    rows_per_worker = 64
     ctx = mp.get_context("spawn")
     with ctx.Pool(cores) as pool:
-        pool.map(_pool_worker, [(8, 0)] * cores)
-        times = []
+        pool.map(_pool_worker, [(args.workload, 0)] * cores)
+        times, nbytes = [], 0
         for step in range(args.warmup + args.steps):
             t0 = time.perf_counter()
-            pool.map(_pool_worker, [(rows_per_worker, 1000 * step + i) for i in range(cores)])
+            res = pool.map(_pool_worker, [(args.workload, 1000 * step + i) for i in range(cores)])
             if step >= args.warmup:
                 times.append(time.perf_counter() - t0)
-    rows = rows_per_worker * cores
-    fwd, bwd = algorithmic_bytes(rows)
+                nbytes = sum(b for _, b in res)
     per_step = sum(times) / len(times)
-    gbs = (fwd + bwd) / per_step / 1e9
+    gbs = nbytes / per_step / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded N(0,1) / U(0.5,1.5) / N(0,0.1) inputs of config 2's distributions)",
-        "config": {"workload": "layer_norm+gelu fwd+bwd, fp32, x [16384, 4096] (BASELINE config 2)",
-                   "rows_per_step_sample": rows, "cols": COLS},
+        "data": "synthetic (seeded inputs with the BASELINE config's shapes and distributions)",
+        "config": {"workload": WORKLOADS[args.workload].DESC},
         "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port",
-                         "sample": f"{rows_per_worker} rows per process x {cores} processes per step "
-                                   "(oracle port of the reference CPU path; Rust reference not "
-                                   "buildable: no cargo)"},
+                         "sample": f"{cores} processes x one bounded {args.workload} sample per "
+                                   "step (oracle port of the reference CPU path; the Rust "
+                                   "reference is not buildable here: no cargo)"},
         "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-# ---- GPU arm -----------------------------------------------------------------------------
+# ---- GPU workloads --------------------------------------------------------------------------
+
+class Workload:
+    """Inputs resident on the device; fwd()/bwd() launch the path's kernels on
+    the current stream; exchange() is the data-parallel collective (N > 1)."""
+
+    flush = False          # inputs fit in L2: flush it between timed steps
+    dominant = "bwd"       # the kernel the roofline reports
+    launches = 0           # our kernels per step
+
+    def __init__(self, dev, rank, world, args):
+        import torch
+        from oxitorch_b200 import _native as N
+        self.torch, self.N, self.L = torch, N, N.load()
+        self.dev, self.rank, self.world, self.args = dev, rank, world, args
+        self.s = torch.cuda.current_stream().cuda_stream
+        self.gen = torch.Generator(device=dev)
+        self.gen.manual_seed(self.SEED + 1000 * rank)
+
+    def randn(self, *shape):
+        return self.torch.randn(*shape, device=self.dev, generator=self.gen)
+
+    def exchange(self):
+        pass
+
+    def config(self):
+        return {"workload": self.DESC}
+
+
+class LnGelu(Workload):
+    DESC = ("layer_norm(affine)+gelu(tanh) fwd+bwd, fp32, x [16384, 4096] per GPU "
+            "(BASELINE config 2)")
+    SEED = 2
+    KERNEL = "ln_bwd_pipe_kernel (layer_norm+gelu VJP) + dweight/dbias finisher"
+    launches = 4
+
+    def __init__(self, dev, rank, world, args):
+        super().__init__(dev, rank, world, args)
+        t = self.torch
+        self.rows, self.cols = args.rows or 16384, 4096
+        R, C = self.rows, self.cols
+        self.x, self.dy = self.randn(R, C), self.randn(R, C)
+        self.w = t.rand(C, device=dev, generator=self.gen) + 0.5
+        self.b = self.randn(C) * 0.1
+        self.y, self.dx = t.empty_like(self.x), t.empty_like(self.x)
+        self.mean, self.rstd = t.empty(R, device=dev), t.empty(R, device=dev)
+        self.dwdb = t.empty(2 * C, device=dev)
+        self.ws_bytes = self.L.oxc_layer_norm_bwd_workspace_size(R, C)
+        self.ws = t.empty(self.ws_bytes, dtype=t.uint8, device=dev)
+        self.fwd_bytes = R * (8 * C + 8) + 8 * C
+        self.bwd_bytes = R * (12 * C + 8) + 16 * C
+
+    def fwd(self, x=None):
+        N, L = self.N, self.L
+        N.check(L.oxc_layer_norm_fwd((x if x is not None else self.x).data_ptr(), self.w.data_ptr(),
+                                     self.b.data_ptr(), self.y.data_ptr(), self.mean.data_ptr(),
+                                     self.rstd.data_ptr(), self.rows, self.cols, 1e-5,
+                                     N.ACT_GELU_TANH, self.s))
+
+    def bwd(self, x=None, dy=None):
+        N, L = self.N, self.L
+        N.check(L.oxc_layer_norm_bwd((x if x is not None else self.x).data_ptr(), self.w.data_ptr(),
+                                     self.b.data_ptr(), self.mean.data_ptr(), self.rstd.data_ptr(),
+                                     (dy if dy is not None else self.dy).data_ptr(),
+                                     self.dx.data_ptr(), self.dwdb.data_ptr(),
+                                     self.dwdb.data_ptr() + self.cols * F32, self.rows, self.cols,
+                                     N.ACT_GELU_TANH, N.GRAD_REF, self.ws.data_ptr(),
+                                     self.ws_bytes, self.s))
+
+    def exchange(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(self.dwdb)
+
+    def e2e_io(self):
+        return [self.x, self.dy], [self.y, self.dx, self.dwdb]
+
+    def e2e_step(self, dev_in):
+        self.fwd(dev_in[0])
+        self.bwd(dev_in[0], dev_in[1])
+        self.exchange()
+
+    def config(self):
+        return {"workload": self.DESC, "rows_per_gpu": self.rows, "cols": self.cols, "eps": 1e-5,
+                "parallelism": f"row-sharded data parallel x{self.world}, dweight/dbias all-reduce",
+                "grad_mode": "ref (reference graph: rsqrt detached)",
+                "l2": "no flush: every input (268 MB) is larger than the 126 MB L2"}
+
+
+class Rms(Workload):
+    DESC = "rms_norm fwd+bwd, fp32, x [4096, 4096] per GPU (BASELINE config 1)"
+    SEED = 1
+    KERNEL = "rms_bwd_kernel (RMSNorm VJP) + dweight finisher"
+    flush = True
+    launches = 3
+
+    def __init__(self, dev, rank, world, args):
+        super().__init__(dev, rank, world, args)
+        t = self.torch
+        self.rows, self.cols = args.rows or 4096, 4096
+        R, C = self.rows, self.cols
+        self.x, self.dy = self.randn(R, C), self.randn(R, C)
+        self.w = t.rand(C, device=dev, generator=self.gen) + 0.5
+        self.y, self.dx = t.empty_like(self.x), t.empty_like(self.x)
+        self.rstd, self.dw = t.empty(R, device=dev), t.empty(C, device=dev)
+        self.ws_bytes = self.L.oxc_rms_norm_bwd_workspace_size(R, C)
+        self.ws = t.empty(self.ws_bytes, dtype=t.uint8, device=dev)
+        self.fwd_bytes = R * (8 * C + 4) + 4 * C
+        self.bwd_bytes = R * (12 * C + 4) + 8 * C
+
+    def fwd(self, x=None):
+        self.N.check(self.L.oxc_rms_norm_fwd((x if x is not None else self.x).data_ptr(),
+                                             self.w.data_ptr(), self.y.data_ptr(), self.rstd.data_ptr(),
+                                             self.rows, self.cols, 1e-6, self.s))
+
+    def bwd(self, x=None, dy=None):
+        self.N.check(self.L.oxc_rms_norm_bwd((x if x is not None else self.x).data_ptr(),
+                                             self.w.data_ptr(), self.rstd.data_ptr(),
+                                             (dy if dy is not None else self.dy).data_ptr(),
+                                             self.dx.data_ptr(), self.dw.data_ptr(), self.rows,
+                                             self.cols, self.N.GRAD_REF, self.ws.data_ptr(),
+                                             self.ws_bytes, self.s))
+
+    def exchange(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(self.dw)
+
+    def e2e_io(self):
+        return [self.x, self.dy], [self.y, self.dx, self.dw]
+
+    def e2e_step(self, dev_in):
+        self.fwd(dev_in[0])
+        self.bwd(dev_in[0], dev_in[1])
+        self.exchange()
+
+    def config(self):
+        return {"workload": self.DESC, "rows_per_gpu": self.rows, "cols": self.cols, "eps": 1e-6,
+                "l2": "flushed between steps (256 MB write, outside the timed events): "
+                      "each 67 MB tensor fits the 126 MB L2"}
+
+
+class CrossEntropy(Workload):
+    DESC = ("log_softmax+cross_entropy (mean) fwd+bwd, fp32, logits [32768, 32000] per GPU "
+            "(BASELINE config 3)")
+    SEED = 3
+    KERNEL = "ce_bwd_kernel (cross-entropy VJP)"
+    launches = 3
+
+    def __init__(self, dev, rank, world, args):
+        super().__init__(dev, rank, world, args)
+        t = self.torch
+        self.rows, self.cols = args.rows or 32768, 32000
+        R, C = self.rows, self.cols
+        self.x = self.randn(R, C) * 2.0
+        self.x[t.rand(R, C, device=dev, generator=self.gen) < 0.01] = 20.0
+        self.t = t.randint(0, C, (R,), device=dev, generator=self.gen)
+        self.loss = t.empty(1, device=dev)
+        self.rmax, self.rsum, self.rnll = (t.empty(R, device=dev) for _ in range(3))
+        self.dx = t.empty_like(self.x)
+        self.flag = t.zeros(4, dtype=t.int32, device=dev)
+        self.total = R * world
+        self.fwd_bytes = R * (4 * C + 8 + 12) + 4
+        self.bwd_bytes = R * (8 * C + 8 + 8)
+
+    def fwd(self, x=None):
+        self.N.check(self.L.oxc_cross_entropy_fwd(
+            (x if x is not None else self.x).data_ptr(), self.t.data_ptr(), self.loss.data_ptr(),
+            self.rmax.data_ptr(), self.rsum.data_ptr(), self.rnll.data_ptr(), self.rows, self.cols,
+            self.total, self.flag.data_ptr(), self.s))
+
+    def bwd(self, x=None):
+        self.N.check(self.L.oxc_cross_entropy_bwd(
+            (x if x is not None else self.x).data_ptr(), self.t.data_ptr(), self.rmax.data_ptr(),
+            self.rsum.data_ptr(), None, self.dx.data_ptr(), self.rows, self.cols, self.total, self.s))
+
+    def exchange(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(self.loss)
+
+    def e2e_io(self):
+        return [self.x], [self.loss, self.dx]
+
+    def e2e_step(self, dev_in):
+        self.fwd(dev_in[0])
+        self.bwd(dev_in[0])
+        self.exchange()
+
+    def config(self):
+        return {"workload": self.DESC, "rows_per_gpu": self.rows, "classes": self.cols,
+                "parallelism": f"row-sharded x{self.world}, loss all-reduce (global mean)",
+                "l2": "no flush: logits (4.19 GB) are larger than L2"}
+
+
+class Embedding(Workload):
+    DESC = ("embedding gather + duplicate-id VJP, fp32, table [32000, 4096], ids [64, 2048] "
+            "Zipf(1.1) clipped to 31999 per GPU (BASELINE config 4)")
+    SEED = 4
+    KERNEL = "emb_gather_kernel (forward gather)"
+    dominant = "fwd"
+    launches = 9  # gather; prepare, sort (4 CUB passes), offsets, split, rows
+
+    def __init__(self, dev, rank, world, args):
+        super().__init__(dev, rank, world, args)
+        import numpy as np
+        t = self.torch
+        self.v, self.d = 32000, 4096
+        n = (args.rows or 64 * 2048)
+        rng = np.random.default_rng(4 + 1000 * rank)
+        ids = np.minimum(rng.zipf(1.1, n) - 1, self.v - 1).astype(np.int64)
+        self.ids = t.from_numpy(ids).to(dev)
+        self.n = n
+        self.table = self.randn(self.v, self.d)
+        self.dout = self.randn(n, self.d)
+        self.out = t.empty(n, self.d, device=dev)
+        self.dtable = t.empty_like(self.table)
+        self.flag = t.zeros(4, dtype=t.int32, device=dev)
+        self.ws_bytes = self.L.oxc_embedding_bwd_workspace_size(n, self.v, self.d)
+        self.ws = t.empty(self.ws_bytes, dtype=t.uint8, device=dev)
+        self.fwd_bytes = n * 8 + 2 * n * self.d * 4
+        self.bwd_bytes = n * 8 + n * self.d * 4 + self.v * self.d * 4
+
+    def fwd(self, dout=None):
+        self.N.check(self.L.oxc_embedding_fwd(self.table.data_ptr(), self.ids.data_ptr(),
+                                              self.out.data_ptr(), self.n, self.v, 0, self.v,
+                                              self.d, self.flag.data_ptr(), self.s))
+
+    def bwd(self, dout=None):
+        self.N.check(self.L.oxc_embedding_bwd((dout if dout is not None else self.dout).data_ptr(),
+                                              self.ids.data_ptr(), self.dtable.data_ptr(), self.n,
+                                              self.v, 0, self.v, self.d, self.flag.data_ptr(),
+                                              self.ws.data_ptr(), self.ws_bytes, self.s))
+
+    def exchange(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(self.dtable)
+
+    def e2e_io(self):
+        return [self.dout], [self.out, self.dtable]
+
+    def e2e_step(self, dev_in):
+        self.fwd()
+        self.bwd(dev_in[0])
+        self.exchange()
+
+    def config(self):
+        return {"workload": self.DESC, "ids_per_gpu": self.n, "table": [self.v, self.d],
+                "parallelism": f"token-sharded data parallel x{self.world}, dtable all-reduce",
+                "l2": "no flush: dout (2.1 GB) is larger than L2; hot table rows are L2 hits "
+                      "by design (algorithmic bytes count every gathered row)"}
+
+
+class MlpBlock(Workload):
+    DESC = ("decoder-MLP activation block fwd+bwd, fp32, 65536 tokens: RMSNorm [.., 4096] "
+            "(broadcast weight view), SwiGLU [.., 11008] (transposed gate view), dim-1 "
+            "sum/max/argmax, whole-tensor L2 of {dx, dg, du} (BASELINE config 5)")
+    SEED = 5
+    KERNEL = "swiglu_bwd_kernel (SwiGLU VJP, sum-of-squares fused)"
+    launches = 8
+
+    def __init__(self, dev, rank, world, args):
+        super().__init__(dev, rank, world, args)
+        t = self.torch
+        M = args.rows or 65536
+        D, H = 4096, 11008
+        self.M, self.D, self.H = M, D, H
+        self.x = self.randn(M, D)
+        self.wbuf = t.rand(1, D, device=dev, generator=self.gen) + 0.5
+        self.gate_buf = self.randn(H, M)
+        self.up = self.randn(M, H)
+        self.dy, self.dh = self.randn(M, D), self.randn(M, H)
+        self.y, self.dx = t.empty_like(self.x), t.empty_like(self.x)
+        self.rstd, self.dw = t.empty(M, device=dev), t.empty(D, device=dev)
+        self.h, self.dg, self.du = (t.empty(M, H, device=dev) for _ in range(3))
+        self.hs, self.hm, self.ha = (t.empty(M, device=dev) for _ in range(3))
+        self.sq = t.empty(2, dtype=t.float64, device=dev)
+        self.rws_bytes = self.L.oxc_rms_norm_bwd_workspace_size(M, D)
+        self.rws = t.empty(self.rws_bytes, dtype=t.uint8, device=dev)
+        self.sws_bytes = self.L.oxc_swiglu_bwd_workspace_size(M, H)
+        self.sws = t.empty(self.sws_bytes, dtype=t.uint8, device=dev)
+        import ctypes
+        self.ctypes = ctypes
+        self.views = {}
+        self.qbytes = 0
+        self.fwd_bytes = M * (8 * D + 4) + 4 * D + M * 12 * H + 12 * M
+        self.bwd_bytes = M * (12 * D + 4) + 8 * D + M * 20 * H + 16
+
+    def _v(self, tensor):
+        return self.ctypes.byref(self.N.make_view(tensor))
+
+    def fwd(self, x=None, gate=None):
+        N, L = self.N, self.L
+        x = x if x is not None else self.x
+        gate = gate if gate is not None else self.gate_buf.t()
+        N.check(L.oxc_rms_norm_fwd(x.data_ptr(), self.wbuf.data_ptr(), self.y.data_ptr(),
+                                   self.rstd.data_ptr(), self.M, self.D, 1e-6, self.s))
+        N.check(L.oxc_swiglu_fwd(self._v(gate), self._v(self.up), self.h.data_ptr(),
+                                 self.hs.data_ptr(), self.hm.data_ptr(), self.ha.data_ptr(), self.s))
+
+    def bwd(self, x=None, gate=None):
+        N, L = self.N, self.L
+        x = x if x is not None else self.x
+        gate = gate if gate is not None else self.gate_buf.t()
+        N.check(L.oxc_rms_norm_bwd(x.data_ptr(), self.wbuf.data_ptr(), self.rstd.data_ptr(),
+                                   self.dy.data_ptr(), self.dx.data_ptr(), self.dw.data_ptr(),
+                                   self.M, self.D, N.GRAD_REF, self.rws.data_ptr(), self.rws_bytes,
+                                   self.s))
+        N.check(L.oxc_swiglu_bwd(self._v(gate), self._v(self.up), self._v(self.dh),
+                                 self.dg.data_ptr(), self.du.data_ptr(), self.sq.data_ptr(),
+                                 self.sws.data_ptr(), self.sws_bytes, self.s))
+        views = (N.View * 1)(N.make_view(self.dx))
+        N.check(L.oxc_sum_squares(views, 1, self.sq.data_ptr() + 8, self.sws.data_ptr(),
+                                  self.sws_bytes, self.s))
+
+    def exchange(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(self.dw)
+            dist.all_reduce(self.sq)
+
+    def e2e_io(self):
+        return ([self.x, self.gate_buf, self.up, self.dy, self.dh],
+                [self.y, self.h, self.hs, self.hm, self.ha, self.dx, self.dw, self.dg, self.du,
+                 self.sq])
+
+    def e2e_step(self, dev_in):
+        x, gate_buf, up, dy, dh = dev_in
+        saved = (self.up, self.dy, self.dh)
+        self.up, self.dy, self.dh = up, dy, dh
+        self.fwd(x, gate_buf.t())
+        self.bwd(x, gate_buf.t())
+        self.exchange()
+        self.up, self.dy, self.dh = saved
+
+    def config(self):
+        return {"workload": self.DESC, "tokens_per_gpu": self.M, "hidden": self.D,
+                "ffn": self.H, "gate_strides": [1, self.M], "weight_strides": [0, 1],
+                "l2": "no flush: every tensor (1-2.9 GB) is larger than L2"}
+
+
+WORKLOADS = {"ln_gelu": LnGelu, "rms": Rms, "ce": CrossEntropy, "embedding": Embedding,
+             "mlp_block": MlpBlock}
+
 
 def run_ours(args, rank, world, local_rank):
-    global ROWS
-    ROWS = args.rows
     import torch
     import torch.distributed as dist
-    from oxitorch_b200 import _native as N
-
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    L = N.load()
+    wl = WORKLOADS[args.workload](dev, rank, world, args)
     stream = torch.cuda.current_stream()
-    s = stream.cuda_stream
+    flush_buf = torch.empty(64 * 1024 * 1024, device=dev) if wl.flush else None  # 256 MB
 
-    g = torch.Generator(device=dev)
-    g.manual_seed(2 + 1000 * rank)
-    x = torch.randn(ROWS, COLS, device=dev, generator=g)
-    dy = torch.randn(ROWS, COLS, device=dev, generator=g)
-    w = torch.rand(COLS, device=dev, generator=g) + 0.5
-    b = torch.randn(COLS, device=dev, generator=g) * 0.1
-    y = torch.empty_like(x)
-    dx = torch.empty_like(x)
-    mean = torch.empty(ROWS, device=dev)
-    rstd = torch.empty(ROWS, device=dev)
-    dw = torch.empty(COLS, device=dev)
-    db = torch.empty(COLS, device=dev)
-    ws_bytes = L.oxc_layer_norm_bwd_workspace_size(ROWS, COLS)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
-    dwdb = torch.empty(2 * COLS, device=dev)
+    def step(ev):
+        if flush_buf is not None:
+            flush_buf.fill_(1.0)  # evict the previous step's data from L2 (outside the events)
+        ev[0].record(stream)
+        wl.fwd()
+        ev[1].record(stream)
+        wl.bwd()
+        ev[2].record(stream)
+        wl.exchange()
+        ev[3].record(stream)
 
-    def fwd(xp, yp):
-        N.check(L.oxc_layer_norm_fwd(xp, w.data_ptr(), b.data_ptr(), yp, mean.data_ptr(),
-                                     rstd.data_ptr(), ROWS, COLS, EPS, N.ACT_GELU_TANH, s))
-
-    def bwd(xp, dyp, dxp):
-        N.check(L.oxc_layer_norm_bwd(xp, w.data_ptr(), b.data_ptr(), mean.data_ptr(),
-                                     rstd.data_ptr(), dyp, dxp, dwdb.data_ptr(),
-                                     dwdb.data_ptr() + COLS * F32, ROWS, COLS, N.ACT_GELU_TANH,
-                                     N.GRAD_REF, ws.data_ptr(), ws_bytes, s))
-
-    def exchange():
-        if world > 1:
-            dist.all_reduce(dwdb)
-
-    def step(ev=None):
-        if ev is not None:
-            ev[0].record(stream)
-        fwd(x.data_ptr(), y.data_ptr())
-        if ev is not None:
-            ev[1].record(stream)
-        bwd(x.data_ptr(), dy.data_ptr(), dx.data_ptr())
-        if ev is not None:
-            ev[2].record(stream)
-        exchange()
-
-    launches_per_step = 4  # fwd, VJP, 2 x column-sum finisher
-
+    warm_ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     for _ in range(args.warmup):
-        step()
+        step(warm_ev)
     torch.cuda.synchronize()
 
     sampler = ClockSampler(local_rank)
     sampler.start()
     time.sleep(0.2)
-    events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    start.record(stream)
     for i in range(args.steps):
         step(events[i])
-    end.record(stream)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clocks = sampler.stop()
-    ms = start.elapsed_time(end)
+    # device time of exactly K steps (the L2 flush of `rms` excluded)
+    ms = sum(e[0].elapsed_time(e[3]) for e in events)
     fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in events)
     bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in events)
     if world > 1:
@@ -279,60 +622,56 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     ms_per_step = ms / args.steps
-
-    fwd_bytes, bwd_bytes = algorithmic_bytes(ROWS)
-    value = world * (fwd_bytes + bwd_bytes) / (ms_per_step * 1e-3) / 1e9
+    value = world * (wl.fwd_bytes + wl.bwd_bytes) / (ms_per_step * 1e-3) / 1e9
     peak, peak_kind = measured_peak()
 
     # ---- e2e: host buffers through the C ABI --------------------------------------------
-    e2e_steps = 0 if args.skip_e2e else max(1, min(args.steps, 5))
-    hx = torch.empty(ROWS, COLS, pin_memory=True)
-    hdy = torch.empty(ROWS, COLS, pin_memory=True)
-    hx.copy_(x)
-    hdy.copy_(dy)
-    hy = torch.empty(ROWS, COLS, pin_memory=True)
-    hdx = torch.empty(ROWS, COLS, pin_memory=True)
-    hdwdb = torch.empty(2 * COLS, pin_memory=True)
-    xs = torch.empty_like(x)
-    dys = torch.empty_like(dy)
+    e2e = None
+    if args.workload == "mlp_block" and not args.e2e_large:
+        e2e = {"value": None, "unit": "GB/s", "skipped": "config 5 moves ~23 GB per step through "
+               "pinned host buffers; pass --e2e-large to measure it"}
+    elif not args.skip_e2e:
+        ins, outs = wl.e2e_io()
+        h_in = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t) for t in ins]
+        d_in = [torch.empty_like(t) for t in ins]
+        h_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in outs]
 
-    def e2e_step():
-        xs.copy_(hx, non_blocking=True)
-        dys.copy_(hdy, non_blocking=True)
-        fwd(xs.data_ptr(), y.data_ptr())
-        bwd(xs.data_ptr(), dys.data_ptr(), dx.data_ptr())
-        exchange()
-        hy.copy_(y, non_blocking=True)
-        hdx.copy_(dx, non_blocking=True)
-        hdwdb.copy_(dwdb, non_blocking=True)
+        def e2e_step():
+            for d, h in zip(d_in, h_in):
+                d.copy_(h, non_blocking=True)
+            wl.e2e_step(d_in)
+            for h, d in zip(h_out, outs):
+                h.copy_(d, non_blocking=True)
 
-    if e2e_steps:
+        e2e_steps = max(1, min(args.steps, 3))
         e2e_step()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_value = (world * (fwd_bytes + bwd_bytes) / (e2e_ms / e2e_steps * 1e-3) / 1e9
-                 if e2e_steps else None)
-    h2d = 2 * ROWS * COLS * F32
-    d2h = 2 * ROWS * COLS * F32 + 2 * COLS * F32
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        e2e = {"value": world * (wl.fwd_bytes + wl.bwd_bytes) / (e2e_ms / e2e_steps * 1e-3) / 1e9,
+               "unit": "GB/s",
+               "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in ins),
+               "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in outs),
+               "ms_per_step": e2e_ms / e2e_steps,
+               "path": "pinned host -> C ABI fwd/bwd entry points -> pinned host"}
 
     if rank != 0:
         return
-    cpu = cpu_baseline() if (world == 1 and not args.no_cpu_baseline) else None
-    achieved = bwd_bytes / (bwd_ms * 1e-3) / 1e9
-    traffic = _profiled_traffic()
+    cpu = cpu_baseline(args.workload) if (world == 1 and not args.no_cpu_baseline) else None
+    dom_ms, dom_bytes = (bwd_ms, wl.bwd_bytes) if wl.dominant == "bwd" else (fwd_ms, wl.fwd_bytes)
+    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
     line = {
         "metric": METRIC,
         "value": value,
@@ -345,46 +684,36 @@ def run_ours(args, rank, world, local_rank):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "f32",
-        "data": "synthetic (seeded torch N(0,1) x/dy, U(0.5,1.5) weight, N(0,0.1) bias; no dataset)",
-        "config": {
-            "workload": "layer_norm(affine)+gelu(tanh) fwd+bwd, fp32, x [16384, 4096] per GPU "
-                        "(BASELINE config 2)",
-            "rows_per_gpu": ROWS, "cols": COLS, "eps": EPS,
-            "parallelism": f"row-sharded data parallel x{world}, dweight/dbias all-reduce",
-            "grad_mode": "ref (reference graph: rsqrt detached)",
-            "l2": "no flush: every input (268 MB) is larger than the 126 MB L2",
-            "algorithmic_bytes_per_gpu_step": fwd_bytes + bwd_bytes,
-        },
+        "data": "synthetic (seeded inputs with the BASELINE config's shapes and distributions; "
+                "no dataset)",
+        "config": {**wl.config(), "algorithmic_bytes_per_gpu_step": wl.fwd_bytes + wl.bwd_bytes},
         "roofline": {
             "bound": "hbm",
-            "kernel": "ln_bwd_kernel (layer_norm+gelu VJP, incl. dweight/dbias finisher)",
+            "kernel": wl.KERNEL,
             "achieved": achieved,
             "peak": peak,
             "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs: torch copy read+write)",
             "unit": "GB/s",
             "frac": achieved / peak,
-            "traffic": traffic,
-            "fwd_kernel_gbs": fwd_bytes / (fwd_ms * 1e-3) / 1e9,
-            "fwd_kernel_frac": fwd_bytes / (fwd_ms * 1e-3) / 1e9 / peak,
+            "traffic": _profiled_traffic(args.workload),
+            "fwd_gbs": wl.fwd_bytes / (fwd_ms * 1e-3) / 1e9,
+            "bwd_gbs": wl.bwd_bytes / (bwd_ms * 1e-3) / 1e9,
             "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
         },
-        "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / e2e_steps if e2e_steps else None,
-                "path": "pinned host -> oxc_layer_norm_fwd/bwd (C ABI) -> pinned host"},
-        "gpu_launches": launches_per_step * args.steps,
+        "e2e": e2e,
+        "gpu_launches": wl.launches * args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
 
 
-def _profiled_traffic():
-    """DRAM bytes per launch of the VJP kernel from the committed ncu summary
-    (profiles/ln_gelu_bwd_16384x4096.json), or None if absent."""
-    path = os.path.join(ROOT, "profiles", "ln_gelu_bwd_16384x4096.json")
+def _profiled_traffic(workload):
+    """DRAM bytes per launch of the roofline kernel at this workload's full
+    size, from the committed ncu summary (profiles/traffic.json), or None."""
     try:
-        with open(path) as f:
-            return json.load(f).get("dram_bytes_per_launch")
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f).get(workload, {}).get("dram_bytes_per_launch")
     except Exception:
         return None
 
@@ -392,13 +721,17 @@ def _profiled_traffic():
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=100)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="ln_gelu", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--rows", type=int, default=ROWS,
-                    help="rows per GPU (default: config 2's 16384; smaller only for profiling)")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="rows / tokens / ids per GPU (0 = the BASELINE config's; smaller only "
+                         "for profiling)")
     ap.add_argument("--skip-e2e", action="store_true", help="profiling runs: no host-buffer leg")
+    ap.add_argument("--e2e-large", action="store_true",
+                    help="also run the host-buffer leg of the mlp_block workload")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -64,36 +64,35 @@ int occupancy(const void* kernel, int block, size_t smem) {
   return n;
 }
 
-// Column sums of per-CTA partials.  CTA = 8 warps x 32 columns; warp w adds
-// parts w, w+8, w+16, ... (sequentially, 4 loads in flight), then warp 0 adds
-// the 8 warp results in order.  Fixed order => deterministic.
-__global__ void __launch_bounds__(256) colsum_partials_kernel(const float* __restrict__ parts,
-                                                              int nparts, int64_t cols,
-                                                              float* __restrict__ out) {
-  __shared__ float red[8][33];
+// Column sums of per-CTA partials.  CTA = 32 warps x 32 columns; warp w adds
+// parts w, w+32, w+64, ... (4 loads in flight), then warp 0 adds the 32 warp
+// results in warp order.  Fixed order => deterministic.
+__global__ void __launch_bounds__(1024) colsum_partials_kernel(const float* __restrict__ parts,
+                                                               int nparts, int64_t cols,
+                                                               float* __restrict__ out) {
+  __shared__ float red[32][33];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t col = (int64_t)blockIdx.x * 32 + lane;
   float acc = 0.0f;
   if (col < cols) {
     int p = warp;
-    for (; p + 24 < nparts; p += 32) {
-      float a = parts[(int64_t)p * cols + col];
-      float b = parts[(int64_t)(p + 8) * cols + col];
-      float c = parts[(int64_t)(p + 16) * cols + col];
-      float d = parts[(int64_t)(p + 24) * cols + col];
+    for (; p + 96 < nparts; p += 128) {
+      const float a = parts[(int64_t)p * cols + col];
+      const float b = parts[(int64_t)(p + 32) * cols + col];
+      const float c = parts[(int64_t)(p + 64) * cols + col];
+      const float d = parts[(int64_t)(p + 96) * cols + col];
       acc = __fadd_rn(acc, a);
       acc = __fadd_rn(acc, b);
       acc = __fadd_rn(acc, c);
       acc = __fadd_rn(acc, d);
     }
-    for (; p < nparts; p += 8) acc = __fadd_rn(acc, parts[(int64_t)p * cols + col]);
+    for (; p < nparts; p += 32) acc = __fadd_rn(acc, parts[(int64_t)p * cols + col]);
   }
   red[warp][lane] = acc;
   __syncthreads();
   if (warp == 0 && col < cols) {
     float s = red[0][lane];
-#pragma unroll
-    for (int w = 1; w < 8; ++w) s = __fadd_rn(s, red[w][lane]);
+    for (int w = 1; w < 32; ++w) s = __fadd_rn(s, red[w][lane]);
     out[col] = s;
   }
 }
@@ -101,7 +100,7 @@ __global__ void __launch_bounds__(256) colsum_partials_kernel(const float* __res
 void launch_colsum_partials(const float* parts, int nparts, int64_t cols, float* out,
                             cudaStream_t stream) {
   const int64_t grid = (cols + 31) / 32;
-  colsum_partials_kernel<<<(unsigned)grid, 256, 0, stream>>>(parts, nparts, cols, out);
+  colsum_partials_kernel<<<(unsigned)grid, 1024, 0, stream>>>(parts, nparts, cols, out);
 }
 
 }  // namespace oxc

@@ -18,7 +18,7 @@
 //        the CUDA toolkit): equal keys keep increasing position order.
 //     3. offsets: segment starts read straight off the sorted keys.
 //     4. split pieces: rows occurring more than P times are cut at the fixed
-//        P-position blocks of the sorted array; one CTA per block sums its (at
+//        P-position blocks (P = 128) of the sorted array; one CTA per block sums its (at
 //        most two) pieces of such rows into partial rows.
 //     5. rows: one CTA per table row writes zeros (no occurrence), the
 //        left-to-right sum of its <= P occurrences in position order
@@ -121,56 +121,45 @@ __global__ void emb_offsets_kernel(const int32_t* __restrict__ skeys, int64_t n,
   }
 }
 
-// Sums dout rows spos[p0..p1) (in order) into acc for this thread's columns.
+// Sums dout rows spos[p0..p1) (in order) into acc for this thread's columns;
+// four rows' loads are in flight before they are added in position order.
 template <int VW, int VPT>
 __device__ __forceinline__ void sum_positions(const float* __restrict__ dout,
                                               const int32_t* __restrict__ spos, int64_t p0,
                                               int64_t p1, int cols, int c_base,
                                               float (&acc)[VPT][VW]) {
   const int nvec = cols / VW;
-  int64_t p = p0;
-  for (; p + 1 < p1; p += 2) {
-    const float* ra = dout + (int64_t)spos[p] * cols;
-    const float* rb = dout + (int64_t)spos[p + 1] * cols;
-    float qa[VPT][VW], qb[VPT][VW];
+  constexpr int U = 4;
+  for (int64_t p = p0; p < p1; p += U) {
+    float q[U][VPT][VW];
 #pragma unroll
-    for (int i = 0; i < VPT; ++i) {
-      const int v = c_base + i * blockDim.x + threadIdx.x;
-      if (v < nvec) {
-        if constexpr (VW == 4) {
-          const float4 a = ld_stream(reinterpret_cast<const float4*>(ra) + v);
-          const float4 b = ld_stream(reinterpret_cast<const float4*>(rb) + v);
-          qa[i][0] = a.x; qa[i][1] = a.y; qa[i][2] = a.z; qa[i][3] = a.w;
-          qb[i][0] = b.x; qb[i][1] = b.y; qb[i][2] = b.z; qb[i][3] = b.w;
+    for (int j = 0; j < U; ++j) {
+      const bool live = p + j < p1;
+      const float* row = dout + (live ? (int64_t)spos[p + j] : 0) * cols;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int v = c_base + i * blockDim.x + threadIdx.x;
+        if (live && v < nvec) {
+          if constexpr (VW == 4) {
+            const float4 a = ld_stream(reinterpret_cast<const float4*>(row) + v);
+            q[j][i][0] = a.x; q[j][i][1] = a.y; q[j][i][2] = a.z; q[j][i][3] = a.w;
+          } else {
+            q[j][i][0] = ld_stream(row + v);
+          }
         } else {
-          qa[i][0] = ld_stream(ra + v);
-          qb[i][0] = ld_stream(rb + v);
-        }
-      } else {
 #pragma unroll
-        for (int e = 0; e < VW; ++e) { qa[i][e] = 0.0f; qb[i][e] = 0.0f; }
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < VPT; ++i)
-#pragma unroll
-      for (int e = 0; e < VW; ++e) acc[i][e] = __fadd_rn(__fadd_rn(acc[i][e], qa[i][e]), qb[i][e]);
-  }
-  if (p < p1) {
-    const float* ra = dout + (int64_t)spos[p] * cols;
-#pragma unroll
-    for (int i = 0; i < VPT; ++i) {
-      const int v = c_base + i * blockDim.x + threadIdx.x;
-      if (v < nvec) {
-        if constexpr (VW == 4) {
-          const float4 a = ld_stream(reinterpret_cast<const float4*>(ra) + v);
-          acc[i][0] = __fadd_rn(acc[i][0], a.x); acc[i][1] = __fadd_rn(acc[i][1], a.y);
-          acc[i][2] = __fadd_rn(acc[i][2], a.z); acc[i][3] = __fadd_rn(acc[i][3], a.w);
-        } else {
-          acc[i][0] = __fadd_rn(acc[i][0], ld_stream(ra + v));
+          for (int e = 0; e < VW; ++e) q[j][i][e] = 0.0f;
         }
       }
     }
+#pragma unroll
+    for (int j = 0; j < U; ++j)
+      if (p + j < p1) {
+#pragma unroll
+        for (int i = 0; i < VPT; ++i)
+#pragma unroll
+          for (int e = 0; e < VW; ++e) acc[i][e] = __fadd_rn(acc[i][e], q[j][i][e]);
+      }
   }
 }
 
@@ -245,23 +234,40 @@ __global__ void __launch_bounds__(256) emb_rows_kernel(
       if (s1 - s0 <= kSplitP) {
         sum_positions<VW, VPT>(dout, spos, s0, s1, cols, c_base, acc);
       } else {
+        // pieces in block order, eight partial rows in flight per step
         const int64_t j0 = s0 / kSplitP, j1 = (s1 - 1) / kSplitP;
-        for (int64_t j = j0; j <= j1; ++j) {
-          const int side = (j == j0 && s0 != j0 * kSplitP) ? 1 : 0;
-          const float* src = parts + (2 * j + side) * (int64_t)cols;
+        constexpr int UJ = 8;
+        for (int64_t jb = j0; jb <= j1; jb += UJ) {
+          float q[UJ][VPT][VW];
 #pragma unroll
-          for (int i = 0; i < VPT; ++i) {
-            const int v = c_base + i * blockDim.x + threadIdx.x;
-            if (v < nvec) {
-              if constexpr (VW == 4) {
-                const float4 a = reinterpret_cast<const float4*>(src)[v];
-                acc[i][0] = __fadd_rn(acc[i][0], a.x); acc[i][1] = __fadd_rn(acc[i][1], a.y);
-                acc[i][2] = __fadd_rn(acc[i][2], a.z); acc[i][3] = __fadd_rn(acc[i][3], a.w);
+          for (int u = 0; u < UJ; ++u) {
+            const int64_t j = jb + u;
+            const int side = (j == j0 && s0 != j0 * kSplitP) ? 1 : 0;
+            const float* src = parts + (2 * min(j, j1) + side) * (int64_t)cols;
+#pragma unroll
+            for (int i = 0; i < VPT; ++i) {
+              const int v = c_base + i * blockDim.x + threadIdx.x;
+              if (j <= j1 && v < nvec) {
+                if constexpr (VW == 4) {
+                  const float4 a = reinterpret_cast<const float4*>(src)[v];
+                  q[u][i][0] = a.x; q[u][i][1] = a.y; q[u][i][2] = a.z; q[u][i][3] = a.w;
+                } else {
+                  q[u][i][0] = src[v];
+                }
               } else {
-                acc[i][0] = __fadd_rn(acc[i][0], src[v]);
+#pragma unroll
+                for (int e = 0; e < VW; ++e) q[u][i][e] = 0.0f;
               }
             }
           }
+#pragma unroll
+          for (int u = 0; u < UJ; ++u)
+            if (jb + u <= j1) {
+#pragma unroll
+              for (int i = 0; i < VPT; ++i)
+#pragma unroll
+                for (int e = 0; e < VW; ++e) acc[i][e] = __fadd_rn(acc[i][e], q[u][i][e]);
+            }
         }
       }
       store_acc<VW, VPT>(dst, cols, c_base, acc, true);

@@ -318,7 +318,9 @@ __global__ void __launch_bounds__((NG * NWG + 1) * 32, 1) ln_fwd_pipe_kernel(
   }
 }
 
-template <int NG, int NWG, int VPT, int ACT, int MODE>
+// SACC: the per-group dweight/dbias accumulators live in shared memory
+// (2 * cols floats per group after w and b) instead of registers.
+template <int NG, int NWG, int VPT, int ACT, int MODE, bool SACC>
 __global__ void __launch_bounds__((NG * NWG + 1) * 32, 1) ln_bwd_pipe_kernel(
     const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
     const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
@@ -329,7 +331,11 @@ __global__ void __launch_bounds__((NG * NWG + 1) * 32, 1) ln_bwd_pipe_kernel(
   const RowRing<2> ring = make_ring<2, NWG>(smem, stages, cols, &red);
   float* ws = red + 64;
   float* bs = ws + cols;
+  float* sacc = bs + cols;  // [NG][2][cols] when SACC
   stage_params(ws, w, bs, b, cols);
+  if constexpr (SACC) {
+    for (int v = threadIdx.x; v < NG * 2 * cols; v += blockDim.x) sacc[v] = 0.0f;
+  }
   __syncthreads();
   const int64_t r0 = (int64_t)blockIdx.x * chunk;
   const int64_t r1 = min(rows, r0 + chunk);
@@ -347,12 +353,16 @@ __global__ void __launch_bounds__((NG * NWG + 1) * 32, 1) ln_bwd_pipe_kernel(
   const int nvec = cols >> 2;
   const float4* w4 = reinterpret_cast<const float4*>(ws);
   const float4* b4 = reinterpret_cast<const float4*>(bs);
-  float4 adw[VPT], adb[VPT];
+  float4 adw[SACC ? 1 : VPT], adb[SACC ? 1 : VPT];
+  if constexpr (!SACC) {
 #pragma unroll
-  for (int k = 0; k < VPT; ++k) {
-    adw[k] = make_float4(0, 0, 0, 0);
-    adb[k] = make_float4(0, 0, 0, 0);
+    for (int k = 0; k < VPT; ++k) {
+      adw[k] = make_float4(0, 0, 0, 0);
+      adb[k] = make_float4(0, 0, 0, 0);
+    }
   }
+  float4* gdw = reinterpret_cast<float4*>(sacc + (size_t)g * 2 * cols);
+  float4* gdb = gdw + nvec;
   const float inv_n = __fdiv_rn(1.0f, (float)cols);
   // Row statistics are prefetched one group-iteration ahead so their global
   // load latency is not on each row's critical path.
@@ -391,8 +401,13 @@ __global__ void __launch_bounds__((NG * NWG + 1) * 32, 1) ln_bwd_pipe_kernel(
       float* ge = reinterpret_cast<float*>(&gv[k]);
       const float* we = reinterpret_cast<const float*>(&wv);
       const float* be = reinterpret_cast<const float*>(&bv);
-      float* dwe = reinterpret_cast<float*>(&adw[k]);
-      float* dbe = reinterpret_cast<float*>(&adb[k]);
+      float4 dw4, db4;
+      if constexpr (SACC) {
+        dw4 = slot < nvec ? gdw[slot] : make_float4(0, 0, 0, 0);
+        db4 = slot < nvec ? gdb[slot] : make_float4(0, 0, 0, 0);
+      }
+      float* dwe = SACC ? reinterpret_cast<float*>(&dw4) : reinterpret_cast<float*>(&adw[SACC ? 0 : k]);
+      float* dbe = SACC ? reinterpret_cast<float*>(&db4) : reinterpret_cast<float*>(&adb[SACC ? 0 : k]);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float t1 = (xe[e] - mu) * inv;
@@ -409,6 +424,12 @@ __global__ void __launch_bounds__((NG * NWG + 1) * 32, 1) ln_bwd_pipe_kernel(
           xe[e] = t1;
           s1 += gw;
           s2 = fmaf(gw, t1, s2);
+        }
+      }
+      if constexpr (SACC) {
+        if (slot < nvec) {
+          gdw[slot] = dw4;
+          gdb[slot] = db4;
         }
       }
     }
@@ -434,9 +455,25 @@ __global__ void __launch_bounds__((NG * NWG + 1) * 32, 1) ln_bwd_pipe_kernel(
       }
     }
   }
-  // Combine the groups' column partials in group order through shared memory
-  // (the ring is idle: every issued copy was waited for by its consumer).
+  // Combine the groups' column partials in group order.
   all_consumers_sync<NG * NWG * 32>();
+  if constexpr (SACC) {
+    float4* pw = reinterpret_cast<float4*>(parts + (int64_t)blockIdx.x * cols);
+    float4* pb = reinterpret_cast<float4*>(parts + ((int64_t)gridDim.x + blockIdx.x) * cols);
+    const float4* s4 = reinterpret_cast<const float4*>(sacc);
+    for (int v = threadIdx.x; v < nvec; v += NG * NWG * 32) {
+      float4 a = s4[v], c = s4[nvec + v];
+      for (int h = 1; h < NG; ++h) {
+        const float4 p = s4[(size_t)2 * h * nvec + v];
+        const float4 q = s4[(size_t)(2 * h + 1) * nvec + v];
+        a.x += p.x; a.y += p.y; a.z += p.z; a.w += p.w;
+        c.x += q.x; c.y += q.y; c.z += q.z; c.w += q.w;
+      }
+      pw[v] = a;
+      pb[v] = c;
+    }
+    return;
+  } else {
   float4* comb = reinterpret_cast<float4*>(ring.buf);  // (NG-1) x 2 x cols floats
   if (g > 0) {
 #pragma unroll
@@ -468,6 +505,7 @@ __global__ void __launch_bounds__((NG * NWG + 1) * 32, 1) ln_bwd_pipe_kernel(
       }
     }
   }
+  }
 }
 
 // Pipeline geometry: NG groups x NWG warps.
@@ -490,17 +528,18 @@ static size_t max_smem_optin() {
 
 // Stages of the ring for `nin` inputs of `cols` floats plus the staged
 // weight/bias (0 = pipeline unusable: fewer than `min_stages` fit).
-static int pipe_stages(int nin, int64_t cols, int max_stages, int min_stages) {
+static int pipe_stages(int nin, int64_t cols, int max_stages, int min_stages,
+                       int64_t extra_floats = 0) {
   const size_t avail = max_smem_optin();
   int st = max_stages;
-  while (st >= min_stages && ring_smem_bytes(nin, cols, st, 2 * cols) > avail) --st;
+  while (st >= min_stages && ring_smem_bytes(nin, cols, st, 2 * cols + extra_floats) > avail) --st;
   return st >= min_stages ? st : 0;
 }
 
 // VPT (float4 slots per consumer thread, threads = nwg * 32), or 0.
 static int pipe_vpt(int64_t cols, int nwg, int max_vpt) {
   const int64_t nvec = cols / 4, T = (int64_t)nwg * 32;
-  for (int v : {1, 2, 4, 8})
+  for (int v : {1, 2, 3, 4, 8})
     if (v <= max_vpt && nvec <= v * T) return v;
   return 0;
 }
@@ -630,7 +669,11 @@ oxc_status oxc_layer_norm_bwd(const float* x, const float* w, const float* b, co
                   aligned16(dy) && aligned16(dx) && aligned16(workspace);
   float* parts = static_cast<float*>(workspace);
   const GeluConst gc = gelu_const();
-  const int stages = v4 ? pipe_stages(2, cols, 6, kBwdNG + 1) : 0;
+  // shared-memory accumulators (2 * NG * cols floats) when the ring keeps
+  // NG + 2 stages alongside them; else register accumulators
+  const int stages_sacc = v4 ? pipe_stages(2, cols, 6, kBwdNG + 2, 2 * kBwdNG * cols) : 0;
+  const bool sacc = stages_sacc > 0;
+  const int stages = sacc ? stages_sacc : (v4 ? pipe_stages(2, cols, 6, kBwdNG + 1) : 0);
   const int vpt = v4 ? pipe_vpt(cols, kBwdNWG, 4) : 0;
   if (stages && vpt) {
     // At most ln_bwd_ctas(rows) CTAs, the partial slots the workspace holds.
@@ -638,14 +681,21 @@ oxc_status oxc_layer_norm_bwd(const float* x, const float* w, const float* b, co
     if ((size_t)2 * ctas * cols * sizeof(float) > workspace_bytes)
       return fail(OXC_ERR_OTHER, "internal: layer_norm backward partials exceed the workspace");
     const int64_t chunk = (rows + ctas - 1) / ctas;
-    const size_t smem = ring_smem_bytes(2, cols, stages, 2 * cols);
+    const size_t smem = ring_smem_bytes(2, cols, stages, 2 * cols + (sacc ? 2 * kBwdNG * cols : 0));
     const int block = (kBwdNG * kBwdNWG + 1) * 32;
 #define LAUNCH_P(VPT, ACT, MODE)                                                              \
   do {                                                                                        \
-    auto k = ln_bwd_pipe_kernel<kBwdNG, kBwdNWG, VPT, ACT, MODE>;                             \
-    allow_smem(k, smem);                                                                      \
-    k<<<(unsigned)ctas, block, smem, s>>>(x, w, b, mean, rstd, dy, dx, parts, rows, (int)cols, \
-                                          chunk, stages, gc);                                 \
+    if (sacc) {                                                                               \
+      auto k = ln_bwd_pipe_kernel<kBwdNG, kBwdNWG, VPT, ACT, MODE, true>;                     \
+      allow_smem(k, smem);                                                                    \
+      k<<<(unsigned)ctas, block, smem, s>>>(x, w, b, mean, rstd, dy, dx, parts, rows,         \
+                                            (int)cols, chunk, stages, gc);                    \
+    } else {                                                                                  \
+      auto k = ln_bwd_pipe_kernel<kBwdNG, kBwdNWG, VPT, ACT, MODE, false>;                    \
+      allow_smem(k, smem);                                                                    \
+      k<<<(unsigned)ctas, block, smem, s>>>(x, w, b, mean, rstd, dy, dx, parts, rows,         \
+                                            (int)cols, chunk, stages, gc);                    \
+    }                                                                                         \
   } while (0)
 #define LAUNCH_A(VPT)                                                                         \
   do {                                                                                        \
@@ -660,6 +710,7 @@ oxc_status oxc_layer_norm_bwd(const float* x, const float* w, const float* b, co
     switch (vpt) {
       case 1: LAUNCH_A(1); break;
       case 2: LAUNCH_A(2); break;
+      case 3: LAUNCH_A(3); break;
       default: LAUNCH_A(4); break;
     }
 #undef LAUNCH_A

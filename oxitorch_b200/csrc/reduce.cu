@@ -365,20 +365,50 @@ __global__ void __launch_bounds__(256) sumsq_multi_stage1(MultiViews mv, double*
   while (t + 1 < mv.count && part >= mv.first_part[t + 1]) ++t;
   const int64_t i0 = (part - mv.first_part[t]) * mv.chunk, i1 = min(mv.n[t], i0 + mv.chunk);
   const bool dense = mv.f[t].nd == 1 && mv.f[t].st[0] == 1;
-  double acc = 0.0;
-  for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
-    const float x = dense ? ld_stream(mv.p[t] + i) : __ldg(mv.p[t] + flat_offset(mv.f[t], i));
-    acc += (double)x * (double)x;
+  double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+  int64_t i = i0 + threadIdx.x;
+  if (dense && (reinterpret_cast<uintptr_t>(mv.p[t] + i0) & 15) == 0) {
+    // 128-bit loads, four independent f64 chains, 4 loads in flight per thread
+    const float4* p4 = reinterpret_cast<const float4*>(mv.p[t] + i0);
+    const int64_t nv = (i1 - i0) / 4;
+    int64_t v = threadIdx.x;
+    for (; v + 3 * (int64_t)blockDim.x < nv; v += 4 * blockDim.x) {
+      float4 q[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) q[u] = ld_stream(p4 + v + u * blockDim.x);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        a0 = fma((double)q[u].x, (double)q[u].x, a0);
+        a1 = fma((double)q[u].y, (double)q[u].y, a1);
+        a2 = fma((double)q[u].z, (double)q[u].z, a2);
+        a3 = fma((double)q[u].w, (double)q[u].w, a3);
+      }
+    }
+    for (; v < nv; v += blockDim.x) {
+      const float4 q = ld_stream(p4 + v);
+      a0 = fma((double)q.x, (double)q.x, a0);
+      a1 = fma((double)q.y, (double)q.y, a1);
+      a2 = fma((double)q.z, (double)q.z, a2);
+      a3 = fma((double)q.w, (double)q.w, a3);
+    }
+    i = i0 + nv * 4 + threadIdx.x;
   }
-  const double s = block_sum(acc, sd);
+  for (; i < i1; i += blockDim.x) {
+    const float x = dense ? ld_stream(mv.p[t] + i) : __ldg(mv.p[t] + flat_offset(mv.f[t], i));
+    a0 = fma((double)x, (double)x, a0);
+  }
+  const double s = block_sum((a0 + a1) + (a2 + a3), sd);
   if (threadIdx.x == 0) ps[part] = s;
 }
 
-__global__ void sumsq_multi_stage2(int64_t nparts, const double* __restrict__ ps, double* __restrict__ out) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+// Fixed-order block reduction of the stage-1 partials.
+__global__ void __launch_bounds__(256) sumsq_multi_stage2(int64_t nparts, const double* __restrict__ ps,
+                                                          double* __restrict__ out) {
+  __shared__ double red[33];
   double a = 0.0;
-  for (int64_t p = 0; p < nparts; ++p) a += ps[p];
-  out[0] = a;
+  for (int64_t p = threadIdx.x; p < nparts; p += blockDim.x) a += ps[p];
+  const double t = block_sum(a, red);
+  if (threadIdx.x == 0) out[0] = t;
 }
 
 // ---- host helpers --------------------------------------------------------------------
@@ -613,7 +643,7 @@ size_t oxc_sum_squares_workspace_size(const oxc_view* views, int32_t count) {
   for (int i = 0; i < count; ++i) {
     int64_t n = 1;
     for (int d = 0; d < views[i].ndim; ++d) n *= views[i].shape[d];
-    parts += (n + (1 << 20) - 1) >> 20;
+    parts += (n + (1 << 18) - 1) >> 18;
   }
   return (size_t)std::max<int64_t>(parts, 1) * sizeof(double) + 256;
 }
@@ -625,7 +655,7 @@ oxc_status oxc_sum_squares(const oxc_view* views, int32_t count, double* out, vo
   if (!out) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: sum_squares: null output");
   MultiViews mv;
   mv.count = count;
-  mv.chunk = 1 << 20;
+  mv.chunk = 1 << 18;
   mv.first_part[0] = 0;
   for (int i = 0; i < count; ++i) {
     oxc_status st = check_view(&views[i], "sum_squares");
@@ -646,7 +676,7 @@ oxc_status oxc_sum_squares(const oxc_view* views, int32_t count, double* out, vo
     oxc_status st = check_launch("oxc_sum_squares");
     if (st) return st;
   }
-  sumsq_multi_stage2<<<1, 32, 0, s>>>(parts, ps, out);
+  sumsq_multi_stage2<<<1, 256, 0, s>>>(parts, ps, out);
   return check_launch("oxc_sum_squares (finish)");
 }
 

@@ -169,11 +169,169 @@ __global__ void __launch_bounds__(256) swiglu_bwd_kernel(View2 g, View2 u, View2
   }
 }
 
-__global__ void sumsq_parts_finish(const double* __restrict__ parts, int n, double* __restrict__ out) {
-  if (threadIdx.x == 0 && blockIdx.x == 0) {
-    double a = 0.0;
-    for (int i = 0; i < n; ++i) a += parts[i];
-    out[0] = a;
+// Fixed-order block reduction of the per-CTA partials (thread t adds parts
+// t, t+256, ... in order; then the warp/block tree of block_sum).
+__global__ void __launch_bounds__(256) sumsq_parts_finish(const double* __restrict__ parts, int n,
+                                                          double* __restrict__ out) {
+  __shared__ double red[33];
+  double a = 0.0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) a += parts[i];
+  const double t = block_sum(a, red);
+  if (threadIdx.x == 0) out[0] = t;
+}
+
+// ---- streaming kernels: row-major u/dh/outputs, gate row- or column-major ----
+//
+// A CTA owns 32 tokens (rows) and walks the features in chunks of 256.  The
+// gate chunk [32 x 256] is staged in shared memory as st[token][feature]
+// (row pitch 257 floats): a column-major gate is read 128 bytes per feature
+// (lanes over tokens), a row-major one 128 bytes per token; writes and reads of
+// the tile are bank-conflict free.  Every row-major operand (u, dh, h, dg, du)
+// is streamed straight between HBM and registers in 1 KB row segments: warp w
+// handles tokens w, w+8, w+16, w+24 and lane l features l + 32k of the chunk.
+constexpr int kSwTok = 32, kSwChunk = 256, kSwPitch = kSwChunk + 1;
+
+__device__ __forceinline__ void stage_gate(float* st, const View2& g, int64_t r0, int64_t c0,
+                                           int64_t R, int64_t C) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (g.sr == 1) {  // column-major: lanes over tokens, one feature row per step
+#pragma unroll 8
+    for (int f = warp; f < kSwChunk; f += 8) {
+      const int64_t r = r0 + lane, c = c0 + f;
+      st[lane * kSwPitch + f] = (r < R && c < C) ? __ldg(g.p + r + c * g.sc) : 0.0f;
+    }
+  } else {  // row-major (or any): lanes over features
+#pragma unroll 4
+    for (int t = warp; t < kSwTok; t += 8) {
+      const int64_t r = r0 + t;
+#pragma unroll
+      for (int k = 0; k < kSwChunk / 32; ++k) {
+        const int64_t c = c0 + lane + 32 * k;
+        st[t * kSwPitch + lane + 32 * k] = (r < R && c < C) ? __ldg(g.p + r * g.sr + c * g.sc) : 0.0f;
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256, 3) swiglu_fwd_stream_kernel(
+    View2 g, const float* __restrict__ u, float* __restrict__ h, int64_t R, int64_t C,
+    float* __restrict__ row_sum, float* __restrict__ row_max, float* __restrict__ row_argmax) {
+  __shared__ float st[kSwTok * kSwPitch];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const bool rows_out = row_sum || row_max || row_argmax;
+  for (int64_t r0 = (int64_t)blockIdx.x * kSwTok; r0 < R; r0 += (int64_t)gridDim.x * kSwTok) {
+    float sum[4], mx[4];
+    int am[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { sum[i] = 0.0f; mx[i] = 0.0f; am[i] = -1; }
+    for (int64_t c0 = 0; c0 < C; c0 += kSwChunk) {
+      __syncthreads();  // previous chunk's tile fully read
+      stage_gate(st, g, r0, c0, R, C);
+      __syncthreads();
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int t = warp + 8 * i;
+        const int64_t r = r0 + t;
+        if (r >= R) continue;
+        float uv[kSwChunk / 32];
+#pragma unroll
+        for (int k = 0; k < kSwChunk / 32; ++k) {
+          const int64_t c = c0 + lane + 32 * k;
+          uv[k] = (u && c < C) ? ld_stream(u + r * C + c) : 1.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < kSwChunk / 32; ++k) {
+          const int64_t c = c0 + lane + 32 * k;
+          if (c < C) {
+            const float gv = st[t * kSwPitch + lane + 32 * k];
+            const float s1 = __fmul_rn(gv, sigmoid_ref(gv));
+            const float hv = u ? __fmul_rn(s1, uv[k]) : s1;
+            st_stream(h + r * C + c, hv);
+            if (rows_out) {
+              sum[i] = __fadd_rn(sum[i], hv);
+              if (!isnan(hv) && (am[i] < 0 || hv > mx[i])) { mx[i] = hv; am[i] = (int)c; }
+            }
+          }
+        }
+      }
+    }
+    if (rows_out) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float s = sum[i], m = mx[i];
+        int a = am[i];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+          s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
+          const float om = __shfl_xor_sync(0xffffffffu, m, off);
+          const int oa = __shfl_xor_sync(0xffffffffu, a, off);
+          if (oa >= 0 && (a < 0 || om > m || (om == m && oa < a))) { m = om; a = oa; }
+        }
+        const int64_t r = r0 + warp + 8 * i;
+        if (lane == 0 && r < R) {
+          if (row_sum) row_sum[r] = s;
+          if (row_max) row_max[r] = a < 0 ? -INFINITY : m;
+          if (row_argmax) {
+            const float h0 = h[r * C];  // written by this lane (feature 0, k = 0)
+            row_argmax[r] = (C > 0 && isnan(h0)) ? 0.0f : (float)(a < 0 ? 0 : a);
+          }
+        }
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) swiglu_bwd_stream_kernel(
+    View2 g, const float* __restrict__ u, const float* __restrict__ dh, float* __restrict__ dg,
+    float* __restrict__ du, int64_t R, int64_t C, double* __restrict__ sumsq_parts) {
+  __shared__ float st[kSwTok * kSwPitch];
+  __shared__ double red[33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  double sq = 0.0;
+  for (int64_t r0 = (int64_t)blockIdx.x * kSwTok; r0 < R; r0 += (int64_t)gridDim.x * kSwTok) {
+    for (int64_t c0 = 0; c0 < C; c0 += kSwChunk) {
+      __syncthreads();
+      stage_gate(st, g, r0, c0, R, C);
+      __syncthreads();
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int t = warp + 8 * i;
+        const int64_t r = r0 + t;
+        if (r >= R) continue;
+        float uv[kSwChunk / 32], dv[kSwChunk / 32];
+#pragma unroll
+        for (int k = 0; k < kSwChunk / 32; ++k) {
+          const int64_t c = c0 + lane + 32 * k;
+          uv[k] = (u && c < C) ? ld_stream(u + r * C + c) : 1.0f;
+          dv[k] = c < C ? ld_stream(dh + r * C + c) : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < kSwChunk / 32; ++k) {
+          const int64_t c = c0 + lane + 32 * k;
+          if (c < C) {
+            const float gv = st[t * kSwPitch + lane + 32 * k];
+            const float s = sigmoid_ref(gv);
+            const float s1 = __fmul_rn(gv, s);
+            float tt = dv[k];
+            if (u) {
+              const float duv = __fmul_rn(dv[k], s1);
+              st_stream(du + r * C + c, duv);
+              sq += (double)duv * (double)duv;
+              tt = __fmul_rn(dv[k], uv[k]);
+            }
+            const float term1 = __fmul_rn(tt, s);
+            const float dsig = __fmul_rn(s, __fsub_rn(1.0f, s));
+            const float dgv = __fadd_rn(term1, __fmul_rn(__fmul_rn(tt, gv), dsig));
+            st_stream(dg + r * C + c, dgv);
+            sq += (double)dgv * (double)dgv;
+          }
+        }
+      }
+    }
+  }
+  if (sumsq_parts) {
+    const double tot = block_sum(sq, red);
+    if (threadIdx.x == 0) sumsq_parts[blockIdx.x] = tot;
   }
 }
 
@@ -202,6 +360,14 @@ static int64_t swiglu_ctas(int64_t R) {
   return std::max<int64_t>(1, std::min<int64_t>(tiles, (int64_t)sm_count() * 8));
 }
 
+// The streaming kernels need u (if any) dense row-major and the gate row- or
+// column-major.
+static bool stream_ok(const View2& g, const View2& u, int64_t C) {
+  const bool g_ok = g.sc == 1 || g.sr == 1;
+  const bool u_ok = !u.p || (u.sc == 1 && u.sr == C);
+  return g_ok && u_ok;
+}
+
 }  // namespace oxc
 
 using namespace oxc;
@@ -216,8 +382,14 @@ oxc_status oxc_swiglu_fwd(const oxc_view* gate, const oxc_view* up, float* h, fl
   if (st || (st = view2(up, "up", &R, &C, &u, false))) return st;
   if (R == 0 || C == 0) return OXC_OK;
   if (!h || !g.p) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: swiglu: null pointer");
-  swiglu_fwd_kernel<<<(unsigned)swiglu_ctas(R), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      g, u, h, R, C, row_sum, row_max, row_argmax);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (stream_ok(g, u, C)) {
+    swiglu_fwd_stream_kernel<<<(unsigned)swiglu_ctas(R), 256, 0, s>>>(g, u.p, h, R, C, row_sum,
+                                                                      row_max, row_argmax);
+  } else {
+    swiglu_fwd_kernel<<<(unsigned)swiglu_ctas(R), 256, 0, s>>>(g, u, h, R, C, row_sum, row_max,
+                                                               row_argmax);
+  }
   return check_launch("oxc_swiglu_fwd");
 }
 
@@ -253,10 +425,13 @@ oxc_status oxc_swiglu_bwd(const oxc_view* gate, const oxc_view* up, const oxc_vi
                   oxc_swiglu_bwd_workspace_size(R, C), workspace_bytes);
     parts = reinterpret_cast<double*>((reinterpret_cast<uintptr_t>(workspace) + 15) & ~uintptr_t(15));
   }
-  swiglu_bwd_kernel<<<(unsigned)ctas, 256, 0, s>>>(g, u, d, dgate, dup, R, C, parts);
+  if (stream_ok(g, u, C) && d.sc == 1 && d.sr == C)
+    swiglu_bwd_stream_kernel<<<(unsigned)ctas, 256, 0, s>>>(g, u.p, d.p, dgate, dup, R, C, parts);
+  else
+    swiglu_bwd_kernel<<<(unsigned)ctas, 256, 0, s>>>(g, u, d, dgate, dup, R, C, parts);
   st = check_launch("oxc_swiglu_bwd");
   if (st || !sumsq) return st;
-  sumsq_parts_finish<<<1, 32, 0, s>>>(parts, (int)ctas, sumsq);
+  sumsq_parts_finish<<<1, 256, 0, s>>>(parts, (int)ctas, sumsq);
   return check_launch("oxc_swiglu_bwd (sumsq)");
 }
 
