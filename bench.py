@@ -301,8 +301,8 @@ class LnGelu(Workload):
 
     def exchange(self):
         if self.world > 1:
-            import torch.distributed as dist
-            dist.all_reduce(self.dwdb)
+            from oxitorch_b200 import sharded
+            sharded.allreduce_sum_(self.dwdb)
 
     def e2e_io(self):
         return [self.x, self.dy], [self.y, self.dx, self.dwdb]
@@ -355,8 +355,8 @@ class Rms(Workload):
 
     def exchange(self):
         if self.world > 1:
-            import torch.distributed as dist
-            dist.all_reduce(self.dw)
+            from oxitorch_b200 import sharded
+            sharded.allreduce_sum_(self.dw)
 
     def e2e_io(self):
         return [self.x, self.dy], [self.y, self.dx, self.dw]
@@ -408,8 +408,8 @@ class CrossEntropy(Workload):
 
     def exchange(self):
         if self.world > 1:
-            import torch.distributed as dist
-            dist.all_reduce(self.loss)
+            from oxitorch_b200 import sharded
+            sharded.allreduce_sum_(self.loss)
 
     def e2e_io(self):
         return [self.x], [self.loss, self.dx]
@@ -466,8 +466,8 @@ class Embedding(Workload):
 
     def exchange(self):
         if self.world > 1:
-            import torch.distributed as dist
-            dist.all_reduce(self.dtable)
+            from oxitorch_b200 import sharded
+            sharded.allreduce_sum_(self.dtable)
 
     def e2e_io(self):
         return [self.dout], [self.out, self.dtable]
@@ -548,9 +548,8 @@ class MlpBlock(Workload):
 
     def exchange(self):
         if self.world > 1:
-            import torch.distributed as dist
-            dist.all_reduce(self.dw)
-            dist.all_reduce(self.sq)
+            from oxitorch_b200 import sharded
+            sharded.allreduce_sum_(self.dw, self.sq)
 
     def e2e_io(self):
         return ([self.x, self.gate_buf, self.up, self.dy, self.dh],

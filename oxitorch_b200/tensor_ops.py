@@ -170,9 +170,15 @@ def clip_grad_norm_(grads, max_norm, norm_type=2.0):
     total = total ** 0.5
     scale = max_norm / (total + 1e-6)
     if scale < 1.0:
-        L = N.load()
         for g in grads:
-            v = N.make_view(g)
-            N.check(L.oxc_binary_scalar(2, ctypes.byref(v), float(scale), 0, ctypes.byref(v),
-                                        _stream()), "clip_grad_norm_")
+            scale_(g, scale)
     return total
+
+
+def scale_(g, scale):
+    """g *= scale in place (the registry's mul with a scalar operand)."""
+    _require_cuda_f32("tensor", g)
+    v = N.make_view(g)
+    N.check(N.load().oxc_binary_scalar(2, ctypes.byref(v), float(scale), 0, ctypes.byref(v),
+                                       _stream()), "scale_")
+    return g

@@ -1,0 +1,206 @@
+"""Row/token sharding on the GPU: the kernels' shard parameters, emulated on
+one device, and (with two or more GPUs visible) the ``sharded`` layers on real
+NCCL ranks against the single-GPU result.
+
+Sharded results follow the single-GPU rules: every row-local output (and the
+cross-entropy VJP, whose scale is g / M_global on every rank) is bit-exact;
+sums over rows that the shards regroup (weight gradients, the loss) are
+compared at rtol 1e-5.
+"""
+
+import os
+import socket
+import traceback
+from datetime import timedelta
+
+import numpy as np
+import pytest
+
+from parity import assert_bitexact, assert_close
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _dev(a, device="cuda"):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(device)
+
+
+def _host(t):
+    return t.detach().cpu().numpy()
+
+
+def test_cross_entropy_row_shards_match_full():
+    """Shards run with the global row count: the per-shard losses sum to the
+    full loss and the per-shard VJPs are the full VJP's rows, bit for bit."""
+    from oxitorch_b200 import functional as F
+    from oxitorch_b200 import sharded as S
+    rng = np.random.default_rng(21)
+    m, c = 1037, 5003
+    logits = (3 * rng.standard_normal((m, c))).astype(np.float32)
+    targets = rng.integers(-c, c, m)
+    g = _dev(np.array([0.75], np.float32))
+    loss, rmax, rsum, _, t, _ = F.cross_entropy_fwd(_dev(logits), _dev(targets))
+    full_d = _host(F.cross_entropy_bwd(_dev(logits), t, rmax, rsum, g))
+    parts = []
+    for r in range(3):
+        lo, hi = S.shard_range(m, r, 3)
+        sl, smax, ssum, _, st, _ = F.cross_entropy_fwd(_dev(logits[lo:hi]), _dev(targets[lo:hi]),
+                                                       total_rows=m)
+        parts.append(float(_host(sl)[0]))
+        d = _host(F.cross_entropy_bwd(_dev(logits[lo:hi]), st, smax, ssum, g, total_rows=m))
+        assert_bitexact(d, full_d[lo:hi], f"cross-entropy VJP rows of shard {r}")
+    assert_close(np.array([sum(parts)]), _host(loss), rtol=1e-5, atol=0, what="sum of shard losses")
+
+
+def test_sharded_layers_single_process():
+    """Without a process group the sharded layers are the single-GPU layers."""
+    import torch
+    from oxitorch_b200 import functional as F
+    from oxitorch_b200 import sharded as S
+    from oxitorch_b200 import tensor_ops as T
+    rng = np.random.default_rng(22)
+    logits = _dev(rng.standard_normal((64, 300)).astype(np.float32))
+    targets = [int(v) for v in rng.integers(0, 300, 64)]
+    a = logits.clone().requires_grad_()
+    b = logits.clone().requires_grad_()
+    la, lb = S.cross_entropy(a, targets), F.cross_entropy(b, targets)
+    la.backward()
+    lb.backward()
+    assert_bitexact(_host(la), _host(lb), "loss")
+    assert_bitexact(_host(a.grad), _host(b.grad), "dlogits")
+    table = _dev(rng.standard_normal((50, 16)).astype(np.float32))
+    ids = [3, -1, 49, 3, 0]
+    ta, tb = table.clone().requires_grad_(), table.clone().requires_grad_()
+    oa, ob = S.embedding(ids, ta, 50), F.embedding(ids, tb)
+    assert_bitexact(_host(oa), _host(ob), "lookup")
+    dout = _dev(rng.standard_normal((5, 16)).astype(np.float32))
+    oa.backward(dout)
+    ob.backward(dout)
+    assert_bitexact(_host(ta.grad), _host(tb.grad), "dtable")
+    g1 = _dev(rng.standard_normal((33, 7)).astype(np.float32))
+    g2 = g1.clone()
+    n1 = S.clip_grad_norm_([g1], 0.5)
+    n2 = T.clip_grad_norm_([g2], 0.5)
+    assert n1 == n2
+    assert_bitexact(_host(g1), _host(g2), "clipped gradient")
+    with pytest.raises(ValueError):
+        S.embedding(ids, table[:10], 50)
+
+
+# ---- real NCCL ranks ---------------------------------------------------------------------
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _nccl_rank(rank, world, port, q):
+    import sys
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    try:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+        try:
+            _nccl_body(rank, world, dev)
+            torch.cuda.synchronize()
+            dist.barrier()
+            q.put(("ok", rank, ""))
+        finally:
+            dist.destroy_process_group()
+    except BaseException:
+        q.put(("fail", rank, traceback.format_exc()))
+
+
+def _nccl_body(rank, world, dev):
+    import torch
+    from oxitorch_b200 import functional as F
+    from oxitorch_b200 import sharded as S
+    rng = np.random.default_rng(23)  # the same data on every rank
+    # LayerNorm+GELU: row shards + weight-gradient sync
+    m, c = 4099, 1024
+    x = rng.standard_normal((m, c)).astype(np.float32)
+    w = rng.uniform(0.5, 1.5, c).astype(np.float32)
+    b = (0.1 * rng.standard_normal(c)).astype(np.float32)
+    dy = rng.standard_normal((m, c)).astype(np.float32)
+    lo, hi = S.shard_range(m, rank, world)
+    wf, bf = _dev(w, dev).requires_grad_(), _dev(b, dev).requires_grad_()
+    F.layer_norm_gelu(_dev(x, dev), wf, bf).backward(_dev(dy, dev))
+    ws, bs = _dev(w, dev).requires_grad_(), _dev(b, dev).requires_grad_()
+    xs = _dev(x[lo:hi], dev).requires_grad_()
+    ys = F.layer_norm_gelu(xs, ws, bs)
+    ys.backward(_dev(dy[lo:hi], dev))
+    S.sync_grads_([ws, bs])
+    yf = F.layer_norm_gelu(_dev(x, dev), wf.detach(), bf.detach())
+    assert_bitexact(_host(ys), _host(yf)[lo:hi], "layer_norm_gelu rows")
+    assert_close(_host(ws.grad), _host(wf.grad), rtol=1e-5, atol=1e-4, what="synced dweight")
+    assert_close(_host(bs.grad), _host(bf.grad), rtol=1e-5, atol=1e-4, what="synced dbias")
+    # cross-entropy: the global mean on every rank, VJP rows bit-exact
+    m, c = 2053, 3001
+    logits = (2 * rng.standard_normal((m, c))).astype(np.float32)
+    targets = rng.integers(0, c, m)
+    lo, hi = S.shard_range(m, rank, world)
+    full = _dev(logits, dev).requires_grad_()
+    lf = F.cross_entropy(full, [int(t) for t in targets])
+    lf.backward()
+    part = _dev(logits[lo:hi], dev).requires_grad_()
+    ls = S.cross_entropy(part, [int(t) for t in targets[lo:hi]])
+    ls.backward()
+    assert_close(_host(ls).reshape(1), _host(lf).reshape(1), rtol=1e-5, atol=0, what="global loss")
+    assert_bitexact(_host(part.grad), _host(full.grad)[lo:hi], "cross-entropy VJP rows")
+    # vocab-sharded embedding: the lookup is exact on every rank; each rank's
+    # dtable is its rows of the full dtable (ids here occur <= 128 times)
+    v, d = 1000, 256
+    table = rng.standard_normal((v, d)).astype(np.float32)
+    ids = [int(i) for i in rng.integers(-v, v, 3000)]
+    dout = rng.standard_normal((len(ids), d)).astype(np.float32)
+    off, rows = S.vocab_shard(v, rank, world)
+    shard = _dev(table[off:off + rows], dev).requires_grad_()
+    out = S.embedding(ids, shard, v)
+    tf = _dev(table, dev).requires_grad_()
+    of = F.embedding(ids, tf)
+    assert_bitexact(_host(out), _host(of), "vocab-sharded lookup")
+    out.backward(_dev(dout, dev))
+    of.backward(_dev(dout, dev))
+    assert_bitexact(_host(shard.grad), _host(tf.grad)[off:off + rows], "dtable shard")
+    # global sum of squares over row shards
+    gsh = _dev(x[lo % 100:lo % 100 + 50], dev)
+    tot = S.sum_squares([gsh])
+    parts = [None] * world
+    import torch.distributed as dist
+    dist.all_gather_object(parts, float(np.sum(x[lo % 100:lo % 100 + 50].astype(np.float64) ** 2)))
+    assert_close(np.array([tot.item()]), np.array([sum(parts)]), rtol=1e-9, atol=0,
+                 what="global sum of squares")
+
+
+def test_nccl_two_ranks():
+    import torch
+    world = min(torch.cuda.device_count(), 4)
+    if world < 2:
+        pytest.skip("needs two or more GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_nccl_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = []
+    try:
+        for _ in procs:
+            out.append(q.get(timeout=300))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    fails = [o for o in out if o[0] != "ok"]
+    assert not fails, "\n".join(f"rank {o[1]}:\n{o[2]}" for o in fails)
