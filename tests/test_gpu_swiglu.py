@@ -80,6 +80,63 @@ def test_swiglu_vs_oracle_layouts(oracle, m, n, transposed_gate):
     assert abs(float(_host(sq)) - want_sq) <= 1e-12 * want_sq + 1e-30
 
 
+def _gate_view(g, layout):
+    """Device view of g [m, n] in one of the layouts the kernels dispatch on."""
+    import torch
+    m, n = g.shape
+    if layout == "row_strided":      # rows of a wider buffer: row stride n + 12
+        buf = torch.zeros(m, n + 12, device="cuda")
+        buf[:, :n] = _dev(g)
+        return buf[:, :n]
+    if layout == "col_strided":      # transposed view of a taller buffer: stride m + 4
+        buf = torch.zeros(n, m + 4, device="cuda")
+        buf[:, :m] = _dev(np.ascontiguousarray(g.T))
+        return buf[:, :m].t()
+    if layout == "misaligned":       # base 4 bytes past a 16-byte boundary
+        buf = torch.zeros(m * n + 1, device="cuda")
+        buf[1:] = _dev(g.reshape(-1))
+        return buf[1:].view(m, n)
+    raise ValueError(layout)
+
+
+@pytest.mark.parametrize("with_up", [True, False])
+@pytest.mark.parametrize("layout", ["row_strided", "col_strided", "misaligned"])
+def test_swiglu_gate_layouts_many_strips(oracle, layout, with_up):
+    """More 32-token strips than SMs (CTAs loop), a feature count that is not a
+    multiple of the 128-feature tile, strided and misaligned gates, silu-only,
+    and NaNs: h[0, 0] NaN (argmax 0, max ignores it) and a NaN mid-row."""
+    from oxitorch_b200 import functional as F
+    rng = np.random.default_rng(31)
+    m, n = 4800, 260
+    g = rng.standard_normal((m, n), dtype=np.float32) * np.float32(3)
+    g[0, 0] = np.nan
+    g[7, 100] = np.nan
+    u = rng.standard_normal((m, n), dtype=np.float32) if with_up else None
+    dh = rng.standard_normal((m, n), dtype=np.float32)
+    outs, budgets = _oracle_swiglu(oracle, g, u, dh)
+    gd = _gate_view(g, layout)
+    ud = _dev(u) if with_up else None
+    h, s, mx, am = F.swiglu_fwd(gd, ud, row_stats=True)
+    res = F.swiglu_bwd(gd, ud, _dev(dh), sumsq=True)
+    assert_close(_host(h), outs[0], atol=ATOL + budgets[0], what="h")
+    assert_close(_host(res[0]), outs[1], atol=ATOL + budgets[1], what="dg")
+    if with_up:
+        assert_close(_host(res[1]), outs[2], atol=ATOL + budgets[2], what="du")
+    hh = _host(h)
+    assert_bitexact(_host(mx), oracle.t_reduce("max", hh, 1, False), "row max")
+    assert_bitexact(_host(am), oracle.t_reduce("argmax", hh, 1, False), "row argmax")
+    assert _host(am)[0] == 0
+    fin = np.isfinite(hh).all(1)
+    want_s = oracle.t_reduce("sum", hh, 1, False)
+    assert np.isnan(_host(s)[~fin]).all()
+    assert_close(_host(s)[fin], want_s[fin], atol=ATOL * np.abs(hh[fin]).sum(1) + 1e-6,
+                 what="row sum")
+    parts = [_host(res[0])] + ([_host(res[1])] if with_up else [])
+    want_sq = sum(float(np.nansum(p.astype(np.float64) ** 2)) for p in parts)
+    got_sq = float(_host(res[-1]))
+    assert np.isnan(got_sq) or abs(got_sq - want_sq) <= 1e-12 * want_sq
+
+
 def test_silu_autograd():
     from oxitorch_b200 import functional as F
     rng = np.random.default_rng(4)
