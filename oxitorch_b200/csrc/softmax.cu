@@ -17,7 +17,8 @@
 //
 // Kernels, all HBM-bound (no contraction):
 //   softmax_fwd/bwd: one CTA per row, two passes; pass 1 reads the row with
-//     L2-allocating 128-bit loads (online max + rescaled sum, or plain sums),
+//     L2-allocating 128-bit loads (online max + rescaled sum over 16-value
+//     chunks, the sum's terms from ex2.approx -- exp_rel -- or plain sums),
 //     pass 2 re-reads it from L2 and writes -- DRAM sees one read + one write.
 //   ce_fwd: one CTA per row, one online pass; writes per-row (max, sum of
 //     exp, -log p_target) and never materialises a full-size tensor.
@@ -36,16 +37,6 @@ struct MaxSum {
   float m;
   float s;
 };
-
-// Online (max, sum exp(x - max)) update with one element.
-__device__ __forceinline__ void ms_push(MaxSum& a, float x) {
-  if (x > a.m) {
-    a.s = a.s * expf(a.m - x) + 1.0f;
-    a.m = x;
-  } else {
-    a.s += expf(x - a.m);
-  }
-}
 
 __device__ __forceinline__ MaxSum ms_merge(MaxSum a, MaxSum b) {
   const float m = fmaxf(a.m, b.m);
@@ -86,32 +77,93 @@ __device__ __forceinline__ MaxSum block_maxsum(MaxSum v, float* scratch) {
   return {scratch[32], scratch[65]};
 }
 
+// e^d for d = x - m <= 0 as 2^(d * log2 e) with the ex2.approx instruction
+// (flush-to-zero: results below 2^-126 of the row maximum's term are 0).  The
+// subtraction comes first, so the terms near the maximum -- the ones that make
+// up the sum -- see only ex2's own error; farther terms carry an extra
+// |d| * 2^-23 relative error from the rounded argument, on values at most
+// e^d of the largest term.  Used only for the row sums of exp; outputs that are
+// themselves exponentials use expf.
+__device__ __forceinline__ float exp_rel(float d) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d * 1.44269504088896341f));
+  return r;
+}
+
+// Folds n values into the running (max, sum): the NaN-ignoring max of the
+// values first, one rescale of the sum when the max grows, then n terms.
+// While the max is still -inf the base is 0, so a -inf value adds 0 and a NaN
+// adds NaN; a row whose final max is -inf gets the reference's NaN sum at the
+// end (row_maxsum).
+// With MIN the running minimum is folded into *mn as well (NaN-ignoring).
+template <int N, bool MIN = false>
+__device__ __forceinline__ void ms_fold(MaxSum& a, const float (&v)[N], float* mn = nullptr) {
+  float mm = a.m;
+#pragma unroll
+  for (int i = 0; i < N; ++i) mm = fmaxf(mm, v[i]);
+  if constexpr (MIN) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) *mn = fminf(*mn, v[i]);
+  }
+  if (mm > a.m) {
+    a.s *= exp_rel(a.m - mm);
+    a.m = mm;
+  }
+  const float base = mm == -INFINITY ? 0.0f : mm;
+  float t = 0.0f;
+#pragma unroll
+  for (int i = 0; i < N; ++i) t += exp_rel(v[i] - base);
+  a.s += t;
+}
+
 // Row statistics (max, sum exp(x - max)) with 128-bit (VW = 4) or scalar
-// loads; `keep` loads allocate in L2 so a second pass hits it.
-template <int VW>
-__device__ __forceinline__ MaxSum row_maxsum(const float* xr, int cols, float* scratch) {
+// loads; `keep` loads allocate in L2 so a second pass hits it.  A row whose
+// max is -inf (all -inf and/or NaN) has sum NaN, as exp(-inf - -inf) is NaN.
+// With MIN, *row_min (every thread) gets the row's NaN-ignoring minimum.
+template <int VW, bool MIN = false>
+__device__ __forceinline__ MaxSum row_maxsum(const float* xr, int cols, float* scratch,
+                                             float* row_min = nullptr) {
   MaxSum a{-INFINITY, 0.0f};
+  float mn = INFINITY;
   if constexpr (VW == 4) {
     const float4* x4 = reinterpret_cast<const float4*>(xr);
     const int nvec = cols >> 2;
     int v = threadIdx.x;
     for (; v + 3 * (int)blockDim.x < nvec; v += 4 * blockDim.x) {
-      float4 q[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) q[u] = ld_keep(x4 + v + u * blockDim.x);
+      float q[16];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        ms_push(a, q[u].x); ms_push(a, q[u].y); ms_push(a, q[u].z); ms_push(a, q[u].w);
+        const float4 t = ld_keep(x4 + v + u * blockDim.x);
+        q[4 * u] = t.x; q[4 * u + 1] = t.y; q[4 * u + 2] = t.z; q[4 * u + 3] = t.w;
       }
+      ms_fold<16, MIN>(a, q, &mn);
     }
     for (; v < nvec; v += blockDim.x) {
-      const float4 q = ld_keep(x4 + v);
-      ms_push(a, q.x); ms_push(a, q.y); ms_push(a, q.z); ms_push(a, q.w);
+      const float4 t = ld_keep(x4 + v);
+      const float q[4] = {t.x, t.y, t.z, t.w};
+      ms_fold<4, MIN>(a, q, &mn);
     }
   } else {
-    for (int c = threadIdx.x; c < cols; c += blockDim.x) ms_push(a, ld_keep(xr + c));
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+      const float q[1] = {ld_keep(xr + c)};
+      ms_fold<1, MIN>(a, q, &mn);
+    }
   }
-  return block_maxsum(a, scratch);
+  MaxSum r = block_maxsum(a, scratch);
+  if (r.m == -INFINITY) r.s = NAN;
+  if constexpr (MIN) {
+    // scratch[66..98]: per-warp minima (block_maxsum's last barrier orders
+    // this after its reads)
+    mn = warp_min(mn);
+    if ((threadIdx.x & 31) == 0) scratch[66 + (threadIdx.x >> 5)] = mn;
+    __syncthreads();
+    const int nw = (blockDim.x + 31) >> 5;
+    float t = INFINITY;
+    for (int w = 0; w < nw; ++w) t = fminf(t, scratch[66 + w]);
+    *row_min = t;
+    __syncthreads();
+  }
+  return r;
 }
 
 template <int VW, bool LOG>
@@ -224,16 +276,26 @@ __global__ void __launch_bounds__(512) ce_fwd_kernel(const float* __restrict__ x
                                                      float* __restrict__ row_sum,
                                                      float* __restrict__ row_nll, int64_t rows,
                                                      int cols, int32_t* err) {
-  __shared__ float scratch[66];
+  __shared__ float scratch[66 + 33];
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     const float* xr = x + row * (int64_t)cols;
-    const MaxSum st = row_maxsum<VW>(xr, cols, scratch);
+    float mn;
+    const MaxSum st = row_maxsum<VW, true>(xr, cols, scratch, &mn);
+    const int64_t t = resolve_target(targets[row], cols);
+    // The reference picks ls_t through a one-hot product summed over the row,
+    // and 0 * -inf is NaN: a -inf logit anywhere but the target makes the
+    // picked value NaN.  Rows without -inf skip the check (mn, t are uniform).
+    int other_ninf = 0;
+    if (mn == -INFINITY && t >= 0) {
+      int f = 0;
+      for (int c = threadIdx.x; c < cols; c += blockDim.x) f |= (c != t && xr[c] == -INFINITY);
+      other_ninf = __syncthreads_or(f);
+    }
     if (threadIdx.x == 0) {
-      const int64_t t = resolve_target(targets[row], cols);
       float nll = NAN;
       if (t < 0) {
         record_bad_index(err, targets[row], cols);
-      } else {
+      } else if (!other_ninf) {
         // ls_t = (x_t - m) - log(s); the picked value is -ls_t
         nll = -((xr[t] - st.m) - logf(st.s));
       }

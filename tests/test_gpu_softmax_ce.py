@@ -152,6 +152,64 @@ def test_cross_entropy_reference_values():
     assert np.allclose(dx, g, rtol=1e-4, atol=1e-6)
 
 
+def _nonfinite_rows(n, seed):
+    """Rows with -inf / +inf / NaN placed the way the reference's edge cases
+    differ: leading -inf then finite values (the online max starts at -inf),
+    all -inf, NaN, -inf only at the target (+inf loss), -inf elsewhere too
+    (NaN loss: the one-hot product 0 * -inf), +inf, a dominated row and a
+    plain row.  Returns logits, targets, upstream gradient."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((8, n)).astype(np.float32)
+    t = rng.integers(0, n, 8)
+    x[0, :2] = -np.inf
+    t[0] = n - 1
+    x[1, :] = -np.inf
+    x[2, n // 2] = np.nan
+    t[3] = 1
+    x[3, 1] = -np.inf
+    t[4] = 0
+    x[4, 0] = -np.inf
+    x[4, n - 1] = -np.inf
+    x[5, n // 3] = np.inf
+    x[6, :] = -30.0
+    x[6, t[6]] = 0.0
+    dy = rng.standard_normal((8, n)).astype(np.float32)
+    return x, t, dy
+
+
+@pytest.mark.parametrize("n", [1000, 37])
+@pytest.mark.parametrize("log", [False, True])
+def test_softmax_nonfinite_rows(oracle, n, log):
+    x, _, dy = _nonfinite_rows(n, n)
+    ref, budget = _oracle_softmax(oracle, x, dy, log)
+    _check_softmax(_dev_softmax(x, dy, log), ref, budget, n)
+
+
+@pytest.mark.parametrize("n", [1000, 37])
+def test_cross_entropy_nonfinite_rows(oracle, n):
+    """Per-row values against the reference graph's picked sum (one-hot
+    product), the mean, and a finite VJP on the rows the reference keeps
+    finite."""
+    from oxitorch_b200 import functional as F
+    x, t, _ = _nonfinite_rows(n, n + 1)
+    loss, rmax, rsum, nll, tt, flag = F.cross_entropy_fwd(_dev(x), [int(v) for v in t])
+    assert int(flag.cpu()[0]) == 0
+    onehot = np.zeros_like(x)
+    onehot[np.arange(8), t] = 1.0
+    ls = oracle.log_softmax(oracle.from_numpy(x), -1)
+    picked = (oracle.from_numpy(onehot) * ls).sum(-1).numpy()
+    want = -picked
+    got = _host(nll)
+    assert np.array_equal(np.isnan(got), np.isnan(want)), (got, want)
+    assert np.array_equal(np.isposinf(got), np.isposinf(want)), (got, want)
+    fin = np.isfinite(want)
+    assert_close(got[fin], want[fin], rtol=RTOL, atol=1e-5, what="row nll")
+    assert np.isnan(_host(loss)[0])
+    (_, dref), (_, bdx) = _oracle_ce(oracle, x, t)
+    dx = _host(F.cross_entropy_bwd(_dev(x), tt, rmax, rsum))
+    assert_close(dx * 8, dref * 8, rtol=RTOL, atol=ATOL + bdx * 8, what="M * dlogits")
+
+
 def test_cross_entropy_errors():
     import torch
     from oxitorch_b200 import functional as F
