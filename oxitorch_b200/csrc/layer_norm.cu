@@ -14,12 +14,17 @@
 //   dx   = gc - (sum_row gc) / cols            (sub and mean VJPs, ops.rs:49-56, 340-349)
 // OXC_GRAD_EXACT: dx = inv * (gw - mean(gw) - xhat*mean(gw*xhat)), gw = g*w.
 //
-// Two implementations of each direction, same arithmetic:
+// Two implementations of each direction:
 //   *_pipe_kernel: rows with cols % 4 == 0 and 16-byte aligned tensors.  One
 //     persistent CTA per SM; a producer warp streams whole rows into a shared-
 //     memory ring with bulk copies (pipeline.cuh) while 16 consumer warps
-//     compute, so HBM stays busy during the arithmetic.
-//   *_kernel: any width up to 32768, register-resident rows, plain loads.
+//     compute, so HBM stays busy during the arithmetic.  Used for the VJP and
+//     for LayerNorm+GELU forward.
+//   *_kernel: any width up to 32768, register-resident rows, plain loads.  The
+//     forward takes mean and variance from one block reduction (a shifted
+//     one-pass sum, corrected by a second pass when the shift was poor); for the
+//     plain LayerNorm it runs
+//     persistent with the next row prefetched, which keeps HBM at copy speed.
 #include <math.h>
 
 #include <algorithm>
@@ -54,45 +59,122 @@ __device__ __forceinline__ float gelu_grad(float y, float g, const GeluConst& gc
   return g * gp;
 }
 
-template <int VW, int VPT, int MAXT, int ACT>
+// Block-wide sums of two values; every thread gets both.  Fixed order: the
+// warp butterfly, then each thread adds the per-warp partials in warp order.
+// scratch: >= 64 floats.
+__device__ __forceinline__ float2 block_sum2(float a, float b, float* scratch) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+  }
+  __syncthreads();  // earlier readers of scratch are done
+  if (lane == 0) {
+    scratch[warp] = a;
+    scratch[32 + warp] = b;
+  }
+  __syncthreads();
+  float2 t = make_float2(0.0f, 0.0f);
+  for (int w = 0; w < nw; ++w) {
+    t.x += scratch[w];
+    t.y += scratch[32 + w];
+  }
+  return t;
+}
+
+// Forward, register-resident rows.  PF: persistent CTAs that load their next
+// row into registers before working on the current one, so a row's loads are
+// in flight while the previous row is reduced and stored (the plain LayerNorm:
+// HBM-bound).  !PF: one row per CTA and fewer registers, so more CTAs share an
+// SM (LayerNorm+GELU: the activation's arithmetic needs the warps more than
+// the prefetch).
+//
+// Statistics in one block reduction: sums around a pilot K (the mean of the
+// row's first min(cols, 32) elements, which every warp computes on its own
+// with the same butterfly, so all get the same K):
+//   S1 = sum(x - K), S2 = sum((x - K)^2);  mean = K + S1/n;  var = S2/n - (S1/n)^2.
+// The rounding of S1 and the cancellation in var grow with |S1/n| / sigma;
+// when (S1/n)^2 > var (a pilot more than one standard deviation off the mean)
+// a second reduction takes the same two sums around the first estimate, which
+// is then within a tiny fraction of sigma of the mean, and corrects both mean
+// and variance.  Every row ends up as accurate as the reference's two-pass
+// formula, and x - mean is rounded once, as in the reference.
+template <int VW, int VPT, int MAXT, int ACT, bool PF>
 __global__ void __launch_bounds__(MAXT) ln_fwd_kernel(
     const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
     float* __restrict__ y, float* __restrict__ mean_out, float* __restrict__ rstd_out,
     int64_t rows, int cols, float eps, GeluConst gc) {
-  __shared__ float scratch[33];
-  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+  __shared__ float scratch[64];
+  const int lane = threadIdx.x & 31;
+  const int npilot = cols < 32 ? cols : 32;
+  const float n = (float)cols;
+  float nv[VPT][VW], np = 0.0f;
+  auto load_row = [&](int64_t row) {
     const float* xr = x + row * (int64_t)cols;
-    float v[VPT][VW];
-    float s = 0.0f;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int e = (i * blockDim.x + threadIdx.x) * VW;
       if (e < cols) {
-        load_vec<VW>(v[i], xr + e, true);
+        load_vec<VW>(nv[i], xr + e, true);
       } else {
 #pragma unroll
-        for (int k = 0; k < VW; ++k) v[i][k] = 0.0f;
+        for (int k = 0; k < VW; ++k) nv[i][k] = 0.0f;
       }
     }
+    np = lane < npilot ? __ldg(xr + lane) : 0.0f;
+  };
+  int64_t row = blockIdx.x;
+  if (row < rows) load_row(row);
+  for (; row < rows; row += gridDim.x) {
+    float v[VPT][VW];
 #pragma unroll
     for (int i = 0; i < VPT; ++i)
 #pragma unroll
-      for (int k = 0; k < VW; ++k) s = __fadd_rn(s, v[i][k]);
-    s = block_sum(s, scratch);
-    const float mu = __fdiv_rn(s, (float)cols);
-    float ss = 0.0f;
+      for (int k = 0; k < VW; ++k) v[i][k] = nv[i][k];
+    // K needs no particular rounding: the sums are taken around whatever
+    // value it has, and only |mean - K| affects the accuracy
+    const float K = warp_sum(np) / (float)npilot;
+    if (PF && row + gridDim.x < rows) load_row(row + gridDim.x);
+    float s1 = 0.0f, s2 = 0.0f;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int e = (i * blockDim.x + threadIdx.x) * VW;
 #pragma unroll
       for (int k = 0; k < VW; ++k) {
-        v[i][k] = __fsub_rn(v[i][k], mu);
-        if (e < cols) ss = __fadd_rn(ss, __fmul_rn(v[i][k], v[i][k]));
+        const float d = e < cols ? v[i][k] - K : 0.0f;
+        s1 += d;
+        s2 = fmaf(d, d, s2);
       }
     }
-    ss = block_sum(ss, scratch);
-    const float var = __fdiv_rn(ss, (float)cols);
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+    float2 r = block_sum2(s1, s2, scratch);
+    const float m1 = __fdiv_rn(r.x, n);
+    float mu = K + m1;
+    float var = __fdiv_rn(r.y, n) - m1 * m1;
+    if (m1 * m1 > var) {  // uniform: every thread holds the same sums
+      // pilot far from the mean: the same sums around the first estimate,
+      // which is close enough for both the mean correction and the variance
+      float t1 = 0.0f, t2 = 0.0f;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int e = (i * blockDim.x + threadIdx.x) * VW;
+#pragma unroll
+        for (int k = 0; k < VW; ++k) {
+          const float d = e < cols ? v[i][k] - mu : 0.0f;
+          t1 += d;
+          t2 = fmaf(d, d, t2);
+        }
+      }
+      r = block_sum2(t1, t2, scratch);
+      const float c1 = __fdiv_rn(r.x, n);
+      mu += c1;
+      var = __fdiv_rn(r.y, n) - c1 * c1;
+    }
+#pragma unroll
+    for (int i = 0; i < VPT; ++i)
+#pragma unroll
+      for (int k = 0; k < VW; ++k) v[i][k] = __fsub_rn(v[i][k], mu);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(fmaxf(var, 0.0f), eps)));
     float* yr = y + row * (int64_t)cols;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
@@ -588,7 +670,10 @@ oxc_status oxc_layer_norm_fwd(const float* x, const float* w, const float* b, fl
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool v4 = cols % 4 == 0 && aligned16(x) && aligned16(w) && aligned16(b) && aligned16(y);
   const GeluConst gc = gelu_const();
-  const int stages = v4 ? pipe_stages(1, cols, 8, kFwdNG + 1) : 0;
+  // LayerNorm+GELU: the pipelined kernel (the activation's arithmetic keeps
+  // the register kernel's warps busy); plain LayerNorm: the register kernel
+  const int stages =
+      v4 && act == OXC_ACT_GELU_TANH ? pipe_stages(1, cols, 8, kFwdNG + 1) : 0;
   const int vpt = v4 ? pipe_vpt(cols, kFwdNWG, 8) : 0;
   if (stages && vpt) {
     const int64_t ctas = std::min<int64_t>(rows, sm_count());
@@ -619,14 +704,21 @@ oxc_status oxc_layer_norm_fwd(const float* x, const float* w, const float* b, fl
   }
   RowGeom g = row_geom(cols, v4);
   const unsigned grid = (unsigned)(rows < 0x7fffffff ? rows : 0x7fffffff);
-#define LAUNCH(VW, VPT, MAXT)                                                            \
-  do {                                                                                   \
-    if (act == OXC_ACT_GELU_TANH)                                                        \
-      ln_fwd_kernel<VW, VPT, MAXT, OXC_ACT_GELU_TANH>                                    \
-          <<<grid, g.block, 0, s>>>(x, w, b, y, mean, rstd, rows, (int)cols, eps, gc);   \
-    else                                                                                 \
-      ln_fwd_kernel<VW, VPT, MAXT, OXC_ACT_NONE>                                         \
-          <<<grid, g.block, 0, s>>>(x, w, b, y, mean, rstd, rows, (int)cols, eps, gc);   \
+  // persistent: as many CTAs as fit on the GPU at once, each looping over rows
+  auto ctas_for = [&](const void* k) {
+    const int64_t fit = (int64_t)sm_count() * std::max(1, occupancy(k, g.block, 0));
+    return (unsigned)std::min<int64_t>(rows, fit);
+  };
+#define LAUNCH(VW, VPT, MAXT)                                                              \
+  do {                                                                                     \
+    if (act == OXC_ACT_GELU_TANH) {                                                        \
+      ln_fwd_kernel<VW, VPT, MAXT, OXC_ACT_GELU_TANH, false>                               \
+          <<<grid, g.block, 0, s>>>(x, w, b, y, mean, rstd, rows, (int)cols, eps, gc);     \
+    } else {                                                                               \
+      auto k = ln_fwd_kernel<VW, VPT, MAXT, OXC_ACT_NONE, true>;                           \
+      k<<<ctas_for((const void*)k), g.block, 0, s>>>(x, w, b, y, mean, rstd, rows,         \
+                                                     (int)cols, eps, gc);                  \
+    }                                                                                      \
   } while (0)
   OXC_DISPATCH_ROW(g, LAUNCH);
 #undef LAUNCH

@@ -10,6 +10,9 @@ Tolerances (from the project's parity contract):
   trees, so the absolute term is scaled by the sum's condition number:
   atol = 1e-6 * sum(|terms|) (each test states the terms); 1e-5 * sum(|terms|)
   when the terms themselves depend on a row reduction over >= 32k elements;
+* outputs computed from a centred value (x - mean, LayerNorm) also allow 4 ulp
+  of |mean| propagated through the normalisation: the kernel's own rounding of
+  a large row mean, which the reference-only budget below does not contain;
 * every output also carries the reference's own summation-order error:
   the element-wise difference between the reference composition with its
   left-to-right f32 folds and the same composition with f64-folded sums
