@@ -99,7 +99,9 @@ __device__ __forceinline__ float2 block_sum2(float a, float b, float* scratch) {
 // a second reduction takes the same two sums around the first estimate, which
 // is then within a tiny fraction of sigma of the mean, and corrects both mean
 // and variance.  Every row ends up as accurate as the reference's two-pass
-// formula, and x - mean is rounded once, as in the reference.
+// formula.  x - mean is rounded once, as in the reference, except on rows
+// that take the second pass: there the centred value is corrected by c1, one
+// more rounding (at most half an ulp of the centred value).
 template <int VW, int VPT, int MAXT, int ACT, bool PF>
 __global__ void __launch_bounds__(MAXT) ln_fwd_kernel(
     const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
@@ -151,16 +153,20 @@ __global__ void __launch_bounds__(MAXT) ln_fwd_kernel(
     const float m1 = __fdiv_rn(r.x, n);
     float mu = K + m1;
     float var = __fdiv_rn(r.y, n) - m1 * m1;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i)
+#pragma unroll
+      for (int k = 0; k < VW; ++k) v[i][k] = __fsub_rn(v[i][k], mu);
     if (m1 * m1 > var) {  // uniform: every thread holds the same sums
-      // pilot far from the mean: the same sums around the first estimate,
-      // which is close enough for both the mean correction and the variance
+      // pilot far from the mean: the same sums over the values centred on the
+      // first estimate give the mean correction c1 and the variance
       float t1 = 0.0f, t2 = 0.0f;
 #pragma unroll
       for (int i = 0; i < VPT; ++i) {
         const int e = (i * blockDim.x + threadIdx.x) * VW;
 #pragma unroll
         for (int k = 0; k < VW; ++k) {
-          const float d = e < cols ? v[i][k] - mu : 0.0f;
+          const float d = e < cols ? v[i][k] : 0.0f;
           t1 += d;
           t2 = fmaf(d, d, t2);
         }
@@ -169,11 +175,11 @@ __global__ void __launch_bounds__(MAXT) ln_fwd_kernel(
       const float c1 = __fdiv_rn(r.x, n);
       mu += c1;
       var = __fdiv_rn(r.y, n) - c1 * c1;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i)
+#pragma unroll
+        for (int k = 0; k < VW; ++k) v[i][k] = __fsub_rn(v[i][k], c1);
     }
-#pragma unroll
-    for (int i = 0; i < VPT; ++i)
-#pragma unroll
-      for (int k = 0; k < VW; ++k) v[i][k] = __fsub_rn(v[i][k], mu);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(fmaxf(var, 0.0f), eps)));
     float* yr = y + row * (int64_t)cols;
 #pragma unroll
