@@ -672,6 +672,7 @@ def run_ours(args, rank, world, local_rank):
     cpu = cpu_baseline(args.workload) if (world == 1 and not args.no_cpu_baseline) else None
     dom_ms, dom_bytes = (bwd_ms, wl.bwd_bytes) if wl.dominant == "bwd" else (fwd_ms, wl.fwd_bytes)
     achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
+    traffic = _profiled_traffic(args.workload)
     line = {
         "metric": METRIC,
         "value": value,
@@ -695,7 +696,10 @@ def run_ours(args, rank, world, local_rank):
             "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs: torch copy read+write)",
             "unit": "GB/s",
             "frac": achieved / peak,
-            "traffic": _profiled_traffic(args.workload),
+            "traffic": traffic,
+            # the same phase time with the profiled DRAM bytes: differs from
+            # `achieved` where L2 serves part of the algorithmic bytes
+            "dram_gbs": traffic / (dom_ms * 1e-3) / 1e9 if traffic else None,
             "fwd_gbs": wl.fwd_bytes / (fwd_ms * 1e-3) / 1e9,
             "bwd_gbs": wl.bwd_bytes / (bwd_ms * 1e-3) / 1e9,
             "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,

@@ -132,6 +132,18 @@ oxc_status oxc_binary_scalar(int32_t op, const oxc_view* a, float scalar, int32_
 size_t oxc_reduce_workspace_size(int32_t kind, const oxc_view* in, int64_t dim);
 oxc_status oxc_reduce(int32_t kind, const oxc_view* in, int64_t dim, int32_t keepdim,
                       const oxc_view* out, void* workspace, size_t workspace_bytes, void* stream);
+/* VJP of Tensor::reduce along `dim` (crates/oxi-autograd/src/ops.rs:327-388):
+ *   sum: dx = g broadcast along dim;  mean: dx = g * f32(1/len);
+ *   max/min: dx = g at each strip's first argmax/argmin, +0 elsewhere (the
+ *            reference recomputes argmax/argmin from x, as this call does);
+ *   norm: dx = g * (x / (norm + 1e-12)), three roundings as in the reference.
+ * x is the forward input (any strides); g is dense with the forward output's
+ * shape (keepdim or not: the same memory); dx is dense with x's shape.
+ * argmax/argmin: OXC_ERR_NOT_IMPLEMENTED (no gradient, as in the reference).
+ * max/min/norm need oxc_reduce_bwd_workspace_size bytes of workspace. */
+size_t oxc_reduce_bwd_workspace_size(int32_t kind, const oxc_view* x, int64_t dim);
+oxc_status oxc_reduce_bwd(int32_t kind, const oxc_view* x, int64_t dim, const float* g, float* dx,
+                          void* workspace, size_t workspace_bytes, void* stream);
 /* Whole-tensor reduction (reduce_strip over every element, as the Python
  * t.sum()/t.mean()/... without a dim: crates/oxi-bindings/src/lib.rs:126-143;
  * sum_all/mean_all/norm, lib.rs:582-604).  Deterministic two-stage reduction

@@ -70,6 +70,8 @@ SIGNATURES = {
     "oxc_binary_scalar": (_I32, [_I32, _VP, _F32, _I32, _VP, _P]),
     "oxc_reduce_workspace_size": (_SZ, [_I32, _VP, _I64]),
     "oxc_reduce": (_I32, [_I32, _VP, _I64, _I32, _VP, _P, _SZ, _P]),
+    "oxc_reduce_bwd_workspace_size": (_SZ, [_I32, _VP, _I64]),
+    "oxc_reduce_bwd": (_I32, [_I32, _VP, _I64, _P, _P, _P, _SZ, _P]),
     "oxc_reduce_all_workspace_size": (_SZ, [_I64]),
     "oxc_reduce_all": (_I32, [_I32, _VP, _P, _P, _P, _SZ, _P]),
     "oxc_sum_squares_workspace_size": (_SZ, [_VP, _I32]),

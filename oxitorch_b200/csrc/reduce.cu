@@ -19,7 +19,8 @@
 //           fold, bit for bit); threads of a warp own neighbouring outputs so
 //           the loads coalesce; long strips over few outputs are cut into
 //           segments whose partials a finisher combines in segment order;
-//   all:    whole-tensor, two stages with f64 partials for sum/mean/norm.
+//   all:    whole-tensor, two stages with f64 partials for sum/mean/norm;
+//   VJPs:   broadcast / scale / scatter / norm-ratio kernels writing dx dense.
 #include <math.h>
 
 #include <algorithm>
@@ -519,6 +520,76 @@ static oxc_status plan_reduce(int32_t kind, const oxc_view* in, int64_t dim, int
   return OXC_OK;
 }
 
+
+// ---- reduce VJPs (crates/oxi-autograd/src/ops.rs:327-388) -------------------------
+//
+// dx has x's shape, dense; view it as [outer, len, inner] around the reduced
+// dim; g and aux (argmax index or norm per strip) are dense [outer, inner].
+//   sum:     dx = g                      (expand_to)
+//   mean:    dx = g * rn,  rn = f32(1/len)  (expand_to, then mul_scalar(1.0 / n))
+//   max/min: dx = g at the strip's first arg position, +0 elsewhere
+//            (scatter_along_dim into zeros)
+//   norm:    dx = g * (x / (norm + 1e-12))  (add_scalar, div, mul: three roundings)
+
+struct XView {
+  int nd;
+  int64_t n[OXC_MAX_DIMS];
+  int64_t st[OXC_MAX_DIMS];
+};
+
+// Offset of the element with dense row-major index j of x's shape.
+__device__ __forceinline__ int64_t x_offset(const XView& X, int64_t j) {
+  int64_t off = 0;
+  for (int d = X.nd - 1; d >= 0; --d) {
+    const int64_t q = j / X.n[d];
+    off += (j - q * X.n[d]) * X.st[d];
+    j = q;
+  }
+  return off;
+}
+
+template <int KIND>
+__device__ __forceinline__ float reduce_vjp_elem(float gv, float aux, int64_t l, float xv, float rn) {
+  if (KIND == RK_SUM) return gv;
+  if (KIND == RK_MEAN) return __fmul_rn(gv, rn);
+  if (KIND == RK_MAX) return l == (int64_t)aux ? gv : 0.0f;
+  return __fmul_rn(gv, __fdiv_rn(xv, __fadd_rn(aux, 1e-12f)));  // RK_NORM
+}
+
+// inner > 1: a CTA walks rows t = o * len + l; its threads cover the inner
+// index, so g, aux and dx are read and written contiguously.
+template <int KIND>
+__global__ void __launch_bounds__(256) reduce_vjp_rows_kernel(
+    const float* __restrict__ x, XView X, bool xdense, const float* __restrict__ g,
+    const float* __restrict__ aux, float* __restrict__ dx, int64_t nrows, int64_t len,
+    int64_t inner, float rn) {
+  for (int64_t t = blockIdx.x; t < nrows; t += gridDim.x) {
+    const int64_t o = t / len, l = t - o * len;
+    const float* gr = g + o * inner;
+    const float* ar = aux ? aux + o * inner : nullptr;
+    float* dr = dx + t * inner;
+    for (int64_t i = threadIdx.x; i < inner; i += blockDim.x) {
+      float xv = 0.0f;
+      if (KIND == RK_NORM) xv = __ldg(x + (xdense ? t * inner + i : x_offset(X, t * inner + i)));
+      dr[i] = reduce_vjp_elem<KIND>(__ldg(gr + i), ar ? __ldg(ar + i) : 0.0f, l, xv, rn);
+    }
+  }
+}
+
+// inner == 1 (the reduced dim is the last one): elementwise over dx.
+template <int KIND>
+__global__ void __launch_bounds__(256) reduce_vjp_last_kernel(
+    const float* __restrict__ x, XView X, bool xdense, const float* __restrict__ g,
+    const float* __restrict__ aux, float* __restrict__ dx, int64_t total, int64_t len, float rn) {
+  for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < total;
+       j += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t s = j / len, l = j - s * len;
+    float xv = 0.0f;
+    if (KIND == RK_NORM) xv = __ldg(x + (xdense ? j : x_offset(X, j)));
+    dx[j] = reduce_vjp_elem<KIND>(__ldg(g + s), aux ? __ldg(aux + s) : 0.0f, l, xv, rn);
+  }
+}
+
 }  // namespace oxc
 
 using namespace oxc;
@@ -592,6 +663,107 @@ oxc_status oxc_reduce(int32_t kind, const oxc_view* in, int64_t dim, int32_t kee
   const unsigned g2 = (unsigned)std::max<int64_t>(1, std::min<int64_t>((P.nout + 255) / 256, cap));
   reduce_col_finish_kernel<<<g2, 256, 0, s>>>(kind, in->data, P.L, P.nout, P.nseg, pv, pi, out->data);
   return check_launch("oxc_reduce (finish)");
+}
+
+// The forward reduction a VJP needs first (argmax/argmin for max/min, norm
+// for norm), or -1.
+static int vjp_aux_kind(int32_t kind) {
+  return kind == RK_MAX ? RK_ARGMAX : kind == RK_MIN ? RK_ARGMIN : kind == RK_NORM ? RK_NORM : -1;
+}
+
+static void keepdim_view(const oxc_view* x, int64_t d, float* data, oxc_view* out) {
+  out->data = data;
+  out->ndim = x->ndim;
+  int64_t expect = 1;
+  for (int i = x->ndim - 1; i >= 0; --i) {
+    out->shape[i] = i == d ? 1 : x->shape[i];
+    out->strides[i] = expect;
+    expect *= out->shape[i];
+  }
+}
+
+size_t oxc_reduce_bwd_workspace_size(int32_t kind, const oxc_view* x, int64_t dim) {
+  const int ak = vjp_aux_kind(kind);
+  if (ak < 0 || !x || x->ndim <= 0 || x->ndim > OXC_MAX_DIMS) return 0;
+  const int64_t d = dim < 0 ? x->ndim + dim : dim;
+  if (d < 0 || d >= x->ndim) return 0;
+  int64_t nout = 1;
+  for (int i = 0; i < x->ndim; ++i) nout *= i == d ? 1 : x->shape[i];
+  return (size_t)nout * sizeof(float) + 256 + oxc_reduce_workspace_size(ak, x, d);
+}
+
+oxc_status oxc_reduce_bwd(int32_t kind, const oxc_view* x, int64_t dim, const float* g, float* dx,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  if (kind < 0 || kind > 6)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: unknown reduction kind %d", kind);
+  if (kind == RK_ARGMAX || kind == RK_ARGMIN)
+    return fail(OXC_ERR_NOT_IMPLEMENTED,
+                "not implemented: argmax/argmin are integer outputs and have no gradient");
+  oxc_status st = check_view(x, "reduce backward");
+  if (st) return st;
+  const int nd = x->ndim;
+  const int64_t d = dim < 0 ? nd + dim : dim;
+  if (d < 0 || d >= nd)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: dim %lld out of range for %d-D tensor",
+                (long long)dim, nd);
+  int64_t outer = 1, inner = 1;
+  for (int i = 0; i < d; ++i) outer *= x->shape[i];
+  for (int i = (int)d + 1; i < nd; ++i) inner *= x->shape[i];
+  const int64_t len = x->shape[d], total = outer * len * inner;
+  if ((kind == RK_MAX || kind == RK_MIN) && len == 0)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: cannot compute max/min over a zero-length dim");
+  if (total == 0) return OXC_OK;
+  if (!g || !dx || !x->data)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: reduce backward: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int ak = vjp_aux_kind(kind);
+  float* aux = nullptr;
+  if (ak >= 0) {
+    const size_t need = oxc_reduce_bwd_workspace_size(kind, x, d);
+    if (!workspace || workspace_bytes < need)
+      return fail(OXC_ERR_INVALID_ARGUMENT,
+                  "invalid argument: reduce backward needs a %zu-byte workspace "
+                  "(oxc_reduce_bwd_workspace_size), got %zu", need, workspace_bytes);
+    aux = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(workspace) + 15) & ~uintptr_t(15));
+    const size_t aux_bytes = ((size_t)outer * inner * sizeof(float) + 15) & ~size_t(15);
+    unsigned char* rws = reinterpret_cast<unsigned char*>(aux) + aux_bytes;
+    const size_t used = (size_t)(rws - static_cast<unsigned char*>(workspace));
+    oxc_view av;
+    keepdim_view(x, d, aux, &av);
+    st = oxc_reduce(ak, x, d, 1, &av, rws, workspace_bytes - used, stream);
+    if (st) return st;
+  }
+  XView X;
+  X.nd = nd;
+  bool xdense = true;
+  int64_t expect = 1;
+  for (int i = nd - 1; i >= 0; --i) {
+    X.n[i] = x->shape[i] > 0 ? x->shape[i] : 1;
+    X.st[i] = x->strides[i];
+    if (x->shape[i] != 1 && x->strides[i] != expect) xdense = false;
+    expect *= x->shape[i];
+  }
+  const float rn = 1.0f / (float)len;
+  const int64_t cap = (int64_t)sm_count() * 16;
+#define OXC_VJP_LAUNCH(K)                                                                        \
+  do {                                                                                           \
+    if (inner > 1) {                                                                             \
+      reduce_vjp_rows_kernel<K><<<(unsigned)std::min<int64_t>(outer * len, cap), 256, 0, s>>>(   \
+          x->data, X, xdense, g, aux, dx, outer * len, len, inner, rn);                          \
+    } else {                                                                                     \
+      reduce_vjp_last_kernel<K><<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(              \
+                                      (total + 255) / 256, cap)), 256, 0, s>>>(                   \
+          x->data, X, xdense, g, aux, dx, total, len, rn);                                       \
+    }                                                                                            \
+  } while (0)
+  switch (kind) {
+    case RK_SUM: OXC_VJP_LAUNCH(RK_SUM); break;
+    case RK_MEAN: OXC_VJP_LAUNCH(RK_MEAN); break;
+    case RK_NORM: OXC_VJP_LAUNCH(RK_NORM); break;
+    default: OXC_VJP_LAUNCH(RK_MAX); break;  // max and min: scatter to the arg position
+  }
+#undef OXC_VJP_LAUNCH
+  return check_launch("oxc_reduce_bwd");
 }
 
 static int64_t all_parts(int64_t n, int64_t* chunk) {

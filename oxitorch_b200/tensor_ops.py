@@ -2,7 +2,9 @@
 
 Same names, argument meaning and errors as ``crates/oxi-tensor/src/lib.rs``:
 ``binary_op(name, a, b)``, ``cmp_op``, ``unary_op``, ``reduce(kind, x, dim,
-keepdim)``, the whole-tensor ``sum_all``/``mean_all``/``reduce_all``, plus
+keepdim)`` with its VJP ``reduce_backward`` and the autograd helper
+``unbroadcast`` (graph.rs:274-313), the whole-tensor
+``sum_all``/``mean_all``/``reduce_all``, plus
 ``clip_grad_norm_`` (python/oxitorch/optim.py:242-263) over device
 gradients.  Inputs are torch CUDA float32 tensors with any strides (views:
 transposes, slices, zero-stride broadcasts); outputs are dense, like the
@@ -95,7 +97,14 @@ def unary_op(name, a):
 
 def reduce(kind, x, dim, keepdim=False):
     """Tensor::reduce (lib.rs:519-576); argmax/argmin come back as float
-    indices like the reference's f32 carrier."""
+    indices like the reference's f32 carrier.  Differentiable (for every kind
+    but argmax/argmin) through the reference's reduce VJP, reduce_backward."""
+    if x.requires_grad and torch.is_grad_enabled() and kind not in ("argmax", "argmin"):
+        return _Reduce.apply(x, kind, dim, keepdim)
+    return _reduce_fwd(kind, x, dim, keepdim)
+
+
+def _reduce_fwd(kind, x, dim, keepdim):
     k = _op_id(REDUCE_KINDS, kind, "reduction")
     _require_cuda_f32("x", x)
     nd = x.dim()
@@ -114,6 +123,80 @@ def reduce(kind, x, dim, keepdim=False):
     N.check(L.oxc_reduce(k, ctypes.byref(xv), d, int(keepdim), ctypes.byref(N.make_view(out)),
                          ws.data_ptr(), ws.numel(), _stream()), kind)
     return out
+
+
+def reduce_backward(kind, x, dim, g):
+    """VJP of reduce(kind, x, dim, keepdim) (crates/oxi-autograd/src/ops.rs:
+    327-388) for upstream gradient g (the forward output's shape, keepdim or
+    not): sum broadcasts g, mean scales it by f32(1/len), max/min send it to
+    each strip's first argmax/argmin, norm multiplies by x / (norm + 1e-12).
+    argmax/argmin raise NotImplementedError, as in the reference."""
+    k = _op_id(REDUCE_KINDS, kind, "reduction")
+    _require_cuda_f32("x", x)
+    _require_cuda_f32("g", g)
+    nd = x.dim()
+    d = dim + nd if dim < 0 else dim
+    if not 0 <= d < nd:
+        raise ValueError(f"invalid argument: dim {dim} out of range for {nd}-D tensor")
+    kshape = list(x.shape)
+    kshape[d] = 1
+    if g.numel() != x.numel() // max(x.shape[d], 1) or list(g.shape) not in (
+            kshape, kshape[:d] + kshape[d + 1:]):
+        raise ValueError(f"shape mismatch: gradient {list(g.shape)} for reduce output of "
+                         f"{list(x.shape)} over dim {d}")
+    g = g.contiguous()
+    dx = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+    L = N.load()
+    xv = N.make_view(x)
+    ws = _workspace(L.oxc_reduce_bwd_workspace_size(k, ctypes.byref(xv), d), x.device)
+    N.check(L.oxc_reduce_bwd(k, ctypes.byref(xv), d, g.data_ptr(), dx.data_ptr(), ws.data_ptr(),
+                             ws.numel(), _stream()), f"{kind} backward")
+    return dx
+
+
+class _Reduce(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, kind, dim, keepdim):
+        ctx.save_for_backward(x)
+        ctx.kind, ctx.dim = kind, dim
+        return _reduce_fwd(kind, x, dim, keepdim)
+
+    @staticmethod
+    def backward(ctx, g):
+        (x,) = ctx.saved_tensors
+        return reduce_backward(ctx.kind, x, ctx.dim, g), None, None, None
+
+
+def unbroadcast(g, shape):
+    """graph.rs:274-313: sums g over the axes a forward broadcast expanded to
+    bring it back to `shape` -- the prepended axes first (each a keepdim sum
+    over the leading axis), then the size-1 target axes -- and reshapes.  Each
+    step is one device reduction, in the reference's order."""
+    _require_cuda_f32("g", g)
+    shape = [int(s) for s in shape]
+    gs = list(g.shape)
+    if len(gs) < len(shape):
+        raise ValueError(f"shape mismatch: {gs} vs {shape}")
+    extra = len(gs) - len(shape)
+    for i, s in enumerate(shape):
+        if gs[extra + i] != s and s != 1:
+            raise ValueError(f"shape mismatch: {gs} vs {shape}")
+    t = g
+    for i in range(extra):
+        t = _reduce_fwd("sum", t, i, True)
+    # the reference indexes t.shape by the target position here, so with
+    # prepended axes it looks at (and sums) the leading axes; kept as is
+    for i, s in enumerate(shape):
+        if s == 1 and t.shape[i] != 1:
+            t = _reduce_fwd("sum", t, i, True)
+    if list(t.shape) != shape:
+        n = 1
+        for s in shape:
+            n *= s
+        if t.numel() != n:  # Tensor::reshape's element-count check
+            raise ValueError(f"shape mismatch: {list(t.shape)} vs {shape}")
+        t = t.reshape(shape)
+    return t
 
 
 def reduce_all(kind, x, f64=False):
