@@ -174,6 +174,18 @@ def cpu_sample(workload, seed):
         for grad in (xt.grad.numpy(), gt.grad.numpy(), ut.grad.numpy()):
             R.sumsq_all_f64(grad)
         return time.perf_counter() - t0, m * (20 * dmod + 32 * hid) + 12 * dmod
+    if workload == "registry":
+        m, hid = 16, 11008
+        g = rng.standard_normal((m, hid), dtype=np.float32)
+        u = rng.standard_normal((m, hid), dtype=np.float32)
+        dh = rng.standard_normal((m, hid), dtype=np.float32)
+        t0 = time.perf_counter()
+        gt, ut = R.from_numpy(g, True), R.from_numpy(u, True)
+        h = R.silu(gt) * ut
+        hv = h.numpy()
+        R.t_reduce("sum", hv, 1, False), R.t_reduce("max", hv, 1, False), R.t_reduce("argmax", hv, 1, False)
+        h.backward(dh)
+        return time.perf_counter() - t0, m * hid * (44 + 92) + 12 * m
     raise ValueError(workload)
 
 
@@ -485,6 +497,7 @@ class Embedding(Workload):
 
 
 class MlpBlock(Workload):
+    E2E_LARGE = True
     DESC = ("decoder-MLP activation block fwd+bwd, fp32, 65536 tokens: RMSNorm [.., 4096] "
             "(broadcast weight view), SwiGLU [.., 11008] (transposed gate view), dim-1 "
             "sum/max/argmax, whole-tensor L2 of {dx, dg, du} (BASELINE config 5)")
@@ -571,8 +584,118 @@ class MlpBlock(Workload):
                 "l2": "no flush: every tensor (1-2.9 GB) is larger than L2"}
 
 
+class Registry(Workload):
+    DESC = ("config-5 SwiGLU composed from the elementwise registry and dim reductions, as the "
+            "reference's F.silu(g) * u graph runs it: sigmoid, mul, mul, dim-1 sum/max/argmax "
+            "forward; the graph's eight elementwise VJP ops backward; gate a transposed view "
+            "(BASELINE config 5, strided engine)")
+    SEED = 6
+    KERNEL = "elem_dense_kernel / elem_tiled_kernel (registry binary ops of the VJP)"
+    launches = 14  # sigmoid, 2 mul, 3 reductions; 7 binary + 1 scalar-binary
+    E2E_LARGE = True
+    MUL, ADD, SUB, SIGMOID = 2, 0, 1, 12
+    R_SUM, R_MAX, R_ARGMAX = 0, 2, 4
+
+    def __init__(self, dev, rank, world, args):
+        super().__init__(dev, rank, world, args)
+        import ctypes
+        t = self.torch
+        M = args.rows or 65536
+        H = 11008
+        self.M, self.H = M, H
+        self.ctypes = ctypes
+        self.gate_buf = self.randn(H, M)
+        self.up, self.dh = self.randn(M, H), self.randn(M, H)
+        (self.sg, self.silu, self.h, self.du, self.t, self.dg1, self.ds, self.oms, self.sds,
+         self.dg2, self.dg) = (t.empty(M, H, device=dev) for _ in range(11))
+        self.hs, self.hm, self.ha = (t.empty(M, device=dev) for _ in range(3))
+        self.fwd_bytes = M * H * (8 + 12 + 12 + 3 * 4) + 3 * 4 * M
+        self.bwd_bytes = M * H * (7 * 12 + 8)
+
+    def _v(self, x):
+        return self.ctypes.byref(self.N.make_view(x))
+
+    def _bin(self, op, a, b, out):
+        self.N.check(self.L.oxc_binary(op, self._v(a), self._v(b), self._v(out), self.s))
+
+    def _red(self, kind, x, out):
+        self.N.check(self.L.oxc_reduce(kind, self._v(x), 1, 0, self._v(out), None, 0, self.s))
+
+    def fwd(self):
+        g = self.gate_buf.t()
+        self.N.check(self.L.oxc_unary(self.SIGMOID, self._v(g), self._v(self.sg), self.s))
+        self._bin(self.MUL, g, self.sg, self.silu)
+        self._bin(self.MUL, self.silu, self.up, self.h)
+        self._red(self.R_SUM, self.h, self.hs)
+        self._red(self.R_MAX, self.h, self.hm)
+        self._red(self.R_ARGMAX, self.h, self.ha)
+
+    def bwd(self):
+        # h = silu * u;  silu = g * s;  s = sigmoid(g)  (autograd/ops.rs mul and sigmoid VJPs)
+        g = self.gate_buf.t()
+        self._bin(self.MUL, self.dh, self.silu, self.du)
+        self._bin(self.MUL, self.dh, self.up, self.t)
+        self._bin(self.MUL, self.t, self.sg, self.dg1)
+        self._bin(self.MUL, self.t, g, self.ds)
+        self.N.check(self.L.oxc_binary_scalar(self.SUB, self._v(self.sg), 1.0, 1, self._v(self.oms),
+                                              self.s))
+        self._bin(self.MUL, self.sg, self.oms, self.sds)
+        self._bin(self.MUL, self.ds, self.sds, self.dg2)
+        self._bin(self.ADD, self.dg1, self.dg2, self.dg)
+
+    def per_op(self):
+        """GB/s of each kernel on its own (CUDA events, median of 5 after 2 warm-ups)."""
+        import statistics
+        torch = self.torch
+        g = self.gate_buf.t()
+        MH = self.M * self.H
+        ops = {
+            "sigmoid(transposed gate)": (lambda: self.N.check(self.L.oxc_unary(
+                self.SIGMOID, self._v(g), self._v(self.sg), self.s)), 8 * MH),
+            "mul(transposed gate, dense)": (lambda: self._bin(self.MUL, g, self.sg, self.silu),
+                                            12 * MH),
+            "mul(dense, dense)": (lambda: self._bin(self.MUL, self.silu, self.up, self.h), 12 * MH),
+            "sub(1, dense) scalar": (lambda: self.N.check(self.L.oxc_binary_scalar(
+                self.SUB, self._v(self.sg), 1.0, 1, self._v(self.oms), self.s)), 8 * MH),
+            "sum over dim 1": (lambda: self._red(self.R_SUM, self.h, self.hs), 4 * MH + 4 * self.M),
+            "max over dim 1": (lambda: self._red(self.R_MAX, self.h, self.hm), 4 * MH + 4 * self.M),
+            "argmax over dim 1": (lambda: self._red(self.R_ARGMAX, self.h, self.ha),
+                                  4 * MH + 4 * self.M),
+        }
+        out = {}
+        for name, (fn, nbytes) in ops.items():
+            for _ in range(2):
+                fn()
+            ts = []
+            for _ in range(5):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                fn()
+                e1.record()
+                torch.cuda.synchronize()
+                ts.append(e0.elapsed_time(e1))
+            out[name] = round(nbytes / (statistics.median(ts) * 1e-3) / 1e9, 1)
+        return out
+
+    def e2e_io(self):
+        return [self.gate_buf, self.up, self.dh], [self.h, self.hs, self.hm, self.ha, self.dg,
+                                                    self.du]
+
+    def e2e_step(self, dev_in):
+        saved = (self.gate_buf, self.up, self.dh)
+        self.gate_buf, self.up, self.dh = dev_in
+        self.fwd()
+        self.bwd()
+        self.gate_buf, self.up, self.dh = saved
+
+    def config(self):
+        return {"workload": self.DESC, "tokens_per_gpu": self.M, "ffn": self.H,
+                "gate_strides": [1, self.M],
+                "l2": "no flush: every tensor (2.9 GB) is larger than L2"}
+
+
 WORKLOADS = {"ln_gelu": LnGelu, "rms": Rms, "ce": CrossEntropy, "embedding": Embedding,
-             "mlp_block": MlpBlock}
+             "mlp_block": MlpBlock, "registry": Registry}
 
 
 def run_ours(args, rank, world, local_rank):
@@ -627,8 +750,8 @@ def run_ours(args, rank, world, local_rank):
 
     # ---- e2e: host buffers through the C ABI --------------------------------------------
     e2e = None
-    if args.workload == "mlp_block" and not args.e2e_large:
-        e2e = {"value": None, "unit": "GB/s", "skipped": "config 5 moves ~23 GB per step through "
+    if getattr(wl, "E2E_LARGE", False) and not args.e2e_large:
+        e2e = {"value": None, "unit": "GB/s", "skipped": "config 5 moves ~9-23 GB per step through "
                "pinned host buffers; pass --e2e-large to measure it"}
     elif not args.skip_e2e:
         ins, outs = wl.e2e_io()
@@ -669,6 +792,7 @@ def run_ours(args, rank, world, local_rank):
 
     if rank != 0:
         return
+    per_op = wl.per_op() if hasattr(wl, "per_op") else None
     cpu = cpu_baseline(args.workload) if (world == 1 and not args.no_cpu_baseline) else None
     dom_ms, dom_bytes = (bwd_ms, wl.bwd_bytes) if wl.dominant == "bwd" else (fwd_ms, wl.fwd_bytes)
     achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
@@ -687,7 +811,8 @@ def run_ours(args, rank, world, local_rank):
         "dtype": "f32",
         "data": "synthetic (seeded inputs with the BASELINE config's shapes and distributions; "
                 "no dataset)",
-        "config": {**wl.config(), "algorithmic_bytes_per_gpu_step": wl.fwd_bytes + wl.bwd_bytes},
+        "config": {**wl.config(), "algorithmic_bytes_per_gpu_step": wl.fwd_bytes + wl.bwd_bytes,
+                   **({"per_op_gbs": per_op} if per_op else {})},
         "roofline": {
             "bound": "hbm",
             "kernel": wl.KERNEL,
