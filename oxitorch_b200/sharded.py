@@ -7,7 +7,9 @@ path.  What crosses ranks is small:
 
 * weight gradients of the norms (dweight / dbias, [cols]) and of a replicated
   embedding table: each rank's VJP leaves the sum over its own rows, and one
-  all-reduce (sum) makes it the sum over every row -- ``allreduce_sum_``;
+  all-reduce (sum) makes it the sum over every row -- ``allreduce_sum_``; a
+  large table's gradient can instead be reduce-scattered so each rank keeps
+  the summed rows of its own shard -- ``reduce_scatter_rows``;
 * the cross-entropy mean: the global row count M is agreed before the forward
   (one int64 all-reduce), each rank's loss kernel divides its partial sum by
   that M, and the partials are summed -- ``cross_entropy``; the VJP scale
@@ -101,6 +103,25 @@ def sync_grads_(params, group=None):
     grads = [p.grad for p in params if p.grad is not None]
     allreduce_sum_(*grads, group=group)
     return grads
+
+
+def reduce_scatter_rows(t: torch.Tensor, group=None) -> torch.Tensor:
+    """Sum of t over the ranks, of which this rank keeps only its row shard
+    (rows shard_range(t.shape[0], rank, G)): the gradient of a replicated
+    table for a caller that updates the table shard by shard.  Half the bytes
+    of an all-reduce cross the links.  One reduce-scatter when the backend has
+    it and the rows split evenly; otherwise an all-reduce and a slice (same
+    result)."""
+    world, rank = _world(group), _rank(group)
+    lo, hi = shard_range(t.shape[0], rank, world)
+    if world == 1:
+        return t
+    if dist.get_backend(group) == "nccl" and t.shape[0] % world == 0 and t.is_contiguous():
+        out = torch.empty((hi - lo,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+        dist.reduce_scatter_tensor(out, t, op=dist.ReduceOp.SUM, group=group)
+        return out
+    allreduce_sum_(t, group=group)
+    return t[lo:hi]
 
 
 # ---- sharded layers -------------------------------------------------------------------

@@ -171,6 +171,12 @@ def _nccl_body(rank, world, dev):
     out.backward(_dev(dout, dev))
     of.backward(_dev(dout, dev))
     assert_bitexact(_host(shard.grad), _host(tf.grad)[off:off + rows], "dtable shard")
+    # reduce-scatter of a replicated table's gradient: this rank's rows of the sum
+    parts_t = [(_dev(np.arange(1000 * 16, dtype=np.float32).reshape(1000, 16), dev) * (r + 1))
+               for r in range(world)]
+    mine = S.reduce_scatter_rows(parts_t[rank].clone())
+    lo_t, hi_t = S.shard_range(1000, rank, world)
+    assert_bitexact(_host(mine), _host(sum(parts_t))[lo_t:hi_t], "reduce-scattered rows")
     # global sum of squares over row shards
     gsh = _dev(x[lo % 100:lo % 100 + 50], dev)
     tot = S.sum_squares([gsh])

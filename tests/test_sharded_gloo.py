@@ -108,6 +108,18 @@ def _collectives(rank, world):
     return None
 
 
+def _reduce_scatter_rows(rank, world):
+    """Each rank keeps its row shard of the sum over ranks (on gloo: the
+    all-reduce-and-slice path; 7 rows do not split evenly over 2 or 3)."""
+    from oxitorch_b200 import sharded as S
+    full = [torch.arange(7 * 3, dtype=torch.float32).reshape(7, 3) * (r + 1) for r in range(world)]
+    got = S.reduce_scatter_rows(full[rank].clone())
+    lo, hi = S.shard_range(7, rank, world)
+    want = sum(full)[lo:hi]
+    assert torch.equal(got, want)
+    return None
+
+
 def _layer_norm_grads(rank, world):
     """LayerNorm+GELU weight gradients: per-shard VJP partials summed over the
     ranks equal the whole-batch VJP."""
@@ -215,6 +227,11 @@ def test_shard_geometry(world):
 
 def test_collectives():
     _run(2, "_collectives")
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_reduce_scatter_rows(world):
+    _run(world, "_reduce_scatter_rows")
 
 
 @pytest.mark.parametrize("world", [2, 3])
