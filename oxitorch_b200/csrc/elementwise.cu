@@ -13,9 +13,14 @@
 // operand into strides over the output grid (0 on broadcast dims), drops
 // size-1 dims and merges dims that are contiguous for every operand.  Then:
 //   contiguous: every operand dense (or a scalar): 128-bit grid-stride loop;
-//   tiled:      a 2-D problem where an operand is column-major (a transposed
-//               view): 32x32 tiles through shared memory, so both the
-//               column-major read and the row-major write are coalesced;
+//   pipelined:  a 2-D problem with one column-major input (a transposed view)
+//               whose columns are 16-byte aligned, and the other input dense
+//               row-major or a scalar: the tile pipeline of tilepipe.cuh (TMA
+//               boxes for the transposed input, bulk row copies, long
+//               row-major segments);
+//   tiled:      other 2-D problems with a column-major operand: 32x32 tiles
+//               through shared memory, so both the column-major read and the
+//               row-major write are coalesced;
 //   general:    any strides, index arithmetic per element (up to 8 dims).
 // Outputs are always dense row-major, like the reference's from_results.
 #include <math.h>
@@ -25,6 +30,7 @@
 #include <cstring>
 
 #include "common.cuh"
+#include "tilepipe.cuh"
 
 namespace oxc {
 
@@ -210,6 +216,62 @@ __global__ void __launch_bounds__(256) elem_tiled_kernel(int kind, int op, Opera
   }
 }
 
+// Transposed-operand path on the tile pipeline (tilepipe.cuh), for 2-D
+// problems whose one column-major input has 16-byte aligned columns: that
+// input arrives as swizzled 2-D TMA boxes of 32 rows x 192 columns, a dense
+// row-major second input (ROW) as 768-byte bulk row copies, and 24 consumer
+// warps apply the op and stream the row-major output in full 32-byte sectors.
+// GB: the column-major input is operand b (the op keeps its argument order);
+// the other operand is the row-major tile or a scalar.
+template <bool GB, bool ROW>
+__global__ void __launch_bounds__(kTThreads, 1) elem_pipe_kernel(
+    const __grid_constant__ CUtensorMap gmap, View2 g, const float* __restrict__ rowp,
+    Operand other, int kind, int op, float* __restrict__ out, int64_t R, int64_t C) {
+  constexpr int NSLOT = ROW ? 2 : 1;
+  extern __shared__ unsigned char smem_raw[];
+  const TileRing<NSLOT, true> ring = make_tile_ring<NSLOT, true>(smem_raw, kStageFwd);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (warp == kTCW) {
+    const float* const src[2] = {rowp, nullptr};
+    tile_producer<true, NSLOT>(ring, &gmap, g, src, ROW ? 1 : 0, R, C);
+    return;
+  }
+  const float so = (!ROW && kind != EK_UNARY) ? scalar_value(other) : 0.0f;
+  const int t = 4 * (warp & 7) + (lane & 3);
+  const int fl = (warp >> 3) * (kTF / kTParts) + (lane >> 2);
+  const int goff = gate_off<true>(t, fl), roff = t * kTP + fl;
+  const int64_t nstrips = (R + kTT - 1) / kTT;
+  int64_t i = 0;
+  for (int64_t strip = blockIdx.x; strip < nstrips; strip += gridDim.x) {
+    const int64_t r = strip * kTT + t;
+    float* orow = out + r * C + fl;
+    for (int64_t c0 = 0; c0 < C; c0 += kTF, ++i) {
+      if (!tile_acquire(ring, i)) continue;
+      const int stage = (int)(i % ring.stages);
+      const float* gs = ring.slot(stage, 0) + goff;
+      const float* rs = ring.slot(stage, NSLOT - 1) + roff;
+      float gv[kTK], ov[kTK];
+#pragma unroll
+      for (int k = 0; k < kTK; ++k) {
+        gv[k] = gs[k * kGateStep<true>];
+        ov[k] = ROW ? rs[8 * k] : so;
+      }
+      tile_release(ring, i);
+      if (r >= R) continue;
+      const bool full = c0 + kTF <= C;
+#pragma unroll
+      for (int k = 0; k < kTK; ++k) {
+        if (full || c0 + fl + 8 * k < C) {
+          const float res = kind == EK_UNARY ? apply(kind, op, gv[k], 0.0f)
+                            : GB             ? apply(kind, op, ov[k], gv[k])
+                                             : apply(kind, op, gv[k], ov[k]);
+          st_stream(orow + c0 + 8 * k, res);
+        }
+      }
+    }
+  }
+}
+
 // ---- host-side view algebra (layout.rs) --------------------------------------
 
 static oxc_status view_ok(const oxc_view* v, const char* what) {
@@ -359,6 +421,38 @@ static oxc_status run_elementwise(int kind, int op, const oxc_view* a, const oxc
     const Operand* os[2] = {&oa, &ob};
     for (int k = 0; k < 2; ++k)
       if (!os[k]->scalar && g.st[k][0] == 1 && g.st[k][1] != 1) colmajor |= 1 << k;
+  }
+  if (colmajor == 1 || colmajor == 2) {
+    // one column-major input: the tile pipeline when its layout allows
+    const int k = colmajor == 1 ? 0 : 1;
+    const Operand& cm = k == 0 ? oa : ob;
+    const Operand& ot = k == 0 ? ob : oa;
+    const int64_t R = g.n[0], C = g.n[1];
+    const bool unary = kind == EK_UNARY;
+    const bool other_row = !unary && !ot.scalar && g.st[1 - k][1] == 1 && g.st[1 - k][0] == C &&
+                           aligned16(ot.p);
+    const bool shape_ok = C % 4 == 0 && C > 1 && R <= INT32_MAX && C <= INT32_MAX &&
+                          aligned16(cm.p) && g.st[k][1] % 4 == 0 && g.st[k][1] >= R;
+    if (shape_ok && (unary || ot.scalar || other_row)) {
+      const View2 gv{cm.p, g.st[k][0], g.st[k][1]};
+      CUtensorMap map{};
+      if (!gate_tensor_map(&map, gv, R, C))
+        return fail(OXC_ERR_OTHER, "%s: cuTensorMapEncodeTiled failed", fn);
+      const float* rowp = other_row ? ot.p : nullptr;
+      const size_t smem = other_row ? tile_smem_bytes<2, true>(kStageFwd, false)
+                                    : tile_smem_bytes<1, true>(kStageFwd, false);
+      if (k == 1 && other_row)
+        return launch_tile(elem_pipe_kernel<true, true>, smem, R, s, fn, nullptr, map, gv, rowp,
+                           ot, (int)kind, op, out->data, R, C);
+      if (k == 1)
+        return launch_tile(elem_pipe_kernel<true, false>, smem, R, s, fn, nullptr, map, gv, rowp,
+                           ot, (int)kind, op, out->data, R, C);
+      if (other_row)
+        return launch_tile(elem_pipe_kernel<false, true>, smem, R, s, fn, nullptr, map, gv, rowp,
+                           ot, (int)kind, op, out->data, R, C);
+      return launch_tile(elem_pipe_kernel<false, false>, smem, R, s, fn, nullptr, map, gv, rowp, ot,
+                         (int)kind, op, out->data, R, C);
+    }
   }
   if (colmajor) {
     const int64_t ntiles = ((g.n[0] + 31) / 32) * ((g.n[1] + 31) / 32);

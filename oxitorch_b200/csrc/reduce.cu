@@ -75,52 +75,84 @@ __device__ __forceinline__ float finish(int kind, float sum_or_v, int64_t idx, i
   }
 }
 
-// One CTA (WARPS = blockDim/32 warps) or one warp per output; strip contiguous.
-template <bool PER_WARP>
-__global__ void __launch_bounds__(256) reduce_row_kernel(int kind, const float* __restrict__ in,
-                                                         Layout L, int64_t nout,
-                                                         float* __restrict__ out) {
+// Per-element step of a row reduction, specialised on the kind.  A thread
+// scans its elements in increasing index order, so for argmax/argmin a strict
+// compare keeps the first occurrence; NaN never compares and is skipped unless
+// nothing else has been seen (f32::max's NaN-ignoring fold).
+template <int KIND>
+__device__ __forceinline__ void rpush(float& acc, float& bv, int64_t& bi, float x, int64_t j) {
+  if constexpr (KIND == RK_NORM) {
+    acc = __fadd_rn(acc, __fmul_rn(x, x));
+  } else if constexpr (KIND == RK_SUM || KIND == RK_MEAN) {
+    acc = __fadd_rn(acc, x);
+  } else if constexpr (KIND == RK_MAX) {
+    acc = fmaxf(acc, x);
+  } else if constexpr (KIND == RK_MIN) {
+    acc = fminf(acc, x);
+  } else {
+    const bool take = KIND == RK_ARGMAX ? x > bv : x < bv;
+    if (take || (bi < 0 && !isnan(x))) { bv = x; bi = j; }
+  }
+}
+
+template <int KIND>
+__device__ __forceinline__ void rcombine(float& acc, float& bv, int64_t& bi, float oa, float ov,
+                                         int64_t oi) {
+  if constexpr (KIND == RK_SUM || KIND == RK_MEAN || KIND == RK_NORM) acc = __fadd_rn(acc, oa);
+  else if constexpr (KIND == RK_MAX) acc = fmaxf(acc, oa);
+  else if constexpr (KIND == RK_MIN) acc = fminf(acc, oa);
+  else if (oi >= 0 && better(KIND, ov, oi, bv, bi)) { bv = ov; bi = oi; }
+}
+
+// One CTA (WARPS = blockDim/32 warps) or one warp per output; strip contiguous
+// (or any stride, scalar loads).  128-bit loads, four in flight per thread.
+template <int KIND, bool PER_WARP>
+__global__ void __launch_bounds__(256) reduce_row_kernel(const float* __restrict__ in, Layout L,
+                                                         int64_t nout, float* __restrict__ out) {
   __shared__ float sv[33];
   __shared__ long long si[33];
+  constexpr bool kArg = KIND == RK_ARGMAX || KIND == RK_ARGMIN;
+  constexpr bool kSum = KIND == RK_SUM || KIND == RK_MEAN || KIND == RK_NORM;
+  constexpr float kInit = kSum ? 0.0f : (KIND == RK_MAX || KIND == RK_ARGMAX ? -INFINITY : INFINITY);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int lanes = PER_WARP ? 32 : blockDim.x;
   const int tid = PER_WARP ? lane : threadIdx.x;
   const int64_t per_block = PER_WARP ? blockDim.x / 32 : 1;
-  const bool sumlike = kind == RK_SUM || kind == RK_MEAN || kind == RK_NORM;
   for (int64_t o0 = (int64_t)blockIdx.x * per_block; o0 < nout; o0 += (int64_t)gridDim.x * per_block) {
     const int64_t o = o0 + (PER_WARP ? warp : 0);
-    float acc = sumlike ? 0.0f : (kind == RK_MAX || kind == RK_ARGMAX ? -INFINITY : INFINITY);
+    float acc = kInit, bv = kInit;
     int64_t bi = -1;
-    float bv = 0.0f;
     if (o < nout) {
       const float* p = in + base_offset(L, o);
       const bool v4 = L.sd == 1 && (reinterpret_cast<uintptr_t>(p) & 15) == 0;
       int64_t j0 = 0;
       if (v4) {
+        const float4* p4 = reinterpret_cast<const float4*>(p);
         const int64_t nv = L.len / 4;
-        for (int64_t v = tid; v < nv; v += lanes) {
-          const float4 q = ld_stream(reinterpret_cast<const float4*>(p) + v);
-          const float e[4] = {q.x, q.y, q.z, q.w};
+        int64_t v = tid;
+        for (; v + 3 * lanes < nv; v += 4 * lanes) {
+          float4 q[4];
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float x = e[k];
-            if (kind == RK_NORM) acc = __fadd_rn(acc, __fmul_rn(x, x));
-            else if (sumlike) acc = __fadd_rn(acc, x);
-            else if (kind == RK_MAX) acc = fmaxf(acc, x);
-            else if (kind == RK_MIN) acc = fminf(acc, x);
-            else if (better(kind, x, 4 * v + k, bv, bi)) { bv = x; bi = 4 * v + k; }
+          for (int u = 0; u < 4; ++u) q[u] = ld_stream(p4 + v + u * lanes);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int64_t j = 4 * (v + u * lanes);
+            rpush<KIND>(acc, bv, bi, q[u].x, j);
+            rpush<KIND>(acc, bv, bi, q[u].y, j + 1);
+            rpush<KIND>(acc, bv, bi, q[u].z, j + 2);
+            rpush<KIND>(acc, bv, bi, q[u].w, j + 3);
           }
+        }
+        for (; v < nv; v += lanes) {
+          const float4 q = ld_stream(p4 + v);
+          rpush<KIND>(acc, bv, bi, q.x, 4 * v);
+          rpush<KIND>(acc, bv, bi, q.y, 4 * v + 1);
+          rpush<KIND>(acc, bv, bi, q.z, 4 * v + 2);
+          rpush<KIND>(acc, bv, bi, q.w, 4 * v + 3);
         }
         j0 = nv * 4;
       }
-      for (int64_t j = j0 + tid; j < L.len; j += lanes) {
-        const float x = ld_stream(p + j * L.sd);
-        if (kind == RK_NORM) acc = __fadd_rn(acc, __fmul_rn(x, x));
-        else if (sumlike) acc = __fadd_rn(acc, x);
-        else if (kind == RK_MAX) acc = fmaxf(acc, x);
-        else if (kind == RK_MIN) acc = fminf(acc, x);
-        else if (better(kind, x, j, bv, bi)) { bv = x; bi = j; }
-      }
+      for (int64_t j = j0 + tid; j < L.len; j += lanes) rpush<KIND>(acc, bv, bi, ld_stream(p + j * L.sd), j);
     }
     // warp combine (fixed order)
 #pragma unroll
@@ -128,44 +160,51 @@ __global__ void __launch_bounds__(256) reduce_row_kernel(int kind, const float* 
       const float oa = __shfl_xor_sync(0xffffffffu, acc, off);
       const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
       const long long oi = __shfl_xor_sync(0xffffffffu, (long long)bi, off);
-      if (sumlike) acc = __fadd_rn(acc, oa);
-      else if (kind == RK_MAX) acc = fmaxf(acc, oa);
-      else if (kind == RK_MIN) acc = fminf(acc, oa);
-      else if (oi >= 0 && better(kind, ov, oi, bv, bi)) { bv = ov; bi = oi; }
+      rcombine<KIND>(acc, bv, bi, oa, ov, oi);
     }
     if (!PER_WARP) {
       __syncthreads();
-      if (lane == 0) { sv[warp] = (kind == RK_ARGMAX || kind == RK_ARGMIN) ? bv : acc; si[warp] = bi; }
+      if (lane == 0) { sv[warp] = kArg ? bv : acc; si[warp] = bi; }
       __syncthreads();
       if (warp == 0) {
         const int nw = blockDim.x / 32;
-        float a2 = lane < nw ? sv[lane] : (sumlike ? 0.0f : (kind == RK_MAX || kind == RK_ARGMAX ? -INFINITY : INFINITY));
-        long long i2 = lane < nw ? si[lane] : -1;
+        float a2 = lane < nw ? sv[lane] : kInit;
+        int64_t i2 = lane < nw ? si[lane] : -1;
         float b2 = a2;
-        if (kind == RK_ARGMAX || kind == RK_ARGMIN) { if (i2 < 0) b2 = 0.0f; }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) {
-          const float oa = __shfl_xor_sync(0xffffffffu, a2, off);
-          const long long oi = __shfl_xor_sync(0xffffffffu, i2, off);
-          if (sumlike) a2 = __fadd_rn(a2, oa);
-          else if (kind == RK_MAX) a2 = fmaxf(a2, oa);
-          else if (kind == RK_MIN) a2 = fminf(a2, oa);
-          else if (oi >= 0 && better(kind, oa, oi, b2, i2)) { b2 = oa; i2 = oi; a2 = oa; }
+          const float oa = __shfl_xor_sync(0xffffffffu, kArg ? b2 : a2, off);
+          const long long oi = __shfl_xor_sync(0xffffffffu, (long long)i2, off);
+          rcombine<KIND>(a2, b2, i2, oa, oa, oi);
         }
         acc = a2;
         bi = i2;
       }
     }
     if ((PER_WARP ? lane == 0 : threadIdx.x == 0) && o < nout) {
-      if (kind == RK_ARGMAX || kind == RK_ARGMIN) {
+      if (kArg) {
         // a NaN at index 0 keeps index 0 (the reference starts from data[0])
         const float first = in[base_offset(L, o)];
-        out[o] = isnan(first) ? 0.0f : finish(kind, 0.0f, bi, L.len);
+        out[o] = isnan(first) ? 0.0f : finish(KIND, 0.0f, bi, L.len);
       } else {
-        out[o] = finish(kind, acc, -1, L.len);
+        out[o] = finish(KIND, acc, -1, L.len);
       }
     }
     if (!PER_WARP) __syncthreads();
+  }
+}
+
+template <bool PER_WARP>
+static void launch_reduce_row(int kind, unsigned grid, cudaStream_t s, const float* in,
+                              const Layout& L, int64_t nout, float* out) {
+  switch (kind) {
+    case RK_SUM: reduce_row_kernel<RK_SUM, PER_WARP><<<grid, 256, 0, s>>>(in, L, nout, out); break;
+    case RK_MEAN: reduce_row_kernel<RK_MEAN, PER_WARP><<<grid, 256, 0, s>>>(in, L, nout, out); break;
+    case RK_MAX: reduce_row_kernel<RK_MAX, PER_WARP><<<grid, 256, 0, s>>>(in, L, nout, out); break;
+    case RK_MIN: reduce_row_kernel<RK_MIN, PER_WARP><<<grid, 256, 0, s>>>(in, L, nout, out); break;
+    case RK_ARGMAX: reduce_row_kernel<RK_ARGMAX, PER_WARP><<<grid, 256, 0, s>>>(in, L, nout, out); break;
+    case RK_ARGMIN: reduce_row_kernel<RK_ARGMIN, PER_WARP><<<grid, 256, 0, s>>>(in, L, nout, out); break;
+    default: reduce_row_kernel<RK_NORM, PER_WARP><<<grid, 256, 0, s>>>(in, L, nout, out); break;
   }
 }
 
@@ -634,12 +673,12 @@ oxc_status oxc_reduce(int32_t kind, const oxc_view* in, int64_t dim, int32_t kee
   }
   if (P.row) {
     if (P.L.len >= 2048) {
-      reduce_row_kernel<false><<<(unsigned)std::min<int64_t>(P.nout, cap), 256, 0, s>>>(
-          kind, in->data, P.L, P.nout, out->data);
+      launch_reduce_row<false>(kind, (unsigned)std::min<int64_t>(P.nout, cap), s, in->data, P.L,
+                               P.nout, out->data);
     } else {
       const int64_t blocks = (P.nout + 7) / 8;
-      reduce_row_kernel<true><<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(blocks, cap)), 256, 0, s>>>(
-          kind, in->data, P.L, P.nout, out->data);
+      launch_reduce_row<true>(kind, (unsigned)std::max<int64_t>(1, std::min<int64_t>(blocks, cap)),
+                              s, in->data, P.L, P.nout, out->data);
     }
     return check_launch("oxc_reduce");
   }

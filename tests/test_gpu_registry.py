@@ -124,6 +124,50 @@ def test_binary_scalar_both_sides(oracle, name):
         assert_bitexact(got, oracle.t_binary(name, np.float32(2.5), x.reshape(17, 59)), name)
 
 
+def _transposed(x, pad=0):
+    """Device view of x [R, C] that is column-major: the transpose of a
+    [C, R + pad] buffer (column stride R + pad)."""
+    import torch
+    r, c = x.shape
+    buf = torch.zeros(c, r + pad, device="cuda")
+    buf[:, :r] = _dev(np.ascontiguousarray(x.T))
+    return buf[:, :r].t()
+
+
+@pytest.mark.parametrize("shape", [(300, 1100), (33, 196), (1000, 388)])
+def test_transposed_operand_paths(oracle, shape):
+    """One column-major input with 16-byte aligned columns takes the tile
+    pipeline (TMA boxes for the transposed input); a misaligned column stride
+    takes the 32x32 tiles.  Every result must match the oracle on the dense
+    values: unary ops, both operand orders of non-commutative binaries, and
+    scalars on either side."""
+    from oxitorch_b200 import tensor_ops as T
+    r, c = shape
+    x = _values(r + c, r * c)[: r * c].reshape(r, c)
+    y = np.random.default_rng(c).standard_normal((r, c)).astype(np.float32)
+    for pad in (0, 1):  # pad 1: column stride r + 1, not a multiple of 4
+        xt = _transposed(x, pad)
+        assert xt.stride() == (1, r + pad)
+        for name in ("neg", "sqrt", "reciprocal", "sigmoid", "exp"):
+            got = _host(T.unary_op(name, xt))
+            want = oracle.t_unary(name, x)
+            if name in EXACT_UNARY:
+                assert_bitexact(got, want, f"{name} pad {pad}")
+            else:
+                _assert_ulps(got, want, LIBM_ULPS[name], f"{name} pad {pad}")
+        for name in ("sub", "div", "max", "mul"):
+            assert_bitexact(_host(T.binary_op(name, xt, _dev(y))), oracle.t_binary(name, x, y),
+                            f"{name}(T, dense) pad {pad}")
+            assert_bitexact(_host(T.binary_op(name, _dev(y), xt)), oracle.t_binary(name, y, x),
+                            f"{name}(dense, T) pad {pad}")
+            assert_bitexact(_host(T.binary_op(name, xt, 1.75)),
+                            oracle.t_binary(name, x, np.float32(1.75)), f"{name}(T, s) pad {pad}")
+            assert_bitexact(_host(T.binary_op(name, 1.75, xt)),
+                            oracle.t_binary(name, np.float32(1.75), x), f"{name}(s, T) pad {pad}")
+        got = _host(T.cmp_op("lt", xt, _dev(y)))
+        assert_bitexact(got, oracle.t_cmp("lt", x, y), f"lt(T, dense) pad {pad}")
+
+
 def test_cmp_ops_bitexact(oracle):
     from oxitorch_b200 import tensor_ops as T
     x = _values(11, 2000)
