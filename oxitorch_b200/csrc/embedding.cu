@@ -186,8 +186,8 @@ __device__ __forceinline__ void store_acc(float* dst, int cols, int c_base,
 // Block j of the sorted array: partial sums of the (at most two) pieces of
 // rows that occur more than kSplitP times.  Slot 2j: the row covering
 // position j*P (if split); slot 2j+1: a split row that starts inside block j.
-template <int VW, int VPT>
-__global__ void __launch_bounds__(256) emb_split_kernel(
+template <int VW, int VPT, int MAXT>
+__global__ void __launch_bounds__(MAXT) emb_split_kernel(
     const float* __restrict__ dout, const int32_t* __restrict__ skeys,
     const int32_t* __restrict__ spos, const int32_t* __restrict__ offsets, int64_t n,
     int64_t rows, int cols, float* __restrict__ parts) {
@@ -216,8 +216,8 @@ __global__ void __launch_bounds__(256) emb_split_kernel(
   }
 }
 
-template <int VW, int VPT>
-__global__ void __launch_bounds__(256) emb_rows_kernel(
+template <int VW, int VPT, int MAXT>
+__global__ void __launch_bounds__(MAXT) emb_rows_kernel(
     const float* __restrict__ dout, const int32_t* __restrict__ spos,
     const int32_t* __restrict__ offsets, const float* __restrict__ parts, int64_t rows, int cols,
     float* __restrict__ dtable) {
@@ -400,15 +400,18 @@ oxc_status oxc_embedding_bwd(const float* dout, const int64_t* ids, float* dtabl
   const int64_t nblocks = (n + kSplitP - 1) / kSplitP;
   const unsigned grows = (unsigned)std::min<int64_t>(rows, (int64_t)sm_count() * 32);
   if (v4) {
-    emb_split_kernel<4, 4><<<(unsigned)nblocks, 256, 0, s>>>(dout, keys_out, vals_out, offsets, n,
-                                                             rows, (int)cols, parts);
-    emb_rows_kernel<4, 4><<<grows, 256, 0, s>>>(dout, vals_out, offsets, parts, rows, (int)cols,
-                                                dtable);
+    // one float4 column slice per thread, up to 1024 threads per row: the
+    // rows in flight cost few registers, so many warps share each SM
+    const int block = (int)std::min<int64_t>(1024, std::max<int64_t>(32, ((cols / 4 + 31) / 32) * 32));
+    emb_split_kernel<4, 1, 1024><<<(unsigned)nblocks, block, 0, s>>>(
+        dout, keys_out, vals_out, offsets, n, rows, (int)cols, parts);
+    emb_rows_kernel<4, 1, 1024><<<grows, block, 0, s>>>(dout, vals_out, offsets, parts, rows,
+                                                        (int)cols, dtable);
   } else {
-    emb_split_kernel<1, 4><<<(unsigned)nblocks, 256, 0, s>>>(dout, keys_out, vals_out, offsets, n,
-                                                             rows, (int)cols, parts);
-    emb_rows_kernel<1, 4><<<grows, 256, 0, s>>>(dout, vals_out, offsets, parts, rows, (int)cols,
-                                                dtable);
+    emb_split_kernel<1, 4, 256><<<(unsigned)nblocks, 256, 0, s>>>(dout, keys_out, vals_out, offsets,
+                                                                  n, rows, (int)cols, parts);
+    emb_rows_kernel<1, 4, 256><<<grows, 256, 0, s>>>(dout, vals_out, offsets, parts, rows,
+                                                     (int)cols, dtable);
   }
   return check_launch("oxc_embedding_bwd");
 }
