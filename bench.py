@@ -244,6 +244,26 @@ def run_reference(args, rank, world):
 
 # ---- GPU workloads --------------------------------------------------------------------------
 
+def _time_ops(torch, ops):
+    """GB/s of each kernel on its own: {name: (callable, bytes)}, CUDA events,
+    median of 5 runs after 2 warm-ups."""
+    import statistics
+    out = {}
+    for name, (fn, nbytes) in ops.items():
+        for _ in range(2):
+            fn()
+        ts = []
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        out[name] = round(nbytes / (statistics.median(ts) * 1e-3) / 1e9, 1)
+    return out
+
+
 class Workload:
     """Inputs resident on the device; fwd()/bwd() launch the path's kernels on
     the current stream; exchange() is the data-parallel collective (N > 1)."""
@@ -406,6 +426,24 @@ class CrossEntropy(Workload):
         self.total = R * world
         self.fwd_bytes = R * (4 * C + 8 + 12) + 4
         self.bwd_bytes = R * (8 * C + 8 + 8)
+
+    def per_op(self):
+        """The standalone F.softmax / F.log_softmax kernels on the same logits
+        (forward reads x and writes y; the VJP reads y and dy and writes dx)."""
+        t = self.torch
+        y, dx = self.dx, t.empty_like(self.x)
+        R, C = self.rows, self.cols
+        L, N, s = self.L, self.N, self.s
+        ops = {}
+        for log in (0, 1):
+            name = "log_softmax" if log else "softmax"
+            ops[f"{name} forward"] = (lambda log=log: N.check(L.oxc_softmax_fwd(
+                self.x.data_ptr(), y.data_ptr(), R, C, log, s)), 8 * R * C)
+            ops[f"{name} VJP"] = (lambda log=log: N.check(L.oxc_softmax_bwd(
+                y.data_ptr(), self.x.data_ptr(), dx.data_ptr(), R, C, log, s)), 12 * R * C)
+        out = _time_ops(t, ops)
+        del dx
+        return out
 
     def fwd(self, x=None):
         self.N.check(self.L.oxc_cross_entropy_fwd(
@@ -646,7 +684,6 @@ class Registry(Workload):
 
     def per_op(self):
         """GB/s of each kernel on its own (CUDA events, median of 5 after 2 warm-ups)."""
-        import statistics
         torch = self.torch
         g = self.gate_buf.t()
         MH = self.M * self.H
@@ -663,20 +700,7 @@ class Registry(Workload):
             "argmax over dim 1": (lambda: self._red(self.R_ARGMAX, self.h, self.ha),
                                   4 * MH + 4 * self.M),
         }
-        out = {}
-        for name, (fn, nbytes) in ops.items():
-            for _ in range(2):
-                fn()
-            ts = []
-            for _ in range(5):
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record()
-                fn()
-                e1.record()
-                torch.cuda.synchronize()
-                ts.append(e0.elapsed_time(e1))
-            out[name] = round(nbytes / (statistics.median(ts) * 1e-3) / 1e9, 1)
-        return out
+        return _time_ops(torch, ops)
 
     def e2e_io(self):
         return [self.gate_buf, self.up, self.dh], [self.h, self.hs, self.hm, self.ha, self.dg,
