@@ -24,7 +24,8 @@
 //     exp, -log p_target) and never materialises a full-size tensor.
 //   ce_loss: deterministic f64 tree over the per-row values.
 //   ce_bwd: grid-stride elementwise over [rows, cols] (128-bit when cols % 4
-//     == 0), per-row (max, 1/s, target) read through L1.
+//     == 0), per-row (max, 1/s, target) read through L1; rows of >= 2048
+//     classes go to ce_bwd_rows (one CTA per row, same per-element expression).
 #include <math.h>
 
 #include <algorithm>
@@ -176,6 +177,9 @@ __global__ void __launch_bounds__(512) softmax_fwd_kernel(const float* __restric
     float* yr = y + row * (int64_t)cols;
     const MaxSum st = row_maxsum<VW>(xr, cols, scratch);
     const float logs = LOG ? logf(st.s) : 0.0f;
+    // exp(x - m) / s as exp(x - m) * (1/s): within one ulp of the quotient,
+    // one multiply per element instead of a division
+    const float inv = LOG ? 0.0f : __frcp_rn(st.s);
     if constexpr (VW == 4) {
       const float4* x4 = reinterpret_cast<const float4*>(xr);
       float4* y4 = reinterpret_cast<float4*>(yr);
@@ -187,15 +191,15 @@ __global__ void __launch_bounds__(512) softmax_fwd_kernel(const float* __restric
           o.x = (q.x - st.m) - logs; o.y = (q.y - st.m) - logs;
           o.z = (q.z - st.m) - logs; o.w = (q.w - st.m) - logs;
         } else {
-          o.x = __fdiv_rn(expf(q.x - st.m), st.s); o.y = __fdiv_rn(expf(q.y - st.m), st.s);
-          o.z = __fdiv_rn(expf(q.z - st.m), st.s); o.w = __fdiv_rn(expf(q.w - st.m), st.s);
+          o.x = expf(q.x - st.m) * inv; o.y = expf(q.y - st.m) * inv;
+          o.z = expf(q.z - st.m) * inv; o.w = expf(q.w - st.m) * inv;
         }
         st_stream(y4 + v, o);
       }
     } else {
       for (int c = threadIdx.x; c < cols; c += blockDim.x) {
         const float q = ld_stream(xr + c);
-        st_stream(yr + c, LOG ? (q - st.m) - logs : __fdiv_rn(expf(q - st.m), st.s));
+        st_stream(yr + c, LOG ? (q - st.m) - logs : expf(q - st.m) * inv);
       }
     }
   }
@@ -379,6 +383,50 @@ __global__ void __launch_bounds__(256) ce_bwd_kernel(const float* __restrict__ x
   }
 }
 
+// The same VJP for rows of at least kCeRowCols classes, laid out like the
+// softmax kernels: one CTA per row at a time, so the row's max, 1/sum scale and
+// target are loaded once per row instead of once per vector, and four float4
+// vectors in flight per thread.  Each element's expression is the one
+// ce_bwd_kernel evaluates, so the two give identical bits.
+constexpr int kCeRowCols = 2048;
+
+__global__ void __launch_bounds__(512) ce_bwd_rows_kernel(const float* __restrict__ x,
+                                                          const int64_t* __restrict__ targets,
+                                                          const float* __restrict__ row_max,
+                                                          const float* __restrict__ row_sum,
+                                                          const float* __restrict__ grad_loss,
+                                                          float* __restrict__ dx, int64_t rows,
+                                                          int cols, float inv_total) {
+  const float g = grad_loss ? __ldg(grad_loss) : 1.0f;
+  const float gm = g * inv_total;
+  const int nv = cols >> 2;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float m = __ldg(row_max + row);
+    const float scale = gm * __fdiv_rn(1.0f, __ldg(row_sum + row));
+    const int64_t t = resolve_target(__ldg(targets + row), cols);
+    const float4* x4 = reinterpret_cast<const float4*>(x + row * (int64_t)cols);
+    float4* d4 = reinterpret_cast<float4*>(dx + row * (int64_t)cols);
+    auto out = [&](const float4& q, int v) {
+      const int c0 = 4 * v;
+      float4 o;
+      o.x = scale * expf(q.x - m) + (c0 + 0 == t ? -gm : -0.0f);
+      o.y = scale * expf(q.y - m) + (c0 + 1 == t ? -gm : -0.0f);
+      o.z = scale * expf(q.z - m) + (c0 + 2 == t ? -gm : -0.0f);
+      o.w = scale * expf(q.w - m) + (c0 + 3 == t ? -gm : -0.0f);
+      return o;
+    };
+    int v = threadIdx.x;
+    for (; v + 3 * (int)blockDim.x < nv; v += 4 * blockDim.x) {
+      float4 q[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) q[u] = ld_stream(x4 + v + u * blockDim.x);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) st_stream(d4 + v + u * blockDim.x, out(q[u], v + u * blockDim.x));
+    }
+    for (; v < nv; v += blockDim.x) st_stream(d4 + v, out(ld_stream(x4 + v), v));
+  }
+}
+
 static unsigned row_grid(int64_t rows) {
   const int64_t cap = (int64_t)sm_count() * 64;
   return (unsigned)(rows < cap ? rows : cap);
@@ -488,6 +536,11 @@ oxc_status oxc_cross_entropy_bwd(const float* logits, const int64_t* targets,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool v4 = cols % 4 == 0 && aligned16(logits) && aligned16(dlogits);
   const float inv_total = 1.0f / (float)total_rows;  // the mean VJP's 1/M (f32)
+  if (v4 && cols >= kCeRowCols) {
+    ce_bwd_rows_kernel<<<row_grid(rows), row_block(cols), 0, s>>>(
+        logits, targets, row_max, row_sum, grad_loss, dlogits, rows, (int)cols, inv_total);
+    return check_launch("oxc_cross_entropy_bwd");
+  }
   const int block = 256;
   const int64_t work = rows * (v4 ? cols / 4 : cols);
   const int64_t cap = (int64_t)sm_count() * 8 * 4;  // 8 CTAs of 256 per SM, 4 waves of ILP
