@@ -235,6 +235,39 @@ def test_layer_norm_gelu_config2_rows(oracle):
     _check_ln(x, w, dy, _ln_dev(x, w, b, dy, True), ref, True)
 
 
+@pytest.mark.parametrize("n", [4096, 4094])
+def test_gelu_evaluation_vs_f64(n):
+    """The kernels' GELU and its derivative at exactly known arguments, against
+    float64.  A row of alternating +1/-1 has mean 0 and variance 1 exactly, so
+    with weight 0 the affine output is fma(xhat, 0, b) = b: y = gelu(b).  With
+    one row and dy = 1, dbias = gelu'(b).  n = 4096 runs the pipelined kernels,
+    n = 4094 (not a multiple of 4) the register kernels.
+
+    Bound: a few ulp, plus 4 ulp of the exponent's size |2 c v| (v = b + k b^3):
+    the rounding of v moves e^(-2 c v) by that much in relative terms, which is
+    the formula's own conditioning far into the negative tail.  Results below
+    1e-36 in magnitude may flush to zero (ex2/rcp run flush-to-zero)."""
+    x = np.tile(np.array([1.0, -1.0], np.float32), (1, n // 2))
+    b = np.linspace(-10.0, 10.0, n).astype(np.float32)
+    b[:12] = [0.0, 1e-20, -1e-20, 1e-3, -1e-3, -0.7517916, 30.0, -30.0, 45.0, -45.0, 5.5, -5.5]
+    w = np.zeros(n, np.float32)
+    dy = np.ones((1, n), np.float32)
+    y, _, _, db, mean, rstd = _ln_dev(x, w, b, dy, True)
+    assert mean[0] == 0.0 and rstd[0] == np.float32(1.0 / np.sqrt(np.float32(1.0) + np.float32(1e-5)))
+    c = np.float64(np.float32(np.sqrt(2.0 / np.pi)))
+    k = np.float64(np.float32(0.044715))
+    b64 = b.astype(np.float64)
+    v = b64 + k * b64 ** 3
+    with np.errstate(over="ignore"):
+        s = 1.0 / (1.0 + np.exp(-2.0 * c * v))
+    g64 = b64 * s
+    d64 = s + 2.0 * b64 * s * (1.0 - s) * c * (1.0 + 3.0 * k * b64 ** 2)
+    rel = 2.0 ** -24 * (8.0 + 4.0 * np.abs(2.0 * c * v))
+    assert_close(y[0], g64, rtol=0, atol=rel * np.abs(g64) + 1e-36, what="gelu(b)")
+    dscale = np.abs(s) + np.abs(2.0 * b64 * s * (1.0 - s) * c * (1.0 + 3.0 * k * b64 ** 2))
+    assert_close(db, d64, rtol=0, atol=rel * dscale + 1e-36, what="gelu'(b)")
+
+
 def test_layer_norm_exact_mode_vs_torch_autograd():
     import torch
     x, w, b, dy = _ln_case(21, 64, 1024)
