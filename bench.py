@@ -408,7 +408,7 @@ class CrossEntropy(Workload):
     DESC = ("log_softmax+cross_entropy (mean) fwd+bwd, fp32, logits [32768, 32000] per GPU "
             "(BASELINE config 3)")
     SEED = 3
-    KERNEL = "ce_bwd_kernel (cross-entropy VJP)"
+    KERNEL = "ce_bwd_rows_kernel (cross-entropy VJP)"
     launches = 3
 
     def __init__(self, dev, rank, world, args):
@@ -541,7 +541,7 @@ class MlpBlock(Workload):
             "(broadcast weight view), SwiGLU [.., 11008] (transposed gate view), dim-1 "
             "sum/max/argmax, whole-tensor L2 of {dx, dg, du} (BASELINE config 5)")
     SEED = 5
-    KERNEL = "swiglu_bwd_kernel (SwiGLU VJP, sum-of-squares fused)"
+    KERNEL = "swiglu_bwd_tile_kernel (SwiGLU VJP, sum-of-squares fused)"
     launches = 8
 
     def __init__(self, dev, rank, world, args):
@@ -629,7 +629,7 @@ class Registry(Workload):
             "forward; the graph's eight elementwise VJP ops backward; gate a transposed view "
             "(BASELINE config 5, strided engine)")
     SEED = 6
-    KERNEL = "elem_dense_kernel / elem_tiled_kernel (registry binary ops of the VJP)"
+    KERNEL = "elem_dense_kernel / elem_pipe_kernel (registry binary ops of the VJP)"
     launches = 14  # sigmoid, 2 mul, 3 reductions; 7 binary + 1 scalar-binary
     E2E_LARGE = True
     MUL, ADD, SUB, SIGMOID = 2, 0, 1, 12

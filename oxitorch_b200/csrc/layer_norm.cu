@@ -14,17 +14,17 @@
 //   dx   = gc - (sum_row gc) / cols            (sub and mean VJPs, ops.rs:49-56, 340-349)
 // OXC_GRAD_EXACT: dx = inv * (gw - mean(gw) - xhat*mean(gw*xhat)), gw = g*w.
 //
-// Two implementations of each direction:
-//   *_pipe_kernel: rows with cols % 4 == 0 and 16-byte aligned tensors.  One
-//     persistent CTA per SM; a producer warp streams whole rows into a shared-
-//     memory ring with bulk copies (pipeline.cuh) while 16 consumer warps
-//     compute, so HBM stays busy during the arithmetic.  Used for the VJP and
-//     for LayerNorm+GELU forward.
-//   *_kernel: any width up to 32768, register-resident rows, plain loads.  The
-//     forward takes mean and variance from one block reduction (a shifted
-//     one-pass sum, corrected by a second pass when the shift was poor); for the
-//     plain LayerNorm it runs
-//     persistent with the next row prefetched, which keeps HBM at copy speed.
+// Kernels:
+//   ln_fwd_kernel: any width up to 32768, register-resident rows, plain loads;
+//     mean and variance from one block reduction (a shifted one-pass sum,
+//     corrected by a second pass when the shift was poor).  Aligned float4
+//     rows of up to 16384 columns run it persistent with the next row
+//     prefetched and 8 vectors per thread where the row allows (row_geom_deep).
+//   ln_bwd_pipe_kernel: the VJP for rows with cols % 4 == 0 and 16-byte
+//     aligned tensors.  One persistent CTA per SM; a producer warp streams
+//     whole rows into a shared-memory ring with bulk copies (pipeline.cuh)
+//     while 16 consumer warps compute, so HBM stays busy during the arithmetic.
+//   ln_bwd_kernel: the VJP for other rows, register-resident.
 #include <math.h>
 
 #include <algorithm>
@@ -106,10 +106,9 @@ __device__ __forceinline__ float2 block_sum2(float a, float b, float* scratch) {
 
 // Forward, register-resident rows.  PF: persistent CTAs that load their next
 // row into registers before working on the current one, so a row's loads are
-// in flight while the previous row is reduced and stored (the plain LayerNorm:
-// HBM-bound).  !PF: one row per CTA and fewer registers, so more CTAs share an
-// SM (LayerNorm+GELU: the activation's arithmetic needs the warps more than
-// the prefetch).
+// in flight while the previous row is reduced and stored.  !PF: one row per
+// CTA and fewer registers (LayerNorm+GELU on rows the prefetching geometry
+// does not cover: unaligned, or wider than 16384 columns).
 //
 // Statistics in one block reduction: sums around a pilot K (the mean of the
 // row's first min(cols, 32) elements, which every warp computes on its own
@@ -349,84 +348,6 @@ __device__ __forceinline__ void stage_params(float* ws, const float* w, float* b
   }
 }
 
-template <int NG, int NWG, int VPT, int ACT>
-__global__ void __launch_bounds__((NG * NWG + 1) * 32, 1) ln_fwd_pipe_kernel(
-    const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
-    float* __restrict__ y, float* __restrict__ mean_out, float* __restrict__ rstd_out,
-    int64_t rows, int cols, int64_t chunk, int stages, float eps, GeluConst gc) {
-  extern __shared__ unsigned char smem[];
-  float* red;
-  const RowRing<1> ring = make_ring<1, NWG>(smem, stages, cols, &red);
-  float* ws = red + 64;
-  float* bs = ws + cols;
-  stage_params(ws, w, bs, b, cols);
-  __syncthreads();
-  const int64_t r0 = (int64_t)blockIdx.x * chunk;
-  const int64_t r1 = min(rows, r0 + chunk);
-  const int warp = threadIdx.x >> 5;
-  if (warp == NG * NWG) {
-    if ((threadIdx.x & 31) == 0 && r0 < r1) {
-      const float* src[1] = {x};
-      produce_rows<1>(ring, src, r0, r1);
-    }
-    return;
-  }
-  constexpr int T = NWG * 32;
-  const int g = warp / NWG, gt = threadIdx.x - g * T, bar = 1 + g;
-  float* gred = red + g * (NWG + 1);
-  const int nvec = cols >> 2;
-  const float4* w4 = reinterpret_cast<const float4*>(ws);
-  const float4* b4 = reinterpret_cast<const float4*>(bs);
-  for (int64_t i = g; i < r1 - r0; i += NG) {
-    const int64_t row = r0 + i;
-    const bool ok = consumer_acquire<1>(ring, i);
-    const float4* src = reinterpret_cast<const float4*>(ring.row((int)(i % ring.stages), 0));
-    float4 v[VPT];
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      const int slot = k * T + gt;
-      v[k] = (ok && slot < nvec) ? src[slot] : make_float4(0, 0, 0, 0);
-    }
-    consumer_release<1>(ring, i);
-    float s = 0.0f;
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
-    s = group_sum<NWG>(s, gred, bar);
-    const float mu = __fdiv_rn(s, (float)cols);
-    float ss = 0.0f;
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      v[k].x -= mu; v[k].y -= mu; v[k].z -= mu; v[k].w -= mu;
-      const float q = (v[k].x * v[k].x + v[k].y * v[k].y) + (v[k].z * v[k].z + v[k].w * v[k].w);
-      if (k * T + gt < nvec) ss += q;
-    }
-    ss = group_sum<NWG>(ss, gred, bar);
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(ss, (float)cols) + eps));
-    float4* yr = reinterpret_cast<float4*>(y + row * (int64_t)cols);
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      const int slot = k * T + gt;
-      if (ok && slot < nvec) {
-        const float4 wv = w4[slot], bv = b4[slot];
-        float4 o;
-        o.x = fmaf(v[k].x * inv, wv.x, bv.x);
-        o.y = fmaf(v[k].y * inv, wv.y, bv.y);
-        o.z = fmaf(v[k].z * inv, wv.z, bv.z);
-        o.w = fmaf(v[k].w * inv, wv.w, bv.w);
-        if constexpr (ACT == OXC_ACT_GELU_TANH) {
-          o.x = gelu_fwd(o.x, gc); o.y = gelu_fwd(o.y, gc);
-          o.z = gelu_fwd(o.z, gc); o.w = gelu_fwd(o.w, gc);
-        }
-        st_stream(yr + slot, o);
-      }
-    }
-    if (gt == 0 && ok) {
-      mean_out[row] = mu;
-      rstd_out[row] = inv;
-    }
-  }
-}
-
 // SACC: the per-group dweight/dbias accumulators live in shared memory
 // (2 * cols floats per group after w and b) instead of registers.
 template <int NG, int NWG, int VPT, int ACT, int MODE, bool SACC>
@@ -618,7 +539,6 @@ __global__ void __launch_bounds__((NG * NWG + 1) * 32, 1) ln_bwd_pipe_kernel(
 }
 
 // Pipeline geometry: NG groups x NWG warps.
-constexpr int kFwdNG = 4, kFwdNWG = 4;   // 4 rows in flight, 128 threads per row
 constexpr int kBwdNG = 2, kBwdNWG = 8;   // 2 rows in flight, 256 threads per row
 
 // Max dynamic shared memory per block (opt-in) of the current device.
@@ -699,38 +619,33 @@ oxc_status oxc_layer_norm_fwd(const float* x, const float* w, const float* b, fl
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool v4 = cols % 4 == 0 && aligned16(x) && aligned16(w) && aligned16(b) && aligned16(y);
   const GeluConst gc = gelu_const();
-  // LayerNorm+GELU: the pipelined kernel (the activation's arithmetic keeps
-  // the register kernel's warps busy); plain LayerNorm: the register kernel
-  const int stages =
-      v4 && act == OXC_ACT_GELU_TANH ? pipe_stages(1, cols, 8, kFwdNG + 1) : 0;
-  const int vpt = v4 ? pipe_vpt(cols, kFwdNWG, 8) : 0;
-  if (stages && vpt) {
-    const int64_t ctas = std::min<int64_t>(rows, sm_count());
-    const int64_t chunk = (rows + ctas - 1) / ctas;
-    const size_t smem = ring_smem_bytes(1, cols, stages, 2 * cols);
-    const int block = (kFwdNG * kFwdNWG + 1) * 32;
-#define LAUNCH_P(VPT, ACT)                                                                  \
-  do {                                                                                      \
-    auto k = ln_fwd_pipe_kernel<kFwdNG, kFwdNWG, VPT, ACT>;                                 \
-    allow_smem(k, smem);                                                                    \
-    k<<<(unsigned)ctas, block, smem, s>>>(x, w, b, y, mean, rstd, rows, (int)cols, chunk,   \
-                                          stages, eps, gc);                                 \
+  // float4 rows that fit 8 vectors per thread on at most 512 threads (up to
+  // 16384 columns): the persistent register kernel, next row prefetched, with
+  // the deep geometry -- for plain LayerNorm and LayerNorm+GELU alike
+  const RowGeom deep = v4 ? row_geom_deep(cols) : RowGeom{};
+  if (deep.ok && deep.block <= 512) {
+    auto ctas = [&](const void* k) {
+      const int64_t fit = (int64_t)sm_count() * std::max(1, occupancy(k, deep.block, 0));
+      return (unsigned)std::min<int64_t>(rows, fit);
+    };
+#define LAUNCH_D(VW, VPT, MAXT)                                                            \
+  do {                                                                                     \
+    if (act == OXC_ACT_GELU_TANH) {                                                        \
+      auto k = ln_fwd_kernel<VW, VPT, MAXT, OXC_ACT_GELU_TANH, true>;                      \
+      k<<<ctas((const void*)k), deep.block, 0, s>>>(x, w, b, y, mean, rstd, rows,          \
+                                                    (int)cols, eps, gc);                   \
+    } else {                                                                               \
+      auto k = ln_fwd_kernel<VW, VPT, MAXT, OXC_ACT_NONE, true>;                           \
+      k<<<ctas((const void*)k), deep.block, 0, s>>>(x, w, b, y, mean, rstd, rows,          \
+                                                    (int)cols, eps, gc);                   \
+    }                                                                                      \
   } while (0)
-#define LAUNCH_A(VPT)                                                                       \
-  do {                                                                                      \
-    if (act == OXC_ACT_GELU_TANH) LAUNCH_P(VPT, OXC_ACT_GELU_TANH);                         \
-    else LAUNCH_P(VPT, OXC_ACT_NONE);                                                       \
-  } while (0)
-    switch (vpt) {
-      case 1: LAUNCH_A(1); break;
-      case 2: LAUNCH_A(2); break;
-      case 4: LAUNCH_A(4); break;
-      default: LAUNCH_A(8); break;
-    }
-#undef LAUNCH_A
-#undef LAUNCH_P
+    OXC_DISPATCH_ROW(deep, LAUNCH_D);
+#undef LAUNCH_D
     return check_launch("oxc_layer_norm_fwd");
   }
+  // wider or unaligned rows: one row per CTA for LayerNorm+GELU, persistent
+  // for plain LayerNorm
   RowGeom g = row_geom(cols, v4);
   const unsigned grid = (unsigned)(rows < 0x7fffffff ? rows : 0x7fffffff);
   // persistent: as many CTAs as fit on the GPU at once, each looping over rows
