@@ -185,7 +185,13 @@ oxc_status oxc_rms_norm_fwd(const float* x, const float* w, float* y, float* rst
     return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: rms_norm: null pointer");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool v4 = cols % 4 == 0 && aligned16(x) && aligned16(w) && aligned16(y);
+  // float4 rows: 8 vectors per thread where the row allows (on B200, 3% over
+  // 256 threads x 4 vectors at [16384, 4096])
   RowGeom g = row_geom(cols, v4);
+  if (v4) {
+    const RowGeom d = row_geom_deep(cols);
+    if (d.ok && d.block <= 512) g = d;
+  }
   const unsigned grid = (unsigned)(rows < 0x7fffffff ? rows : 0x7fffffff);
 #define LAUNCH(VW, VPT, MAXT) \
   rms_fwd_kernel<VW, VPT, MAXT><<<grid, g.block, 0, s>>>(x, w, y, rstd, rows, (int)cols, eps)
