@@ -168,6 +168,35 @@ def test_transposed_operand_paths(oracle, shape):
         assert_bitexact(got, oracle.t_cmp("lt", x, y), f"lt(T, dense) pad {pad}")
 
 
+@pytest.mark.parametrize("pad", [0, 1])
+def test_transposed_every_op(oracle, pad):
+    """Every unary op, and every binary op with a scalar on either side, on a
+    column-major view: pad 0 takes the tile pipeline, whose consumers select
+    one op-specialised loop per tile; pad 1 the 32x32 tiles."""
+    from oxitorch_b200 import tensor_ops as T
+    r, c = 257, 392
+    x = _values(5, r * c)[: r * c].reshape(r, c)
+    xt = _transposed(x, pad)
+    for name in EXACT_UNARY + list(LIBM_ULPS):
+        got = _host(T.unary_op(name, xt))
+        want = oracle.t_unary(name, x)
+        if name in EXACT_UNARY:
+            if name == "relu":  # f32::max(-0.0, 0.0) may return either zero
+                got, want = got + 0.0, want + 0.0
+            assert_bitexact(got, want, f"{name} pad {pad}")
+        else:
+            _assert_ulps(got, want, LIBM_ULPS[name], f"{name} pad {pad}")
+    for name in ("add", "sub", "mul", "div", "min", "max", "pow"):
+        for s, first in ((1.75, False), (-0.5, True)):
+            got = _host(T.binary_op(name, s, xt) if first else T.binary_op(name, xt, s))
+            want = (oracle.t_binary(name, np.float32(s), x) if first
+                    else oracle.t_binary(name, x, np.float32(s)))
+            if name == "pow":
+                _assert_ulps(got, want, 6, f"pow pad {pad} scalar first {first}")
+            else:
+                assert_bitexact(got, want, f"{name} pad {pad} scalar first {first}")
+
+
 def test_cmp_ops_bitexact(oracle):
     from oxitorch_b200 import tensor_ops as T
     x = _values(11, 2000)
