@@ -295,7 +295,7 @@ class LnGelu(Workload):
             "(BASELINE config 2)")
     SEED = 2
     KERNEL = "ln_bwd_pipe_kernel (layer_norm+gelu VJP) + dweight/dbias finisher"
-    launches = 4
+    launches = 3  # forward, VJP, dweight+dbias finisher
 
     def __init__(self, dev, rank, world, args):
         super().__init__(dev, rank, world, args)

@@ -67,10 +67,17 @@ int occupancy(const void* kernel, int block, size_t smem) {
 // Column sums of per-CTA partials.  CTA = 32 warps x 32 columns; warp w adds
 // parts w, w+32, w+64, ... (4 loads in flight), then warp 0 adds the 32 warp
 // results in warp order.  Fixed order => deterministic.
-__global__ void __launch_bounds__(1024) colsum_partials_kernel(const float* __restrict__ parts,
+// blockIdx.y selects the column set: (parts1, out1) or (parts2, out2), so the
+// dweight and dbias sums of a VJP finish in one launch.
+__global__ void __launch_bounds__(1024) colsum_partials_kernel(const float* __restrict__ parts1,
                                                                int nparts, int64_t cols,
-                                                               float* __restrict__ out) {
+                                                               float* __restrict__ out1,
+                                                               const float* __restrict__ parts2,
+                                                               float* __restrict__ out2) {
+  const float* __restrict__ parts = blockIdx.y ? parts2 : parts1;
+  float* __restrict__ out = blockIdx.y ? out2 : out1;
   __shared__ float red[32][33];
+  pdl_wait();  // the partials are the previous kernel's output
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t col = (int64_t)blockIdx.x * 32 + lane;
   float acc = 0.0f;
@@ -98,9 +105,9 @@ __global__ void __launch_bounds__(1024) colsum_partials_kernel(const float* __re
 }
 
 void launch_colsum_partials(const float* parts, int nparts, int64_t cols, float* out,
-                            cudaStream_t stream) {
-  const int64_t grid = (cols + 31) / 32;
-  colsum_partials_kernel<<<(unsigned)grid, 1024, 0, stream>>>(parts, nparts, cols, out);
+                            cudaStream_t stream, const float* parts2, float* out2) {
+  launch_dependent(colsum_partials_kernel, dim3((unsigned)((cols + 31) / 32), parts2 ? 2u : 1u),
+                   dim3(1024), stream, parts, nparts, cols, out, parts2, out2);
 }
 
 }  // namespace oxc

@@ -106,11 +106,48 @@ __device__ __forceinline__ float block_max(float v, float* scratch) {
   return scratch[32];
 }
 
+// Programmatic dependent launch.  A kernel launched with the
+// programmatic-stream-serialization attribute may be scheduled while the
+// kernel before it in the stream is still running; pdl_wait() then blocks
+// until that kernel has completed and its memory is visible, so it must come
+// before any read of the predecessor's output.  pdl_launch_dependents() in the
+// predecessor lets the dependent be scheduled once every CTA of the
+// predecessor has issued it (or exited), so a dependent never takes resources
+// that a predecessor CTA still waits for.  Both are no-ops without the
+// attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Launches `kernel` as a programmatic dependent of the previous kernel in the
+// stream (the kernel must call pdl_wait() before it reads that kernel's
+// output).  A launch error is left for check_launch().
+template <typename... KArgs, typename... Args>
+inline void launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t s,
+                             Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // Column sums of `parts` [nparts, cols] into out[cols] (f32), in a fixed
-// order: warp w of a CTA sums parts w, w+8, ... for 32 columns, then warp
+// order: warp w of a CTA sums parts w, w+32, ... for 32 columns, then warp
 // partials are added in warp order.  Used to finish per-CTA weight-gradient
-// partials deterministically.
+// partials deterministically.  With parts2/out2 a second set of the same
+// shape is summed in the same launch.  Launched as a programmatic dependent
+// of the VJP kernel that wrote the partials (that kernel calls
+// pdl_launch_dependents()).
 void launch_colsum_partials(const float* parts, int nparts, int64_t cols, float* out,
-                            cudaStream_t stream);
+                            cudaStream_t stream, const float* parts2 = nullptr,
+                            float* out2 = nullptr);
 
 }  // namespace oxc

@@ -192,6 +192,9 @@ __global__ void __launch_bounds__(MAXT) emb_split_kernel(
     const float* __restrict__ dout, const int32_t* __restrict__ skeys,
     const int32_t* __restrict__ spos, const int32_t* __restrict__ offsets, int64_t n,
     int64_t rows, int cols, float* __restrict__ parts) {
+  // emb_rows_kernel may start on the rows that need no pieces while this grid
+  // runs (it was launched after the sort and offsets had completed)
+  pdl_launch_dependents();
   const int64_t j = blockIdx.x;
   const int64_t b0 = j * kSplitP, b1 = min(n, b0 + kSplitP);
   if (b0 >= n) return;
@@ -223,6 +226,11 @@ __global__ void __launch_bounds__(MAXT) emb_rows_kernel(
     const float* __restrict__ dout, const int32_t* __restrict__ spos,
     const int32_t* __restrict__ offsets, const float* __restrict__ parts, int64_t rows, int cols,
     float* __restrict__ dtable) {
+  // Launched as a programmatic dependent of emb_split_kernel: rows with at
+  // most kSplitP occurrences read only the sort's output and run while the
+  // split grid is still working; rows made of pieces wait for it (pdl_wait)
+  // before reading `parts`, and every CTA waits once more before it exits,
+  // so this grid never completes ahead of the split grid.
   const int nvec = cols / VW;
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const int64_t s0 = offsets[r], s1 = offsets[r + 1];
@@ -237,6 +245,7 @@ __global__ void __launch_bounds__(MAXT) emb_rows_kernel(
       if (s1 - s0 <= kSplitP) {
         sum_positions<VW, VPT>(dout, spos, s0, s1, cols, c_base, acc);
       } else {
+        pdl_wait();  // the pieces are the split grid's output
         // pieces in block order, eight partial rows in flight per step
         const int64_t j0 = s0 / kSplitP, j1 = (s1 - 1) / kSplitP;
         constexpr int UJ = 8;
@@ -276,6 +285,7 @@ __global__ void __launch_bounds__(MAXT) emb_rows_kernel(
       store_acc<VW, VPT>(dst, cols, c_base, acc, true);
     }
   }
+  pdl_wait();
 }
 
 struct EmbLayout {
@@ -416,13 +426,13 @@ oxc_status oxc_embedding_bwd(const float* dout, const int64_t* ids, float* dtabl
   if (v4) {
     emb_split_kernel<4, 1, kEmbChunkThreads><<<gsplit, block, 0, s>>>(
         dout, keys_out, vals_out, offsets, n, rows, (int)cols, parts);
-    emb_rows_kernel<4, 1, kEmbChunkThreads><<<grow, block, 0, s>>>(dout, vals_out, offsets, parts,
-                                                                   rows, (int)cols, dtable);
+    launch_dependent(emb_rows_kernel<4, 1, kEmbChunkThreads>, grow, block, s, dout, vals_out,
+                     offsets, (const float*)parts, rows, (int)cols, dtable);
   } else {
     emb_split_kernel<1, 4, kEmbChunkThreads><<<gsplit, block, 0, s>>>(
         dout, keys_out, vals_out, offsets, n, rows, (int)cols, parts);
-    emb_rows_kernel<1, 4, kEmbChunkThreads><<<grow, block, 0, s>>>(dout, vals_out, offsets, parts,
-                                                                   rows, (int)cols, dtable);
+    launch_dependent(emb_rows_kernel<1, 4, kEmbChunkThreads>, grow, block, s, dout, vals_out,
+                     offsets, (const float*)parts, rows, (int)cols, dtable);
   }
   return check_launch("oxc_embedding_bwd");
 }

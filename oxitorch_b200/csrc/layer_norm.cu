@@ -232,6 +232,7 @@ __global__ void __launch_bounds__(MAXT) ln_bwd_kernel(
     const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
     const float* __restrict__ dy, float* __restrict__ dx, float* __restrict__ parts,
     int64_t rows, int cols, int64_t chunk, GeluConst gc) {
+  pdl_launch_dependents();  // the dweight/dbias finisher waits for this grid
   __shared__ float scratch[33];
   const int64_t r0 = (int64_t)blockIdx.x * chunk;
   const int64_t r1 = min(rows, r0 + chunk);
@@ -356,6 +357,7 @@ __global__ void __launch_bounds__((NG * NWG + 1) * 32, 1) ln_bwd_pipe_kernel(
     const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
     const float* __restrict__ dy, float* __restrict__ dx, float* __restrict__ parts,
     int64_t rows, int cols, int64_t chunk, int stages, GeluConst gc) {
+  pdl_launch_dependents();  // the dweight/dbias finisher waits for this grid
   extern __shared__ unsigned char smem[];
   float* red;
   const RowRing<2> ring = make_ring<2, NWG>(smem, stages, cols, &red);
@@ -753,8 +755,7 @@ oxc_status oxc_layer_norm_bwd(const float* x, const float* w, const float* b, co
 #undef LAUNCH_P
     oxc_status st = check_launch("oxc_layer_norm_bwd");
     if (st) return st;
-    launch_colsum_partials(parts, (int)ctas, cols, dw, s);
-    launch_colsum_partials(parts + ctas * cols, (int)ctas, cols, db, s);
+    launch_colsum_partials(parts, (int)ctas, cols, dw, s, parts + ctas * cols, db);
     return check_launch("oxc_layer_norm_bwd (dw, db)");
   }
   RowGeom g = row_geom(cols, v4, 512);
@@ -780,8 +781,7 @@ oxc_status oxc_layer_norm_bwd(const float* x, const float* w, const float* b, co
 #undef LAUNCH_M
   oxc_status st = check_launch("oxc_layer_norm_bwd");
   if (st) return st;
-  launch_colsum_partials(parts, (int)ctas, cols, dw, s);
-  launch_colsum_partials(parts + ctas * cols, (int)ctas, cols, db, s);
+  launch_colsum_partials(parts, (int)ctas, cols, dw, s, parts + ctas * cols, db);
   return check_launch("oxc_layer_norm_bwd (dw, db)");
 }
 

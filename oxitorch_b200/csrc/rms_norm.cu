@@ -71,6 +71,7 @@ __global__ void __launch_bounds__(MAXT) rms_bwd_kernel(
     const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ rstd,
     const float* __restrict__ dy, float* __restrict__ dx, float* __restrict__ parts, int64_t rows,
     int cols, int64_t chunk) {
+  pdl_launch_dependents();  // the dweight finisher waits for this grid
   __shared__ float scratch[33];
   const int64_t r0 = (int64_t)blockIdx.x * chunk;
   const int64_t r1 = min(rows, r0 + chunk);
