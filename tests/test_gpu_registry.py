@@ -9,7 +9,8 @@
   f32::max and first-occurrence argmax); column-mode sums/means/norms
   bit-exact (same left-to-right order as the reference); tree-order sums
   within rtol 1e-5 (1e-4 from 32k elements) plus the reference's own
-  summation-order error.
+  summation-order error, and on long rows 1e-6 x sum|terms| (a reordered sum
+  of cancelling terms).
 """
 
 import json
@@ -267,6 +268,42 @@ def test_reduce_all_kinds_dims(oracle, kind, dim, keepdim):
             oracle.PRECISE_SUMS[0] = False
             budget = np.abs(want.astype(np.float64) - exact)
             assert_close(got, want, rtol=RTOL, atol=ATOL + budget, what=what)
+
+
+@pytest.mark.parametrize("shape", [(9600, 2100), (500, 4100)])
+def test_reduce_long_rows_both_geometries(oracle, shape):
+    """Rows of 2048+ elements over dim 1: with at least 64 outputs per SM
+    (9600 rows on 148 SMs) a warp takes each output, with fewer (500 rows) a
+    CTA.  Every kind against the oracle; ties and NaNs placed in some rows.
+    The kernels sum in a tree, the reference left to right, so sums are held
+    to 1e-6 x sum|terms| per row (the column-sum convention of tests/parity.py):
+    a row of 2100 N(0,1) values can sum to ~1 with sum|x| ~ 1700."""
+    import torch
+    from oxitorch_b200 import tensor_ops as T
+    rng = np.random.default_rng(shape[0])
+    a = rng.standard_normal(shape, dtype=np.float32)
+    a[3, 100:110] = 7.5      # ties: the first index wins
+    a[7, 1999] = np.nan      # NaN ignored by max/argmax
+    a[8, 0] = np.nan         # NaN at index 0: argmax keeps 0
+    warps = shape[0] >= torch.cuda.get_device_properties(0).multi_processor_count * 64
+    assert warps == (shape[0] == 9600)
+    d = _dev(a)
+    for kind in ("sum", "mean", "max", "min", "argmax", "argmin", "norm"):
+        got = _host(T.reduce(kind, d, 1))
+        want = oracle.t_reduce(kind, a, 1, False)
+        what = f"{kind} {shape}"
+        if kind in ("max", "min", "argmax", "argmin"):
+            assert_bitexact(got, want, what)
+        else:
+            oracle.PRECISE_SUMS[0] = True
+            exact = oracle.t_reduce(kind, a, 1, False)
+            oracle.PRECISE_SUMS[0] = False
+            budget = np.abs(want.astype(np.float64) - exact)
+            terms = np.abs(a.astype(np.float64))
+            scale = {"sum": terms.sum(1), "mean": terms.mean(1),
+                     "norm": np.sqrt((terms * terms).sum(1))}[kind]
+            assert_close(got, want, rtol=RTOL, atol=ATOL * np.maximum(scale, 1.0) + budget,
+                         what=what)
 
 
 def test_reduce_column_mode_is_the_reference_order(oracle):
