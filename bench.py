@@ -270,6 +270,7 @@ class Workload:
 
     dominant = "bwd"       # the kernel the roofline reports
     launches = 0           # our kernels per step
+    ROWS = ("rows", "rows")  # (attribute holding the rows per GPU step, unit)
 
     def __init__(self, dev, rank, world, args):
         import torch
@@ -498,6 +499,7 @@ class Embedding(Workload):
     KERNEL = "emb_gather_kernel (forward gather)"
     dominant = "fwd"
     launches = 9  # gather; prepare, sort (4 CUB passes), offsets, split, rows
+    ROWS = ("n", "tokens")
 
     def __init__(self, dev, rank, world, args):
         super().__init__(dev, rank, world, args)
@@ -559,6 +561,7 @@ class MlpBlock(Workload):
     SEED = 5
     KERNEL = "swiglu_bwd_tile_kernel (SwiGLU VJP, sum-of-squares fused)"
     launches = 8
+    ROWS = ("M", "tokens")
 
     def __init__(self, dev, rank, world, args):
         super().__init__(dev, rank, world, args)
@@ -650,6 +653,7 @@ class Registry(Workload):
     E2E_LARGE = True
     MUL, ADD, SUB, SIGMOID = 2, 0, 1, 12
     R_SUM, R_MAX, R_ARGMAX = 0, 2, 4
+    ROWS = ("M", "tokens")
 
     def __init__(self, dev, rank, world, args):
         super().__init__(dev, rank, world, args)
@@ -881,6 +885,9 @@ def run_ours(args, rank, world, local_rank):
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": ms_per_step,
+        # whole-job rows (or tokens) per second, on the same device time as value
+        "rows_per_s": {"value": world * getattr(wl, wl.ROWS[0]) / (ms_per_step * 1e-3),
+                       "unit": f"{wl.ROWS[1]}/s"},
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
