@@ -17,6 +17,9 @@ parity configs; the headline line is config 2):
              ids [64, 2048] Zipf(1.1) clipped
   mlp_block  config 5: RMSNorm + SwiGLU (transposed gate view) + dim-1
              sum/max/argmax + whole-tensor L2 of {dx, dg, du}, 65536 tokens
+  registry   config 5 through the generic elementwise registry and reductions
+  optim      the optimizer step on device (the scope table's next row):
+             AdamW step + SGD Nesterov-momentum step over 2^28-float parameters
 
 `value` is whole-job algorithmic GB/s: sum over ranks of the bytes each kernel
 must move (each input read once, each output written once) divided by the max
@@ -174,6 +177,14 @@ def cpu_sample(workload, seed):
         for grad in (xt.grad.numpy(), gt.grad.numpy(), ut.grad.numpy()):
             R.sumsq_all_f64(grad)
         return time.perf_counter() - t0, m * (20 * dmod + 32 * hid) + 12 * dmod
+    if workload == "optim":
+        n = 1 << 20
+        p = rng.standard_normal(n, dtype=np.float32)
+        g = rng.standard_normal(n, dtype=np.float32)
+        t0 = time.perf_counter()
+        R.adamw_step(p, g, None, None, 1e-3, 0.9, 0.999, 1e-8, 0.01, True, 1)
+        R.sgd_step(p, g, None, 1e-2, 0.9, True)
+        return time.perf_counter() - t0, 48 * n
     if workload == "registry":
         m, hid = 16, 11008
         g = rng.standard_normal((m, hid), dtype=np.float32)
@@ -739,8 +750,59 @@ class Registry(Workload):
                 "l2": "no flush: every tensor (2.9 GB) is larger than L2"}
 
 
+class Optim(Workload):
+    DESC = ("optimizer step on device, fp32: AdamW (forward phase) and SGD with Nesterov "
+            "momentum (backward phase), each over a flat parameter of 2^28 elements per GPU")
+    SEED = 7
+    KERNEL = "adam_kernel (AdamW step)"
+    dominant = "fwd"
+    launches = 2
+    E2E_LARGE = True
+    ROWS = ("n", "elements")
+
+    def __init__(self, dev, rank, world, args):
+        super().__init__(dev, rank, world, args)
+        n = self.n = args.rows or (1 << 28)
+        self.p, self.g = self.randn(n), self.randn(n) * 0.01
+        self.m = self.torch.zeros(n, device=dev)
+        self.v = self.torch.zeros(n, device=dev)
+        self.p2 = self.randn(n)
+        self.vel = self.torch.zeros(n, device=dev)
+        self.t = 0
+        self.fwd_bytes = 28 * n  # read p, g, m, v; write p, m, v
+        self.bwd_bytes = 20 * n  # read p, g, buf; write p, buf
+
+    def fwd(self, g=None):
+        self.t += 1
+        self.N.check(self.L.oxc_adamw_step(
+            self.p.data_ptr(), (g if g is not None else self.g).data_ptr(), self.m.data_ptr(),
+            self.v.data_ptr(), self.n, 1e-3, 0.9, 0.999, 1e-8, 0.01, 1, self.t, self.s))
+
+    def bwd(self, g=None):
+        self.N.check(self.L.oxc_sgd_step(
+            self.p2.data_ptr(), (g if g is not None else self.g).data_ptr(), self.vel.data_ptr(),
+            self.n, 1e-2, 0.9, 1, self.s))
+
+    def exchange(self):
+        pass  # data-parallel replicas apply the same all-reduced gradient: nothing crosses
+
+    def e2e_io(self):
+        return [self.g], [self.p, self.p2]
+
+    def e2e_step(self, dev_in):
+        self.fwd(dev_in[0])
+        self.bwd(dev_in[0])
+
+    def config(self):
+        return {"workload": self.DESC, "elements_per_gpu": self.n,
+                "hyperparameters": "AdamW lr 1e-3, betas (0.9, 0.999), eps 1e-8, wd 0.01; "
+                                   "SGD lr 1e-2, momentum 0.9, Nesterov",
+                "parallelism": f"data-parallel replicas x{self.world}, no exchange in the step",
+                "l2": "no flush: every tensor (1.07 GB) is larger than the 126 MB L2"}
+
+
 WORKLOADS = {"ln_gelu": LnGelu, "rms": Rms, "ce": CrossEntropy, "embedding": Embedding,
-             "mlp_block": MlpBlock, "registry": Registry}
+             "mlp_block": MlpBlock, "registry": Registry, "optim": Optim}
 
 
 def run_ours(args, rank, world, local_rank):
@@ -793,8 +855,11 @@ def run_ours(args, rank, world, local_rank):
     # ---- e2e: host buffers through the C ABI --------------------------------------------
     e2e = None
     if getattr(wl, "E2E_LARGE", False) and not args.e2e_large:
-        e2e = {"value": None, "unit": "GB/s", "skipped": "config 5 moves ~9-23 GB per step through "
-               "pinned host buffers; pass --e2e-large to measure it"}
+        ins, outs = wl.e2e_io()
+        gb = sum(t.numel() * t.element_size() for t in ins + outs) / 1e9
+        e2e = {"value": None, "unit": "GB/s",
+               "skipped": f"this workload moves {gb:.1f} GB per step through pinned host "
+                          "buffers; pass --e2e-large to measure it"}
     elif not args.skip_e2e:
         ins, outs = wl.e2e_io()
         h_in = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t) for t in ins]

@@ -90,6 +90,27 @@ oxc_status oxc_check_error_flag(int32_t* flag_dev, void* stream, int64_t timeout
 #define OXC_KERR_PIPELINE_TIMEOUT 1u
 oxc_status oxc_kernel_error(uint32_t* bits, int32_t clear);
 
+/* ---- optimizer step (crates/oxi-autograd/src/optim.rs) ------------------
+ * Both update one flat f32 parameter in place, the per-element arithmetic in
+ * the reference's order and rounding, so results are the reference's bits.
+ * The caller owns the state buffers (zero-initialised before a parameter's
+ * first step, as the reference's lazily created slots are) and skips
+ * parameters that have no gradient.
+ *
+ * oxc_sgd_step: Sgd::step_param (optim.rs:104-138).  velocity [n] is used
+ *   (and may be null otherwise) when momentum > 0; nesterov needs
+ *   momentum > 0 (OXC_ERR_INVALID_ARGUMENT, the reference's ValueError).
+ * oxc_adamw_step: AdamW::step_param (optim.rs:223-261): decoupled != 0 is
+ *   AdamW (decay on the parameter), 0 classic Adam (decay added to the
+ *   gradient).  step = the parameter's own step counter including this step
+ *   (1 on its first step); the bias corrections 1 - beta^step use the C
+ *   library's powf, like the reference's f32::powf.  m, v: [n]. */
+oxc_status oxc_sgd_step(float* param, const float* grad, float* velocity, int64_t n, float lr,
+                        float momentum, int32_t nesterov, void* stream);
+oxc_status oxc_adamw_step(float* param, const float* grad, float* m, float* v, int64_t n,
+                          float lr, float beta1, float beta2, float eps, float weight_decay,
+                          int32_t decoupled, int64_t step, void* stream);
+
 /* ---- registry ids: the order of the reference registry tables ---------
  * binary: add,sub,mul,div,pow,min,max          (crates/oxi-tensor/src/ops.rs:55-91)
  * cmp:    eq,ne,lt,le,gt,ge                    (ops.rs:96-121)

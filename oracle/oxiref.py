@@ -832,3 +832,60 @@ def colsum_abs_prod_f64(a, b=None):
     lib().oxr_colsum_abs_prod_f64(_fp(a), None if bb is None else _fp(bb), rows, cols,
                                   out.ctypes.data_as(F64P))
     return out
+
+
+# ---- optimizer step (crates/oxi-autograd/src/optim.rs) ---------------------------------------
+#
+# Per element, every operation a float32 operation rounded on its own, in the
+# reference's order (Rust does not contract a*b + c).  numpy float32 array
+# arithmetic rounds each ufunc result, so the expressions below are the
+# reference's.  Hyperparameters arrive as Python floats and are rounded to f32
+# as the reference's constructors do (``as f32``, optim.rs:79-86, 186-205).
+
+_libm = None
+
+
+def _powf(x, y):
+    """C ``powf`` -- the function Rust's ``f32::powf`` calls (glibc here)."""
+    global _libm
+    if _libm is None:
+        _libm = ctypes.CDLL("libm.so.6")
+        _libm.powf.restype = ctypes.c_float
+        _libm.powf.argtypes = [ctypes.c_float, ctypes.c_float]
+    return np.float32(_libm.powf(float(np.float32(x)), float(np.float32(y))))
+
+
+def sgd_step(param, grad, buf, lr, momentum, nesterov):
+    """``Sgd::step_param`` (optim.rs:104-138) on flat float32 arrays; returns
+    (new param, new velocity buffer or None when momentum == 0)."""
+    p, g = f32(param), f32(grad)
+    lr, mom = np.float32(lr), np.float32(momentum)
+    if mom > 0.0:
+        buf = f32(np.zeros_like(g) if buf is None else buf)
+        buf = (mom * buf + g).astype(np.float32)             # :117-119
+        upd = (g + mom * buf).astype(np.float32) if nesterov else buf  # :120-127
+    else:
+        buf, upd = None, g                                   # :128-130
+    return (p - lr * upd).astype(np.float32), buf            # :132-136
+
+
+def adamw_step(param, grad, m, v, lr, beta1, beta2, eps, weight_decay, decoupled, t):
+    """``AdamW::step_param`` (optim.rs:223-261) on flat float32 arrays, ``t`` the
+    parameter's own step counter including this step; returns (param, m, v)."""
+    p, g = f32(param), f32(grad)
+    m = f32(np.zeros_like(g) if m is None else m)
+    v = f32(np.zeros_like(g) if v is None else v)
+    lr, b1, b2 = np.float32(lr), np.float32(beta1), np.float32(beta2)
+    eps, wd = np.float32(eps), np.float32(weight_decay)
+    one = np.float32(1.0)
+    bc1 = one - _powf(b1, np.float32(t))                     # :253
+    bc2 = one - _powf(b2, np.float32(t))                     # :254
+    ge = (g + wd * p).astype(np.float32) if (not decoupled and wd != 0.0) else g   # :263-267
+    m = (b1 * m + (one - b1) * ge).astype(np.float32)        # :268
+    v = (b2 * v + (one - b2) * ge * ge).astype(np.float32)   # :269 (left to right)
+    m_hat = (m / bc1).astype(np.float32)                     # :270
+    v_hat = (v / bc2).astype(np.float32)                     # :271
+    nxt = (p - lr * m_hat / (np.sqrt(v_hat) + eps)).astype(np.float32)  # :272
+    if decoupled and wd != 0.0:
+        nxt = (nxt - lr * wd * p).astype(np.float32)         # :273-275
+    return nxt, m, v

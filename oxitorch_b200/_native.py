@@ -95,6 +95,8 @@ SIGNATURES = {
     "oxc_embedding_bwd": (_I32, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _SZ, _P]),
     "oxc_layer_norm_bwd_noalloc": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32,
                                           _I32, _P]),
+    "oxc_sgd_step": (_I32, [_P, _P, _P, _I64, _F32, _F32, _I32, _P]),
+    "oxc_adamw_step": (_I32, [_P, _P, _P, _P, _I64, _F32, _F32, _F32, _F32, _F32, _I32, _I64, _P]),
 }
 
 NOALLOC_SCRATCH_BYTES = 16 * 1024 * 1024
