@@ -111,6 +111,86 @@ oxc_status oxc_adamw_step(float* param, const float* grad, float* m, float* v, i
                           float lr, float beta1, float beta2, float eps, float weight_decay,
                           int32_t decoupled, int64_t step, void* stream);
 
+/* ---- data path: dataset columns in device memory, batches built on device --
+ * The reference's DataLoader (crates/oxi-bindings/src/data.rs:116-330) gathers
+ * each batch on CPU worker threads (TensorBatchSource::get_batch,
+ * crates/oxi-data/src/batch.rs:378-387 -> gather_columns :411-425) and runs the
+ * augmentation pipeline on the image column (transform.rs:105-223).  Here the
+ * columns stay on the device and a whole epoch is materialised by two
+ * launches; the host supplies the order and the per-plane draws.
+ *
+ * oxc_gather_rows: for every column c, dst_c[i] = src_c[idx[i]] (rows of
+ *   row_bytes bytes), i < nidx; idx is a device array.  Ids outside
+ *   [0, nrows) are recorded in err_flag (int32[4], may be null) and skipped
+ *   (read it with oxc_check_error_flag: gather_columns' OutOfBounds).
+ * oxc_image_epoch: the image column gathered and transformed in one pass.
+ *   Output plane q (out_h x out_w floats at out + q*out_h*out_w) reads, for
+ *   row r and column x, element (r + row_offset, col_base + col_step*x) of
+ *   the in_h x in_w plane starting at element src_offset of the virtual
+ *   tensor src[order[0..nidx)] (rows of row_elems floats), then applies nnorm
+ *   normalize steps in order, v = (v - mean[c]) * inv[c] with
+ *   c = planes[q].channel; norm is a device array [nnorm][2][channels]
+ *   (mean, then 1/std rounded to f32), at most 4 steps.  planes: device
+ *   array from oxc_epoch_transform_plan; a plane whose map points outside
+ *   its source plane, or whose order entry is outside [0, nrows), is
+ *   recorded in err_flag and skipped.
+ *
+ * Host-side helpers (no device work):
+ * oxc_epoch_seed: the per-epoch seed, SplitMix64 of base + epoch*golden
+ *   (EpochSeeds::next, data.rs:43-55).
+ * oxc_batch_seed: batch_seed(epoch_seed, FNV-1a of the batch's indices)
+ *   (transform.rs:231-244, batch.rs:394-404).
+ * oxc_permutation: MT19937(seed) Fisher-Yates order of 0..n, NumPy's
+ *   RandomState.permutation stream (rng.rs:84-95).
+ * oxc_epoch_transform_plan: for the batches order[k*batch_size ..] of an
+ *   epoch, draws every batch's random crops and flips from
+ *   MT19937(batch_rng(oxc_batch_seed(epoch_seed, batch))) in the reference's
+ *   order and composes the steps into one oxc_plane_map per output plane.
+ *   kinds[s] is OXC_TRANSFORM_*; args[s] the crop size or the normalize
+ *   channel count; norm_params packs each normalize step's mean[] then
+ *   std[].  rank is the column's rank (3 or 4), row_shape its dims after
+ *   dim 0.  result[4] = {planes written, out_h, out_w, failing batch or -1}:
+ *   on a batch whose transform the reference rejects, the planes of the
+ *   batches before it are written and the reference's message returned. */
+#define OXC_MAX_GATHER_COLUMNS 8
+#define OXC_TRANSFORM_CROP 0      /* NativeTransform::RandomCrop(size) */
+#define OXC_TRANSFORM_FLIP 1      /* NativeTransform::RandomHorizontalFlip */
+#define OXC_TRANSFORM_NORMALIZE 2 /* NativeTransform::Normalize(mean, std) */
+typedef struct oxc_gather_column {
+  const void* src;
+  void* dst;
+  int64_t row_bytes;
+} oxc_gather_column;
+typedef struct oxc_plane_map {
+  int64_t src_offset;
+  int32_t row_offset;
+  int32_t col_base;
+  int32_t col_step; /* +1, or -1 for a mirrored plane */
+  int32_t channel;
+} oxc_plane_map;
+oxc_status oxc_gather_rows(const oxc_gather_column* columns, int32_t ncols, const int64_t* idx,
+                           int64_t nidx, int64_t nrows, int32_t* err_flag, void* stream);
+oxc_status oxc_image_epoch(const float* src, int64_t row_elems, const int64_t* order, int64_t nidx,
+                           int64_t nrows, const oxc_plane_map* planes, int64_t nplanes, int32_t in_h,
+                           int32_t in_w, int32_t out_h, int32_t out_w, const float* norm, int32_t nnorm,
+                           int32_t channels, float* out, int32_t* err_flag, void* stream);
+uint64_t oxc_epoch_seed(uint64_t base, uint64_t epoch);
+uint64_t oxc_batch_seed(uint64_t epoch_seed, const int64_t* indices, int64_t n);
+oxc_status oxc_permutation(uint32_t seed, int64_t n, int64_t* out);
+oxc_status oxc_epoch_transform_plan(const int64_t* order, int64_t nidx, int64_t batch_size,
+                                    uint64_t epoch_seed, const int32_t* kinds, const int64_t* args,
+                                    const float* norm_params, int32_t nsteps, int32_t rank,
+                                    const int64_t* row_shape, oxc_plane_map* planes, int64_t planes_cap,
+                                    int64_t* result);
+
+/* Host <-> device copies through a pinned two-slot staging ring, the host
+ * copy of one slot overlapping the DMA of the other; they return once the
+ * bytes have arrived; the two 8 MiB pinned slots are allocated on first use
+ * (the reference's from_numpy / Tensor::numpy copies,
+ * crates/oxi-bindings/src/lib.rs:769-780, 382-391).  Ordered on `stream`. */
+oxc_status oxc_upload(void* dst_device, const void* src_host, int64_t bytes, void* stream);
+oxc_status oxc_download(void* dst_host, const void* src_device, int64_t bytes, void* stream);
+
 /* ---- registry ids: the order of the reference registry tables ---------
  * binary: add,sub,mul,div,pow,min,max          (crates/oxi-tensor/src/ops.rs:55-91)
  * cmp:    eq,ne,lt,le,gt,ge                    (ops.rs:96-121)

@@ -862,11 +862,11 @@ def sgd_step(param, grad, buf, lr, momentum, nesterov):
     lr, mom = np.float32(lr), np.float32(momentum)
     if mom > 0.0:
         buf = f32(np.zeros_like(g) if buf is None else buf)
-        buf = (mom * buf + g).astype(np.float32)             # :117-119
-        upd = (g + mom * buf).astype(np.float32) if nesterov else buf  # :120-127
+        buf = (mom * buf + g).astype(np.float32)             # :115-117
+        upd = (g + mom * buf).astype(np.float32) if nesterov else buf  # :118-126
     else:
-        buf, upd = None, g                                   # :128-130
-    return (p - lr * upd).astype(np.float32), buf            # :132-136
+        buf, upd = None, g                                   # :127-129
+    return (p - lr * upd).astype(np.float32), buf            # :134
 
 
 def adamw_step(param, grad, m, v, lr, beta1, beta2, eps, weight_decay, decoupled, t):
@@ -878,14 +878,222 @@ def adamw_step(param, grad, m, v, lr, beta1, beta2, eps, weight_decay, decoupled
     lr, b1, b2 = np.float32(lr), np.float32(beta1), np.float32(beta2)
     eps, wd = np.float32(eps), np.float32(weight_decay)
     one = np.float32(1.0)
-    bc1 = one - _powf(b1, np.float32(t))                     # :253
-    bc2 = one - _powf(b2, np.float32(t))                     # :254
-    ge = (g + wd * p).astype(np.float32) if (not decoupled and wd != 0.0) else g   # :263-267
-    m = (b1 * m + (one - b1) * ge).astype(np.float32)        # :268
-    v = (b2 * v + (one - b2) * ge * ge).astype(np.float32)   # :269 (left to right)
-    m_hat = (m / bc1).astype(np.float32)                     # :270
-    v_hat = (v / bc2).astype(np.float32)                     # :271
-    nxt = (p - lr * m_hat / (np.sqrt(v_hat) + eps)).astype(np.float32)  # :272
+    bc1 = one - _powf(b1, np.float32(t))                     # :232
+    bc2 = one - _powf(b2, np.float32(t))                     # :233
+    ge = (g + wd * p).astype(np.float32) if (not decoupled and wd != 0.0) else g   # :243-247
+    m = (b1 * m + (one - b1) * ge).astype(np.float32)        # :248
+    v = (b2 * v + (one - b2) * ge * ge).astype(np.float32)   # :249 (left to right)
+    m_hat = (m / bc1).astype(np.float32)                     # :250
+    v_hat = (v / bc2).astype(np.float32)                     # :251
+    nxt = (p - lr * m_hat / (np.sqrt(v_hat) + eps)).astype(np.float32)  # :252
     if decoupled and wd != 0.0:
-        nxt = (nxt - lr * wd * p).astype(np.float32)         # :273-275
+        nxt = (nxt - lr * wd * p).astype(np.float32)         # :253-255
     return nxt, m, v
+
+
+# ---- data loader (crates/oxi-data, crates/oxi-bindings/src/data.rs) --------------------------
+#
+# Pure-Python restatement of the loader's index and augmentation arithmetic,
+# for small cases: MT19937 and its NumPy-compatible draws (rng.rs), the
+# per-epoch and per-batch seeds, epoch_plan, gather_columns and the three
+# native transforms, applied batch by batch exactly as TensorBatchSource does.
+
+_M64 = (1 << 64) - 1
+
+
+class Mt19937:
+    """rng.rs:1-125: MT19937 with init_genrand seeding, NumPy's 53-bit
+    ``random()`` rounded to f32, and masked-rejection ``below``."""
+
+    def __init__(self, seed):
+        mt = [seed & 0xFFFFFFFF]
+        for i in range(1, 624):
+            mt.append((1812433253 * (mt[-1] ^ (mt[-1] >> 30)) + i) & 0xFFFFFFFF)
+        self.mt, self.mti = mt, 624
+
+    def _twist(self):
+        mt = self.mt
+        for i in range(624):
+            y = (mt[i] & 0x80000000) | (mt[(i + 1) % 624] & 0x7FFFFFFF)
+            nxt = mt[(i + 397) % 624] ^ (y >> 1)
+            if y & 1:
+                nxt ^= 0x9908B0DF
+            mt[i] = nxt
+        self.mti = 0
+
+    def next_u32(self):
+        if self.mti >= 624:
+            self._twist()
+        y = self.mt[self.mti]
+        self.mti += 1
+        y ^= y >> 11
+        y ^= (y << 7) & 0x9D2C5680
+        y ^= (y << 15) & 0xEFC60000
+        y ^= y >> 18
+        return y & 0xFFFFFFFF
+
+    def random(self):
+        a = float(self.next_u32() >> 5)
+        b = float(self.next_u32() >> 6)
+        return np.float32((a * 67108864.0 + b) / 9007199254740992.0)
+
+    def below(self, bound):
+        rng = (bound - 1) & 0xFFFFFFFF
+        mask = rng
+        for sh in (1, 2, 4, 8, 16):
+            mask |= mask >> sh
+        while True:
+            v = self.next_u32() & mask
+            if v <= rng:
+                return v
+
+    def permutation(self, n):
+        idx = list(range(n))
+        for i in range(n - 1, 0, -1):
+            j = self.below(i + 1)
+            idx[i], idx[j] = idx[j], idx[i]
+        return idx
+
+
+def _splitmix(z):
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & _M64
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & _M64
+    return z ^ (z >> 31)
+
+
+def epoch_seed(base, counter):
+    """``EpochSeeds::next`` (data.rs:43-55) for the given counter value."""
+    return _splitmix((base + counter * 0x9E3779B97F4A7C15) & _M64)
+
+
+def indices_seed(indices):
+    """FNV-1a over the indices' little-endian bytes (batch.rs:394-404)."""
+    h = 0xCBF29CE484222325
+    for i in indices:
+        for b in int(i).to_bytes(8, "little", signed=False):
+            h ^= b
+            h = (h * 0x100000001B3) & _M64
+    return h
+
+
+def batch_seed(epoch_seed_, seq):
+    """transform.rs:231-237."""
+    return _splitmix((epoch_seed_ ^ ((seq * 0x9E3779B97F4A7C15) & _M64)) & _M64)
+
+
+def batch_rng(seed):
+    """transform.rs:241-244: the two halves folded into a 32-bit seed."""
+    return Mt19937((seed ^ (seed >> 32)) & 0xFFFFFFFF)
+
+
+def epoch_plan(order, batch_size, drop_last):
+    """batch.rs:271-291: chunks of batch_size; a short last chunk is dropped
+    with drop_last only when an earlier batch exists."""
+    if batch_size == 0:
+        raise ValueError("batch_size must be >= 1")
+    chunks = [list(order[i:i + batch_size]) for i in range(0, len(order), batch_size)]
+    out = []
+    for k, ch in enumerate(chunks):
+        last = k == len(chunks) - 1
+        if last and drop_last and len(ch) < batch_size and out:
+            break
+        out.append(ch)
+    return out
+
+
+def gather_columns(columns, indices):
+    """batch.rs:411-425: index_select(0, indices) per column."""
+    n = columns[0].shape[0]
+    if any(i >= n for i in indices):
+        raise IndexError(f"out of bounds: index out of range (n={n})")
+    idx = np.asarray(indices, dtype=np.int64)
+    return [np.ascontiguousarray(c[idx]) for c in columns]
+
+
+def _geometry(shape):
+    """transform.rs:66-95: (samples, channels, height, width)."""
+    if len(shape) < 2:
+        raise ValueError(f"shape mismatch: rank {len(shape)} vs image batches need at least (h, w)")
+    h, w = shape[-2], shape[-1]
+    if len(shape) == 2:
+        return 1, 1, h, w
+    if len(shape) == 3:
+        return 1, shape[0], h, w
+    return shape[0], shape[1], h, w
+
+
+def random_crop(batch, size, rng):
+    """transform.rs:105-133: a (top, left) per plane, drawn plane by plane."""
+    s, c, h, w = _geometry(batch.shape)
+    if size == 0 or size > h or size > w:
+        raise ValueError(f"invalid argument: crop size {size} exceeds image {h}x{w}")
+    planes = batch.reshape(s * c, h, w)
+    out = np.empty((s * c, size, size), np.float32)
+    for p in range(s * c):
+        top = rng.below(h - size + 1)
+        left = rng.below(w - size + 1)
+        out[p] = planes[p, top:top + size, left:left + size]
+    return out.reshape(batch.shape[:-2] + (size, size))
+
+
+def random_horizontal_flip(batch, rng):
+    """transform.rs:139-160: one draw per sample at its first plane; that
+    plane stays put when the draw is >= 0.5, every other plane is reversed."""
+    s, c, h, w = _geometry(batch.shape)
+    out = batch.reshape(s * c, h, w).copy()
+    for p in range(s * c):
+        if p % c == 0 and rng.random() >= np.float32(0.5):
+            continue
+        out[p] = out[p][:, ::-1]
+    return out.reshape(batch.shape)
+
+
+def normalize(batch, mean, std):
+    """transform.rs:163-191: (v - mean[c]) * (1 / std[c]), f32 throughout."""
+    s, c, h, w = _geometry(batch.shape)
+    if len(mean) != c or len(std) != c:
+        raise ValueError(f"invalid argument: normalize expects {c} channels, got mean {len(mean)} "
+                         f"/ std {len(std)}")
+    if any(x <= 0.0 for x in std):
+        raise ValueError("invalid argument: normalize std must be > 0")
+    planes = batch.reshape(s * c, h * w).copy()
+    for p in range(s * c):
+        m = np.float32(mean[p % c])
+        inv = np.float32(1.0) / np.float32(std[p % c])
+        planes[p] = ((planes[p] - m).astype(np.float32) * inv).astype(np.float32)
+    return planes.reshape(batch.shape)
+
+
+def apply_transforms(batch, steps, rng):
+    """TransformPipeline::apply (transform.rs:218-223); steps are
+    ("crop", size) / ("flip",) / ("normalize", mean, std)."""
+    cur = f32(batch)
+    for st in steps:
+        if st[0] == "crop":
+            cur = random_crop(cur, int(st[1]), rng)
+        elif st[0] == "flip":
+            cur = random_horizontal_flip(cur, rng)
+        else:
+            cur = normalize(cur, [np.float32(x) for x in st[1]], [np.float32(x) for x in st[2]])
+    return cur
+
+
+def loader_epoch(columns, batch_size, shuffle, drop_last, seed, steps=None, transform_seed=0,
+                 epoch=0):
+    """One ``__iter__`` of the native DataLoader (data.rs:216-262 and
+    TensorBatchSource::get_batch, batch.rs:378-387): the ``epoch``-th pass of
+    one loader object.  Returns the list of batches (lists of arrays)."""
+    n = columns[0].shape[0]
+    if shuffle and seed is not None:
+        order = Mt19937(epoch_seed(seed, epoch) & 0xFFFFFFFF).permutation(n)
+    else:
+        order = list(range(n))
+    tseed = epoch_seed(transform_seed, epoch)
+    out = []
+    for idx in epoch_plan(order, batch_size, drop_last):
+        cols = gather_columns(columns, idx)
+        if steps:
+            rng = batch_rng(batch_seed(tseed, indices_seed(idx)))
+            cols[0] = apply_transforms(cols[0], steps, rng)
+        out.append(cols)
+    return out

@@ -45,12 +45,32 @@ class View(ctypes.Structure):
     ]
 
 
+class GatherColumn(ctypes.Structure):
+    """struct oxc_gather_column: source rows, destination rows, bytes per row."""
+
+    _fields_ = [("src", ctypes.c_void_p), ("dst", ctypes.c_void_p), ("row_bytes", ctypes.c_int64)]
+
+
+class PlaneMap(ctypes.Structure):
+    """struct oxc_plane_map: where one output image plane reads its pixels."""
+
+    _fields_ = [
+        ("src_offset", ctypes.c_int64),
+        ("row_offset", ctypes.c_int32),
+        ("col_base", ctypes.c_int32),
+        ("col_step", ctypes.c_int32),
+        ("channel", ctypes.c_int32),
+    ]
+
+
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _I32 = ctypes.c_int32
 _F32 = ctypes.c_float
 _SZ = ctypes.c_size_t
 _VP = ctypes.POINTER(View)
+_U32 = ctypes.c_uint32
+_U64 = ctypes.c_uint64
 
 # name -> (restype, argtypes); one line per entry point of include/oxicuda.h
 SIGNATURES = {
@@ -97,6 +117,16 @@ SIGNATURES = {
                                           _I32, _P]),
     "oxc_sgd_step": (_I32, [_P, _P, _P, _I64, _F32, _F32, _I32, _P]),
     "oxc_adamw_step": (_I32, [_P, _P, _P, _P, _I64, _F32, _F32, _F32, _F32, _F32, _I32, _I64, _P]),
+    "oxc_gather_rows": (_I32, [ctypes.POINTER(GatherColumn), _I32, _P, _I64, _I64, _P, _P]),
+    "oxc_image_epoch": (_I32, [_P, _I64, _P, _I64, _I64, _P, _I64, _I32, _I32, _I32, _I32, _P, _I32,
+                               _I32, _P, _P, _P]),
+    "oxc_epoch_seed": (_U64, [_U64, _U64]),
+    "oxc_batch_seed": (_U64, [_U64, _P, _I64]),
+    "oxc_permutation": (_I32, [_U32, _I64, _P]),
+    "oxc_epoch_transform_plan": (_I32, [_P, _I64, _I64, _U64, _P, _P, _P, _I32, _I32, _P, _P, _I64,
+                                        _P]),
+    "oxc_upload": (_I32, [_P, _P, _I64, _P]),
+    "oxc_download": (_I32, [_P, _P, _I64, _P]),
 }
 
 NOALLOC_SCRATCH_BYTES = 16 * 1024 * 1024
