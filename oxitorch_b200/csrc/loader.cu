@@ -191,16 +191,23 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(GatherArgs args, const
   }
 }
 
-// One warp per output plane.  Output plane q, row r, column x reads source
-// row r + row_offset, column col_base + col_step * x of its plane, where the
-// plane sits at element src_offset of the virtual tensor column[order[0..nidx)]
-// (rows of row_elems elements; a plane never spans two rows); then every
-// normalize step in order: v = (v - mean[c]) * inv[c], each operation
-// rounded.  The plane's source row, its bounds and its normalize constants
-// are resolved once; rows then stream four at a time, lanes across columns.
+// Each warp takes two output planes at a time.  Output plane q, row r,
+// column x reads source row r + row_offset, column col_base + col_step * x
+// of its plane, where the plane sits at element src_offset of the virtual
+// tensor column[order[0..nidx)] (rows of row_elems elements; a plane never
+// spans two rows); then every normalize step in order:
+// v = (v - mean[c]) * inv[c], each operation rounded.  A plane's source row,
+// its bounds and its normalize constants are resolved once, for both planes
+// together (their map -> order -> pixel chains overlap); rows then stream
+// four at a time per plane, lanes across columns, so eight loads per lane
+// are in flight.
 constexpr int kMaxFusedNorm = 4;
+constexpr int kPlanesPerWarp = 2;
 
-__global__ void __launch_bounds__(256) image_epoch_kernel(
+// NORM_SLOTS: normalize steps held in registers (2: the common pipelines, 64
+// registers without spills; 4: up to four steps).
+template <int NORM_SLOTS>
+__global__ void __launch_bounds__(256, 4) image_epoch_kernel(
     const float* __restrict__ src, int64_t row_elems, const int64_t* __restrict__ order, int64_t nidx,
     int64_t nrows, const oxc_plane_map* __restrict__ planes, int64_t nplanes, int in_h, int in_w,
     int out_h, int out_w, const float* __restrict__ norm, int nnorm, int channels,
@@ -209,49 +216,83 @@ __global__ void __launch_bounds__(256) image_epoch_kernel(
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int64_t plane_out = (int64_t)out_h * out_w;
-  for (int64_t q = warp; q < nplanes; q += nwarps) {
-    const oxc_plane_map pm = planes[q];
-    const int64_t ds = pm.src_offset / row_elems;
-    const int64_t off = pm.src_offset - ds * row_elems;
-    const int x_last = pm.col_base + pm.col_step * (out_w - 1);
-    const bool geom_ok = pm.src_offset >= 0 && ds < nidx && off + (int64_t)in_h * in_w <= row_elems &&
-                         pm.row_offset >= 0 &&
-                         pm.row_offset + out_h <= in_h && pm.col_base >= 0 && pm.col_base < in_w &&
-                         x_last >= 0 && x_last < in_w && pm.channel >= 0 && pm.channel < channels;
-    const int64_t id = geom_ok ? order[ds] : -1;
-    if (!geom_ok || id < 0 || id >= nrows) {
-      if (lane == 0) loader_record_bad(err, geom_ok ? id : pm.src_offset, geom_ok ? nrows : row_elems);
-      continue;
-    }
-    float mean[kMaxFusedNorm], inv[kMaxFusedNorm];
+  for (int64_t q0 = warp * kPlanesPerWarp; q0 < nplanes; q0 += nwarps * kPlanesPerWarp) {
+    oxc_plane_map pm[kPlanesPerWarp];
+    bool ok[kPlanesPerWarp];
 #pragma unroll
-    for (int k = 0; k < kMaxFusedNorm; ++k) {
-      mean[k] = k < nnorm ? norm[(2 * k) * channels + pm.channel] : 0.0f;
-      inv[k] = k < nnorm ? norm[(2 * k + 1) * channels + pm.channel] : 1.0f;
+    for (int j = 0; j < kPlanesPerWarp; ++j) {
+      ok[j] = q0 + j < nplanes;
+      if (ok[j]) pm[j] = planes[q0 + j];
     }
-    const float* s = src + id * row_elems + off + (int64_t)pm.row_offset * in_w + pm.col_base;
-    float* d = out + q * plane_out;
+    int64_t ds[kPlanesPerWarp], off[kPlanesPerWarp], id[kPlanesPerWarp];
+#pragma unroll
+    for (int j = 0; j < kPlanesPerWarp; ++j) {
+      id[j] = -1;
+      if (!ok[j]) continue;
+      ds[j] = pm[j].src_offset / row_elems;
+      off[j] = pm[j].src_offset - ds[j] * row_elems;
+      const int x_last = pm[j].col_base + pm[j].col_step * (out_w - 1);
+      const bool geom_ok = pm[j].src_offset >= 0 && ds[j] < nidx &&
+                           off[j] + (int64_t)in_h * in_w <= row_elems && pm[j].row_offset >= 0 &&
+                           pm[j].row_offset + out_h <= in_h && pm[j].col_base >= 0 &&
+                           pm[j].col_base < in_w && x_last >= 0 && x_last < in_w &&
+                           pm[j].channel >= 0 && pm[j].channel < channels;
+      if (geom_ok) id[j] = order[ds[j]];
+      if (!geom_ok || id[j] < 0 || id[j] >= nrows) {
+        if (lane == 0)
+          loader_record_bad(err, geom_ok ? id[j] : pm[j].src_offset, geom_ok ? nrows : row_elems);
+        ok[j] = false;
+      }
+    }
+    float mean[kPlanesPerWarp][NORM_SLOTS], inv[kPlanesPerWarp][NORM_SLOTS];
+    const float* sp[kPlanesPerWarp];
+    float* dp[kPlanesPerWarp];
+    int step[kPlanesPerWarp];
+#pragma unroll
+    for (int j = 0; j < kPlanesPerWarp; ++j) {
+      const int c = ok[j] ? pm[j].channel : 0;
+#pragma unroll
+      for (int k = 0; k < NORM_SLOTS; ++k) {
+        mean[j][k] = (ok[j] && k < nnorm) ? norm[(2 * k) * channels + c] : 0.0f;
+        inv[j][k] = (ok[j] && k < nnorm) ? norm[(2 * k + 1) * channels + c] : 1.0f;
+      }
+      sp[j] = ok[j] ? src + id[j] * row_elems + off[j] + (int64_t)pm[j].row_offset * in_w + pm[j].col_base
+                    : src;
+      dp[j] = out + (q0 + j) * plane_out;
+      step[j] = ok[j] ? pm[j].col_step : 0;
+    }
     for (int x = lane; x < out_w; x += 32) {
-      const float* sx = s + pm.col_step * x;
       int r = 0;
       for (; r + 4 <= out_h; r += 4) {
-        float v[4];
+        float v[kPlanesPerWarp][4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) v[u] = __ldg(sx + (int64_t)(r + u) * in_w);
+        for (int j = 0; j < kPlanesPerWarp; ++j)
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+          for (int u = 0; u < 4; ++u)
+            if (ok[j]) v[j][u] = __ldg(sp[j] + step[j] * x + (int64_t)(r + u) * in_w);
 #pragma unroll
-          for (int k = 0; k < kMaxFusedNorm; ++k)
-            if (k < nnorm) v[u] = __fmul_rn(__fsub_rn(v[u], mean[k]), inv[k]);
-          d[(int64_t)(r + u) * out_w + x] = v[u];
+        for (int j = 0; j < kPlanesPerWarp; ++j) {
+          if (!ok[j]) continue;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            float w = v[j][u];
+#pragma unroll
+            for (int k = 0; k < NORM_SLOTS; ++k)
+              if (k < nnorm) w = __fmul_rn(__fsub_rn(w, mean[j][k]), inv[j][k]);
+            dp[j][(int64_t)(r + u) * out_w + x] = w;
+          }
         }
       }
       for (; r < out_h; ++r) {
-        float v = __ldg(sx + (int64_t)r * in_w);
 #pragma unroll
-        for (int k = 0; k < kMaxFusedNorm; ++k)
-          if (k < nnorm) v = __fmul_rn(__fsub_rn(v, mean[k]), inv[k]);
-        d[(int64_t)r * out_w + x] = v;
+        for (int j = 0; j < kPlanesPerWarp; ++j) {
+          if (!ok[j]) continue;
+          float w = __ldg(sp[j] + step[j] * x + (int64_t)r * in_w);
+#pragma unroll
+          for (int k = 0; k < NORM_SLOTS; ++k)
+            if (k < nnorm) w = __fmul_rn(__fsub_rn(w, mean[j][k]), inv[j][k]);
+          dp[j][(int64_t)r * out_w + x] = w;
+        }
       }
     }
   }
@@ -384,7 +425,9 @@ oxc_status oxc_image_epoch(const float* src, int64_t row_elems, const int64_t* o
   if (nnorm > kMaxFusedNorm)
     return fail(OXC_ERR_NOT_IMPLEMENTED, "not implemented: more than %d normalize steps in one pipeline",
                 kMaxFusedNorm);
-  image_epoch_kernel<<<loader_grid(nplanes), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  const dim3 grid(loader_grid((nplanes + kPlanesPerWarp - 1) / kPlanesPerWarp));
+  auto kernel = nnorm <= 2 ? image_epoch_kernel<2> : image_epoch_kernel<kMaxFusedNorm>;
+  kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       src, row_elems, order, nidx, nrows, planes, nplanes, in_h, in_w, out_h, out_w, norm, nnorm, channels,
       out, err_flag);
   return check_launch("oxc_image_epoch");

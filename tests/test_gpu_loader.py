@@ -92,6 +92,9 @@ CASES = [
     ((97, 3, 8, 8), 10, False, False, None, [("crop", 5), ("crop", 3), ("flip",)]),
     ((45, 8, 8), 9, True, False, 2, [("crop", 5), ("flip",)]),
     ((5, 4, 4), 8, True, True, 1, [("flip",)]),   # one short batch, kept despite drop_last
+    ((40, 2, 6, 6), 7, True, False, 5,             # three normalize steps: the 4-slot kernel
+     [("normalize", [0.5, -0.5], [2.0, 0.5]), ("crop", 4), ("normalize", [0.1, 0.2], [0.3, 0.7]),
+      ("flip",), ("normalize", [1.5, 0.0], [1.1, 0.9])]),
 ]
 
 
