@@ -110,6 +110,12 @@ oxc_status oxc_sgd_step(float* param, const float* grad, float* velocity, int64_
 oxc_status oxc_adamw_step(float* param, const float* grad, float* m, float* v, int64_t n,
                           float lr, float beta1, float beta2, float eps, float weight_decay,
                           int32_t decoupled, int64_t step, void* stream);
+/* oxc_clip_grad_value: clip_grad_value_ (python/oxitorch/optim.py:266-272) on
+ *   one gradient in place, np.clip(g, -clip_value, clip_value) with NumPy's
+ *   NaN rules (a NaN element or bound gives NaN).  The caller applies the
+ *   reference's "clip_value must be positive" check to its double value; a
+ *   negative f32 bound is refused here with that message. */
+oxc_status oxc_clip_grad_value(float* grad, int64_t n, float clip_value, void* stream);
 
 /* ---- data path: dataset columns in device memory, batches built on device --
  * The reference's DataLoader (crates/oxi-bindings/src/data.rs:116-330) gathers

@@ -1097,3 +1097,28 @@ def loader_epoch(columns, batch_size, shuffle, drop_last, seed, steps=None, tran
             cols[0] = apply_transforms(cols[0], steps, rng)
         out.append(cols)
     return out
+
+
+# ---- gradient clipping (python/oxitorch/optim.py:242-272) -------------------------------------
+
+def clip_grad_norm_np(grads, max_norm, norm_type=2.0):
+    """optim.py:242-263 on a list of float32 arrays (None = no gradient):
+    returns (pre-clip total norm, clipped copies)."""
+    present = [f32(g) for g in grads if g is not None]
+    if norm_type == float("inf"):
+        total = max((float(np.max(np.abs(g))) for g in present), default=0.0)
+    else:
+        total = sum(float(np.sum(np.abs(g) ** norm_type)) for g in present) ** (1.0 / norm_type)
+    scale = max_norm / (total + 1e-6)
+    out = [None if g is None else f32(g) for g in grads]
+    if scale < 1.0:
+        out = [None if g is None else (g * scale).astype(np.float32) for g in out]
+    return total, out
+
+
+def clip_grad_value_np(grads, clip_value):
+    """optim.py:266-272: np.clip of every gradient to [-c, c]."""
+    clip_value = float(clip_value)
+    if clip_value <= 0:
+        raise ValueError("clip_value must be positive")
+    return [None if g is None else np.clip(f32(g), -clip_value, clip_value) for g in grads]

@@ -117,6 +117,7 @@ SIGNATURES = {
                                           _I32, _P]),
     "oxc_sgd_step": (_I32, [_P, _P, _P, _I64, _F32, _F32, _I32, _P]),
     "oxc_adamw_step": (_I32, [_P, _P, _P, _P, _I64, _F32, _F32, _F32, _F32, _F32, _I32, _I64, _P]),
+    "oxc_clip_grad_value": (_I32, [_P, _I64, _F32, _P]),
     "oxc_gather_rows": (_I32, [ctypes.POINTER(GatherColumn), _I32, _P, _I64, _I64, _P, _P]),
     "oxc_image_epoch": (_I32, [_P, _I64, _P, _I64, _I64, _P, _I64, _I32, _I32, _I32, _I32, _P, _I32,
                                _I32, _P, _P, _P]),

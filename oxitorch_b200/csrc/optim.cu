@@ -129,6 +129,36 @@ __global__ void __launch_bounds__(256) sgd_kernel(float* __restrict__ p,
   }
 }
 
+// clip_grad_value_ (python/oxitorch/optim.py:266-272) clamps with np.clip:
+// min(max(x, lo), hi), where max(a, b) = isnan(a) ? a : (a > b ? a : b) and
+// min likewise, so NaN gradients stay NaN, -0.0 stays -0.0 and NaN bounds
+// give NaN.
+__device__ __forceinline__ float np_clip(float x, float lo, float hi) {
+  const float m = isnan(x) ? x : (x > lo ? x : lo);
+  return isnan(m) ? m : (m < hi ? m : hi);
+}
+
+template <bool V4>
+__global__ void __launch_bounds__(256) clip_value_kernel(float* __restrict__ g, int64_t n, float lo,
+                                                         float hi) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if constexpr (V4) {
+    const int64_t nv = n / 4;
+    float4* g4 = reinterpret_cast<float4*>(g);
+    for (int64_t k = i; k < nv; k += stride) {
+      float4 v = ld_stream(g4 + k);
+      v.x = np_clip(v.x, lo, hi);
+      v.y = np_clip(v.y, lo, hi);
+      v.z = np_clip(v.z, lo, hi);
+      v.w = np_clip(v.w, lo, hi);
+      st_stream(g4 + k, v);
+    }
+    i += nv * 4;
+  }
+  for (; i < n; i += stride) g[i] = np_clip(g[i], lo, hi);
+}
+
 static unsigned elem_grid(int64_t work) {
   const int64_t cap = (int64_t)sm_count() * 8 * 4;  // 8 CTAs of 256 per SM, 4 waves
   return (unsigned)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, cap));
@@ -189,6 +219,22 @@ oxc_status oxc_adamw_step(float* param, const float* grad, float* m, float* v, i
   else
     adam_kernel<false><<<elem_grid(n), 256, 0, s>>>(param, grad, m, v, n, c);
   return check_launch("oxc_adamw_step");
+}
+
+oxc_status oxc_clip_grad_value(float* grad, int64_t n, float clip_value, void* stream) {
+  // The reference checks the Python float (<= 0 raises) before NumPy rounds
+  // it to f32; here only a negative f32 bound is refused, so a positive bound
+  // that rounds to 0 clamps to +-0 as np.clip does, and a NaN bound gives NaN.
+  if (clip_value < 0.0f) return fail(OXC_ERR_INVALID_ARGUMENT, "clip_value must be positive");
+  if (n < 0) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: clip_grad_value_: negative size");
+  if (n == 0) return OXC_OK;
+  if (!grad) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: clip_grad_value_: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (aligned16(grad))
+    clip_value_kernel<true><<<elem_grid(n / 4 + 1), 256, 0, s>>>(grad, n, -clip_value, clip_value);
+  else
+    clip_value_kernel<false><<<elem_grid(n), 256, 0, s>>>(grad, n, -clip_value, clip_value);
+  return check_launch("oxc_clip_grad_value");
 }
 
 }  // extern "C"

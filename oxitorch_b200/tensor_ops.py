@@ -5,8 +5,8 @@ Same names, argument meaning and errors as ``crates/oxi-tensor/src/lib.rs``:
 keepdim)`` with its VJP ``reduce_backward`` and the autograd helper
 ``unbroadcast`` (graph.rs:274-313), the whole-tensor
 ``sum_all``/``mean_all``/``reduce_all``, plus
-``clip_grad_norm_`` (python/oxitorch/optim.py:242-263) over device
-gradients.  Inputs are torch CUDA float32 tensors with any strides (views:
+``clip_grad_norm_`` and ``clip_grad_value_`` (python/oxitorch/optim.py:242-272)
+over device gradients.  Inputs are torch CUDA float32 tensors with any strides (views:
 transposes, slices, zero-stride broadcasts); outputs are dense, like the
 reference's ``from_results``.  Every op is one call into liboxicuda.so.
 """
@@ -238,24 +238,63 @@ def sum_squares(tensors):
 
 
 def clip_grad_norm_(grads, max_norm, norm_type=2.0):
-    """clip_grad_norm_ (python/oxitorch/optim.py:242-263) for norm_type 2 over
-    device gradients, in place: total = sqrt(sum of squares); if
-    max_norm / (total + 1e-6) < 1 every gradient is scaled by it.  Returns
-    the pre-clip total norm as a Python float, like the reference."""
-    if norm_type != 2.0:
-        raise NotImplementedError("not implemented: clip_grad_norm_ with norm_type != 2 on device")
+    """clip_grad_norm_ (python/oxitorch/optim.py:242-263) over device
+    gradients, in place; returns the pre-clip total norm as a Python float.
+
+    * norm_type 2: sqrt of the f64 sum of squares (one multi-tensor pass);
+    * inf: the largest |g| of each gradient (a gradient holding a NaN gives
+      NaN, as np.max does), combined in list order with Python's ``max``
+      like the reference, so a NaN counts only when it comes first;
+    * any other p: (sum over gradients of sum |g|**p) ** (1/p), |g|**p in
+      f32 through the registry's pow, each gradient's sum in f64.
+
+    If max_norm / (total + 1e-6) < 1, every gradient is scaled by it (an f32
+    multiply, as NumPy's f32 * Python float)."""
     grads = [g for g in grads if g is not None]
     if not grads:
         return 0.0
-    total = 0.0
-    for i in range(0, len(grads), 16):
-        total += float(sum_squares(grads[i:i + 16]).item())
-    total = total ** 0.5
+    if norm_type == float("inf"):
+        total = None
+        for g in grads:
+            m = float(reduce_all("max", unary_op("abs", g)).item())
+            if float(reduce_all("max", cmp_op("ne", g, g)).item()) > 0.0:
+                m = float("nan")
+            if total is None or m > total:
+                total = m
+    elif norm_type == 2.0:
+        total = 0.0
+        for i in range(0, len(grads), 16):
+            total += float(sum_squares(grads[i:i + 16]).item())
+        total = total ** 0.5
+    else:
+        p = float(norm_type)
+        acc = 0.0
+        for g in grads:
+            powed = binary_op("pow", unary_op("abs", g), p)
+            acc += float(reduce_all("sum", powed, f64=True)[1].item())
+        total = acc ** (1.0 / p)
     scale = max_norm / (total + 1e-6)
     if scale < 1.0:
         for g in grads:
             scale_(g, scale)
     return total
+
+
+def clip_grad_value_(grads, clip_value):
+    """clip_grad_value_ (python/oxitorch/optim.py:266-272): every gradient
+    clamped in place to [-clip_value, clip_value] with np.clip's NaN rules."""
+    clip_value = float(clip_value)
+    if clip_value <= 0:
+        raise ValueError("clip_value must be positive")
+    L = N.load()
+    for g in grads:
+        if g is None:
+            continue
+        _require_cuda_f32("grad", g)
+        if not g.is_contiguous():
+            raise ValueError("invalid argument: clip_grad_value_ takes contiguous gradients")
+        N.check(L.oxc_clip_grad_value(g.data_ptr(), g.numel(), clip_value, _stream()),
+                "clip_grad_value_")
 
 
 def scale_(g, scale):

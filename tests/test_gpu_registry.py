@@ -398,3 +398,47 @@ def test_clip_grad_norm(oracle):
     scale = 1.0 / (want_total + 1e-6)
     for g, d in zip(gs, dev):
         assert_close(_host(d), g * np.float32(scale), rtol=1e-5, atol=1e-7, what="clipped grad")
+
+
+@pytest.mark.parametrize("norm_type", [1.0, 3.0, float("inf")])
+def test_clip_grad_norm_other_norms(oracle, norm_type):
+    """optim.py:242-263 for p = 1, 3 and inf: the inf total is exact; finite p
+    within the f32 pairwise-sum and powf budget of the reference's numpy."""
+    from oxitorch_b200 import tensor_ops as T
+    rng = np.random.default_rng(int(norm_type) if norm_type != float("inf") else 99)
+    gs = [rng.standard_normal(s, dtype=np.float32) for s in [(300, 70), (5001,), (64, 64, 3)]]
+    want_total, want = oracle.clip_grad_norm_np(gs, 1.0, norm_type)
+    dev = [_dev(g) for g in gs]
+    total = T.clip_grad_norm_(dev, 1.0, norm_type)
+    if norm_type == float("inf"):
+        assert total == want_total
+    else:
+        assert abs(total - want_total) <= 1e-5 * want_total
+    for w, d in zip(want, dev):
+        assert_close(_host(d), w, rtol=1e-5, atol=1e-7, what="clipped grad")
+    # reference cases (python/tests/test_phase4_training.py:211-223)
+    g = _dev(np.array([[3.0, -4.0]], np.float32))
+    assert T.clip_grad_norm_([g], 1.0, float("inf")) == 4.0
+    assert np.allclose(_host(g), [[0.75, -1.0]], rtol=1e-5)
+    nan_first = [_dev(np.array([np.nan, 1.0], np.float32)), _dev(np.array([5.0], np.float32))]
+    assert np.isnan(T.clip_grad_norm_(nan_first, 1.0, float("inf")))
+
+
+def test_clip_grad_value_matches_np_clip(oracle):
+    """optim.py:266-272: np.clip, NaN kept, -0.0 kept, both vector and scalar
+    paths (a gradient 4 bytes off alignment and an odd length)."""
+    import torch
+    from oxitorch_b200 import tensor_ops as T
+    rng = np.random.default_rng(21)
+    g = (rng.standard_normal(100003) * 3).astype(np.float32)
+    g[:6] = [np.nan, np.inf, -np.inf, -0.0, 0.0, 2.0]
+    buf = torch.zeros(g.size + 1, dtype=torch.float32, device="cuda")
+    mis = buf[1:]
+    mis.copy_(torch.from_numpy(g))
+    dense = _dev(g)
+    T.clip_grad_value_([dense, None, mis], 2.0)
+    (want,) = oracle.clip_grad_value_np([g], 2.0)
+    for d in (dense, mis):
+        assert np.array_equal(_host(d).view(np.uint32), want.view(np.uint32))
+    with pytest.raises(ValueError, match="clip_value must be positive"):
+        T.clip_grad_value_([dense], 0.0)
