@@ -22,6 +22,7 @@
 //   the SplitMix64 finaliser (Steele, Lea & Flood 2014) for per-epoch seeds
 //     (data.rs:43-55) and per-batch seeds (transform.rs:231-244);
 //   FNV-1a over the batch's indices (batch.rs:394-404).
+#include <limits.h>
 #include <string.h>
 
 #include <algorithm>
@@ -468,6 +469,20 @@ oxc_status oxc_epoch_transform_plan(const int64_t* order, int64_t nidx, int64_t 
   if (rank < 3 || rank > 4)
     return fail(OXC_ERR_NOT_IMPLEMENTED,
                 "not implemented: device transforms take image columns of rank 3 or 4 (got rank %d)", rank);
+  if (!row_shape) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: transform plan: null row shape");
+  for (int d = 0; d < rank - 1; ++d)
+    if (row_shape[d] <= 0 || row_shape[d] > (int64_t)INT32_MAX)
+      return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: transform plan: row dim %d is %lld", d,
+                  (long long)row_shape[d]);
+  for (int s = 0; s < nsteps; ++s) {
+    if (kinds[s] < OXC_TRANSFORM_CROP || kinds[s] > OXC_TRANSFORM_NORMALIZE)
+      return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: transform kind %d", kinds[s]);
+    if (kinds[s] == OXC_TRANSFORM_NORMALIZE && (args[s] < 1 || !norm_params))
+      return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: normalize step %d without parameters", s);
+    if (kinds[s] == OXC_TRANSFORM_CROP && args[s] < 0)
+      return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: crop size %lld", (long long)args[s]);
+  }
+  if (!planes && nidx > 0) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: null plane buffer");
   const int64_t h0 = row_shape[rank - 3], w0 = row_shape[rank - 2];
   int64_t row_elems = 1;
   for (int d = 0; d < rank - 1; ++d) row_elems *= row_shape[d];

@@ -252,3 +252,35 @@ def test_native_transform_wire_errors():
         NativeTransform([("normalize", [1.0, 2.0, 3.0])])
     with pytest.raises(ValueError, match="unknown native transform 'blur'"):
         NativeTransform([("blur", [])])
+
+
+def test_library_transform_plan_rejects_bad_arguments():
+    N, L = _lib()
+    order = np.arange(4, dtype=np.int64)
+    kinds = np.array([2], np.int32)
+    args = np.array([1], np.int64)
+    result = np.zeros(4, np.int64)
+    planes = (N.PlaneMap * 4)()
+    shape = np.array([1, 2, 2], np.int64)
+    # a normalize step without its parameters
+    assert L.oxc_epoch_transform_plan(order.ctypes.data, 4, 2, 0, kinds.ctypes.data, args.ctypes.data,
+                                      None, 1, 4, shape.ctypes.data, planes, 4, result.ctypes.data) == 1
+    # no row shape, a zero dim, an unknown kind, a negative crop
+    assert L.oxc_epoch_transform_plan(order.ctypes.data, 4, 2, 0, None, None, None, 0, 4, None, planes,
+                                      4, result.ctypes.data) == 1
+    zero = np.array([1, 0, 2], np.int64)
+    assert L.oxc_epoch_transform_plan(order.ctypes.data, 4, 2, 0, None, None, None, 0, 4,
+                                      zero.ctypes.data, planes, 4, result.ctypes.data) == 1
+    bad = np.array([7], np.int32)
+    assert L.oxc_epoch_transform_plan(order.ctypes.data, 4, 2, 0, bad.ctypes.data, args.ctypes.data,
+                                      None, 1, 4, shape.ctypes.data, planes, 4, result.ctypes.data) == 1
+    crop = np.array([0], np.int32)
+    neg = np.array([-3], np.int64)
+    assert L.oxc_epoch_transform_plan(order.ctypes.data, 4, 2, 0, crop.ctypes.data, neg.ctypes.data,
+                                      None, 1, 4, shape.ctypes.data, planes, 4, result.ctypes.data) == 1
+    # too small a plane buffer
+    flip = np.array([1], np.int32)
+    zarg = np.array([0], np.int64)
+    assert L.oxc_epoch_transform_plan(order.ctypes.data, 4, 2, 0, flip.ctypes.data, zarg.ctypes.data,
+                                      None, 1, 4, shape.ctypes.data, planes, 1, result.ctypes.data) == 1
+    assert "plane buffer holds 1 planes" in N.last_error()
