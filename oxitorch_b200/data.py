@@ -63,6 +63,36 @@ def to_numpy(tensor: torch.Tensor) -> np.ndarray:
     return out
 
 
+def gather_rows(columns, indices):
+    """``[c[indices] for c in columns]`` for device columns: one
+    ``oxc_gather_rows`` launch per 8 columns, the indices uploaded once.
+    Indices are validated on the host like NumPy indexing (negative ones
+    count from the end; out of range raises IndexError)."""
+    cols = list(columns)
+    n = cols[0].shape[0]
+    idx = np.asarray(indices, dtype=np.int64).reshape(-1)
+    if idx.size and (idx.min() < -n or idx.max() >= n):
+        bad = int(idx[(idx < -n) | (idx >= n)][0])
+        raise IndexError(f"index {bad} is out of bounds for axis 0 with size {n}")
+    idx = np.where(idx < 0, idx + n, idx)
+    dev = cols[0].device
+    stream = _stream(dev)
+    L = N.load()
+    outs = [torch.empty((idx.size,) + tuple(c.shape[1:]), dtype=c.dtype, device=dev) for c in cols]
+    if idx.size == 0:
+        return outs
+    idx_dev = torch.empty(idx.size, dtype=torch.int64, device=dev)
+    N.check(L.oxc_upload(idx_dev.data_ptr(), idx.ctypes.data, idx.nbytes, stream), "gather indices")
+    for g in range(0, len(cols), 8):
+        group = list(zip(cols[g:g + 8], outs[g:g + 8]))
+        desc = (N.GatherColumn * len(group))(*[
+            N.GatherColumn(c.data_ptr(), o.data_ptr(), c[0].numel() * c.element_size() if c.dim() > 1
+                           else c.element_size()) for c, o in group])
+        N.check(L.oxc_gather_rows(desc, len(group), idx_dev.data_ptr(), idx.size, n, None, stream),
+                "gather_rows")
+    return outs
+
+
 class NativeTransform:
     """The augmentation pipeline applied to the first column inside the
     loader (data.rs:60-105).  Wire format: ``("crop", [size])``,

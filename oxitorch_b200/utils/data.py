@@ -14,6 +14,9 @@ Two paths behind one ``DataLoader``, chosen as the reference chooses them
   reference's fresh ``_native.DataLoader`` per pass.  Host columns are
   uploaded on the first pass and stay resident for the later ones (the
   reference copies them again on every pass); CUDA columns are used in place;
+* a tensor-backed dataset driven by a sampler or batch sampler keeps the
+  default collation's result (the sampled rows stacked per column, float32)
+  but builds it with one device gather per batch;
 * anything else runs the reference's generic path: per-item ``__getitem__``
   (in a thread pool when ``num_workers > 1``) and ``default_collate``, whose
   stacked host arrays are uploaded with ``from_numpy``.
@@ -206,10 +209,9 @@ class DataLoader:
             if raw is None:
                 return None
         if self._resident is None or self._resident[0] is not raw:
-            cols = [c if isinstance(c, torch.Tensor) and c.is_cuda
-                    else _device.from_numpy(np.ascontiguousarray(_host_array(c)))
-                    for c in raw]
-            self._resident = (raw, cols)
+            self._resident = (raw, [c if isinstance(c, torch.Tensor) and c.is_cuda
+                                    else _device.from_numpy(np.ascontiguousarray(_host_array(c)))
+                                    for c in raw])
         return _device.DataLoader(self._resident[1], batch_size=self.batch_size, shuffle=self.shuffle,
                                   drop_last=self.drop_last, seed=epoch_seed,
                                   num_workers=self.num_workers, transforms=transforms,
@@ -250,6 +252,23 @@ class DataLoader:
         if batch and (not self.drop_last or len(batch) == self.batch_size):
             yield self._collate_index_batch(batch)
 
+    def _gatherable_columns(self):
+        """The resident device columns when a batch of items can be gathered
+        on the device (tensor columns, default collation, no per-item
+        transform), else None."""
+        if self.collate_fn is not default_collate:
+            return None
+        raw = getattr(self.dataset, "tensors", None)
+        if raw is None or getattr(self.dataset, "native_parts", None) is not None:
+            return None
+        if any(isinstance(c, torch.Tensor) and c.requires_grad for c in raw):
+            return None  # default_collate keeps requires_grad: take the per-item path
+        if self._resident is None or self._resident[0] is not raw:
+            self._resident = (raw, [c if isinstance(c, torch.Tensor) and c.is_cuda
+                                    else _device.from_numpy(np.ascontiguousarray(_host_array(c)))
+                                    for c in raw])
+        return self._resident[1]
+
     def _iter_stream(self):
         items = []
         for item in self.dataset:
@@ -261,6 +280,12 @@ class DataLoader:
             yield self.collate_fn(items)
 
     def _collate_index_batch(self, batch):
+        cols = self._gatherable_columns()
+        if cols is not None:
+            # default_collate of TensorDataset items is the rows stacked per
+            # column, as float32: one device gather instead of per-item fetches
+            out = _device.gather_rows(cols, batch)
+            return tuple(o if o.dtype == torch.float32 else o.float() for o in out)
         if self.num_workers > 1 and len(batch) > 1:
             with ThreadPoolExecutor(max_workers=self.num_workers) as pool:
                 items = list(pool.map(self.dataset.__getitem__, batch))

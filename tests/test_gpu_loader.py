@@ -191,6 +191,8 @@ def test_utils_data_loader_epochs_match_oracle():
     for e in range(2):
         want = O.loader_epoch([x, y], 16, True, True, 40 + e, None, 40 + e, 0)
         _epoch_equal(list(loader), want)
-    got = list(D.DataLoader(D.TensorDataset(x, y), batch_size=3, sampler=[5, 0, 69, 2]))
+    got = list(D.DataLoader(D.TensorDataset(x, y), batch_size=3, sampler=[5, 0, 69, 2, -1]))
     assert np.array_equal(got[0][0].cpu().numpy(), x[[5, 0, 69]])
-    assert np.array_equal(got[1][1].cpu().numpy(), y[[2]])
+    assert np.array_equal(got[1][1].cpu().numpy(), y[[2, -1]])
+    with pytest.raises(IndexError, match="index 70 is out of bounds for axis 0 with size 70"):
+        list(D.DataLoader(D.TensorDataset(x, y), batch_size=2, sampler=[1, 70]))

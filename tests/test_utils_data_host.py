@@ -31,8 +31,13 @@ def fakes(monkeypatch):
         uploads.append(np.array(a))
         return np.array(a)
 
+    def fake_gather_rows(columns, indices):
+        import torch
+        return [torch.from_numpy(np.asarray(c)[np.asarray(indices, np.int64)]) for c in columns]
+
     monkeypatch.setattr(device, "DataLoader", _FakeLoader)
     monkeypatch.setattr(device, "from_numpy", fake_from_numpy)
+    monkeypatch.setattr(device, "gather_rows", fake_gather_rows)
     return uploads
 
 
@@ -69,8 +74,11 @@ def test_samplers_and_custom_collate_take_the_generic_path(fakes):
     got = list(D.DataLoader(ds, batch_size=4, sampler=[9, 1, 3, 5, 7], collate_fn=lambda it: it))
     assert got == [[(9.0,), (1.0,), (3.0,), (5.0,)], [(7.0,)]]
     assert not _FakeLoader.made
+    # a sampler with the default collation: the sampled rows, gathered per batch
     batches = list(D.DataLoader(ds, batch_size=3, sampler=D.SequentialSampler(ds), drop_last=True))
     assert len(batches) == 3 and np.array_equal(batches[1][0], [3.0, 4.0, 5.0])
+    got = list(D.DataLoader(ds, batch_sampler=[[4, 2], [9]]))
+    assert np.array_equal(got[0][0], [4.0, 2.0]) and np.array_equal(got[1][0], [9.0])
 
 
 def test_random_sampler_streams():
