@@ -9,6 +9,8 @@ import os
 import subprocess
 import sys
 
+import pytest
+
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
@@ -17,8 +19,10 @@ def _bench(*args, timeout=600):
                           capture_output=True, text=True, timeout=timeout)
 
 
-def test_reference_arm_json_line():
-    r = _bench("--impl", "reference", "--steps", "1", "--warmup", "3")
+@pytest.mark.parametrize("workload", [None, "optim", "loader"])
+def test_reference_arm_json_line(workload):
+    extra = ("--workload", workload) if workload else ()
+    r = _bench("--impl", "reference", "--steps", "1", "--warmup", "3", *extra)
     assert r.returncode == 0, r.stderr[-2000:]
     lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
     assert len(lines) == 1, r.stdout[-2000:]
