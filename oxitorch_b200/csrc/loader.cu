@@ -80,13 +80,17 @@ class Mt19937 {
  private:
   static constexpr int kN = 624;
   static constexpr int kM = 397;
+  static uint32_t twist(uint32_t hi, uint32_t lo, uint32_t far) {
+    const uint32_t y = (hi & 0x80000000u) | (lo & 0x7fffffffu);
+    return far ^ (y >> 1) ^ ((0u - (y & 1u)) & 0x9908b0dfu);
+  }
+  // The recurrence over the state in place, in three index ranges so that no
+  // index wraps inside a loop.
   void regenerate() {
-    for (int i = 0; i < kN; ++i) {
-      const uint32_t y = (s_[i] & 0x80000000u) | (s_[(i + 1) % kN] & 0x7fffffffu);
-      uint32_t v = s_[(i + kM) % kN] ^ (y >> 1);
-      if (y & 1u) v ^= 0x9908b0dfu;
-      s_[i] = v;
-    }
+    int i = 0;
+    for (; i < kN - kM; ++i) s_[i] = twist(s_[i], s_[i + 1], s_[i + kM]);
+    for (; i < kN - 1; ++i) s_[i] = twist(s_[i], s_[i + 1], s_[i + kM - kN]);
+    s_[kN - 1] = twist(s_[kN - 1], s_[0], s_[kM - 1]);
     pos_ = 0;
   }
   uint32_t s_[kN];
