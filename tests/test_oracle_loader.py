@@ -284,3 +284,49 @@ def test_library_transform_plan_rejects_bad_arguments():
     assert L.oxc_epoch_transform_plan(order.ctypes.data, 4, 2, 0, flip.ctypes.data, zarg.ctypes.data,
                                       None, 1, 4, shape.ctypes.data, planes, 1, result.ctypes.data) == 1
     assert "plane buffer holds 1 planes" in N.last_error()
+
+
+@pytest.mark.parametrize("case", range(12))
+def test_library_transform_plan_random_pipelines(case):
+    """Seeded random pipelines of one to five steps over rank-3 and rank-4
+    columns with ragged last batches: the composed plane maps, applied with
+    the kernel's indexing, reproduce the oracle batch by batch."""
+    N, L = _lib()
+    rng = np.random.default_rng(1000 + case)
+    rank = 4 if case % 3 else 3
+    c = int(rng.integers(1, 4))
+    h, w = int(rng.integers(3, 9)), int(rng.integers(3, 9))
+    n = int(rng.integers(5, 30))
+    bs = int(rng.integers(1, 9))
+    shape = (n, c, h, w) if rank == 4 else (n, h, w)
+    steps, ch, hh, ww = [], None, h, w
+    for _ in range(int(rng.integers(1, 6))):
+        kind = rng.choice(["crop", "flip", "normalize"])
+        if kind == "crop":
+            size = int(rng.integers(1, min(hh, ww) + 1))
+            steps.append(("crop", size))
+            hh = ww = size
+        elif kind == "flip":
+            steps.append(("flip",))
+        elif rank == 4 and sum(s[0] == "normalize" for s in steps) < 4:
+            mean = rng.standard_normal(c).astype(np.float32).tolist()
+            std = rng.uniform(0.2, 2.0, c).astype(np.float32).tolist()
+            steps.append(("normalize", mean, std))
+    if not steps:
+        steps = [("flip",)]
+    col = rng.standard_normal(shape).astype(np.float32)
+    order = np.random.RandomState(case).permutation(n).astype(np.int64)
+    tseed = O.epoch_seed(case, 3)
+    st, planes, result, tf = _plan(L, N, order, bs, tseed, steps, shape)
+    assert st == 0, N.last_error()
+    nplanes, oh, ow = int(result[0]), int(result[1]), int(result[2])
+    channels = c if rank == 4 else bs
+    got = _apply_planes(col, order, planes, nplanes, (oh, ow), tf._norm_table(channels), channels)
+    want = []
+    for k in range(0, n, bs):
+        idx = order[k:k + bs].tolist()
+        b = O.gather_columns([col], idx)[0]
+        r = O.batch_rng(O.batch_seed(tseed, O.indices_seed(idx)))
+        want.append(O.apply_transforms(b, steps, r).reshape(-1, oh, ow))
+    want = np.concatenate(want)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
