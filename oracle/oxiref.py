@@ -281,6 +281,85 @@ def scatter_index_select(g, dim, idx, full_shape):
     return out
 
 
+def t_scatter_dim0(base, indices, values):
+    """Tensor::scatter_dim0 (crates/oxi-tensor/src/lib.rs:895-933): a copy of
+    ``base`` whose rows ``indices[p]`` (negative ids wrap) take ``values[p]``,
+    in position order, so a repeated row keeps its last write."""
+    if np.ndim(base) == 0:
+        raise InvalidArgument("invalid argument: scatter_dim0 requires at least a 1-D tensor")
+    base, values = f32(base), f32(values)
+    shape = (len(indices),) + base.shape[1:]
+    if values.shape != shape:
+        raise ShapeMismatch(f"shape mismatch: {list(values.shape)} vs {list(shape)}")
+    rows = base.shape[0]
+    for i in indices:
+        r = rows + i if i < 0 else i
+        if r < 0 or r >= rows:
+            raise OutOfBounds(f"out of bounds: index {i} out of range for dim 0 of size {rows}")
+    out = base.copy()
+    for p, i in enumerate(indices):
+        out[rows + i if i < 0 else i] = values[p]
+    return out
+
+
+def scatter_dim0_vjp(g, rows, indices):
+    """The VJP closure of ops::scatter_dim0 (crates/oxi-autograd/src/ops.rs:531-598):
+    d/dbase is ``g`` with every written row zeroed; d/dvalues[p] is ``g`` at
+    row ``indices[p]`` when slot p is that row's last write, else zero."""
+    g = f32(g)
+    resolved = [rows + i if i < 0 else i for i in indices]
+    last = {}
+    for p, r in enumerate(resolved):
+        last[r] = p
+    gb = g.copy()
+    for r in last:
+        gb[r] = 0.0
+    gv = np.zeros((len(indices),) + g.shape[1:], np.float32)
+    for p, r in enumerate(resolved):
+        if last[r] == p:
+            gv[p] = g[r]
+    return gb, gv
+
+
+def t_masked_select(x, mask):
+    """Tensor::masked_select (crates/oxi-tensor/src/lib.rs:939-960): the
+    elements of ``x`` where the broadcast ``mask`` is nonzero, in row-major
+    order of the broadcast grid.  The reference marks unpicked slots NaN and
+    then drops every NaN, so a picked NaN of ``x`` is dropped too."""
+    x, mask = f32(x), f32(mask)
+    shape = broadcast_shapes(x.shape, mask.shape)
+    xv = np.broadcast_to(x, shape).reshape(-1)
+    mv = np.broadcast_to(mask, shape).reshape(-1)
+    picked = np.where(mv == 0.0, np.float32(np.nan), xv)
+    return np.ascontiguousarray(picked[~np.isnan(picked)], dtype=np.float32)
+
+
+def masked_select_vjp(g, x_shape, mask):
+    """The VJP closure of ops::masked_select (crates/oxi-autograd/src/ops.rs:610-665):
+    walk the broadcast grid in row-major order; at every point whose mask is
+    nonzero add the next element of ``g`` into the x element that point reads,
+    so elements picked more than once through broadcasting accumulate in grid
+    order, from 0.0, in f32.  The walk follows the mask alone: a picked NaN of
+    x (dropped by the forward) still consumes an element of ``g`` here, and the
+    reference indexes past the end of ``g`` in that case; this restatement
+    raises instead."""
+    g = f32(g).reshape(-1)
+    mask = f32(mask)
+    x_shape = tuple(x_shape)
+    shape = broadcast_shapes(x_shape, mask.shape)
+    mv = np.broadcast_to(mask, shape).reshape(-1)
+    x_index = np.broadcast_to(np.arange(int(np.prod(x_shape, dtype=np.int64)),
+                                        dtype=np.int64).reshape(x_shape), shape).reshape(-1)
+    grads = np.zeros(int(np.prod(x_shape, dtype=np.int64)), np.float32)
+    pick = 0
+    for k in np.flatnonzero(mv != 0.0):
+        if pick >= g.size:
+            raise OutOfBounds("out of bounds: masked_select grad has fewer elements than picks")
+        grads[x_index[k]] = np.float32(grads[x_index[k]] + g[pick])
+        pick += 1
+    return grads.reshape(x_shape)
+
+
 def full(shape, c):
     return np.full(shape, np.float32(c), np.float32)
 

@@ -1,0 +1,91 @@
+"""The oracle's scatter_dim0 and masked_select (forward and VJP) pinned on the
+reference's own known answers:
+
+* crates/oxi-tensor/src/tests.rs:378-406 (forward values and errors);
+* crates/oxi-autograd/src/tests.rs:240-331 (last-write-wins grads, broadcast
+  accumulation);
+* python/tests/test_indexing_grad.py:20-70 (the Python surface's cases).
+"""
+import numpy as np
+import pytest
+
+
+def test_scatter_dim0_forward_kats(oracle):
+    base = np.array([[1, 2], [3, 4]], np.float32)
+    out = oracle.t_scatter_dim0(base, [1], np.array([[9, 8]], np.float32))
+    np.testing.assert_array_equal(out, [[1, 2], [9, 8]])
+    np.testing.assert_array_equal(oracle.t_index_select(out, 0, [1]), [[9, 8]])
+    with pytest.raises(oracle.OutOfBounds, match="index 5 out of range for dim 0 of size 2"):
+        oracle.t_scatter_dim0(base, [5], np.array([[9, 8]], np.float32))
+    with pytest.raises(oracle.ShapeMismatch):
+        oracle.t_scatter_dim0(base, [0], np.zeros((2, 2), np.float32))
+    with pytest.raises(oracle.InvalidArgument):
+        oracle.t_scatter_dim0(np.float32(1.0), [0], np.zeros((1,), np.float32))
+
+
+def test_scatter_dim0_last_write_wins_kats(oracle):
+    b = np.array([[10, 11], [20, 21], [30, 31]], np.float32)
+    v = np.array([[1, 2], [3, 4], [5, 6]], np.float32)
+    out = oracle.t_scatter_dim0(b, [2, 0, 2], v)
+    np.testing.assert_array_equal(out, [[3, 4], [20, 21], [5, 6]])
+    gb, gv = oracle.scatter_dim0_vjp(np.ones((3, 2), np.float32), 3, [2, 0, 2])
+    np.testing.assert_array_equal(gb, [[0, 0], [1, 1], [0, 0]])
+    np.testing.assert_array_equal(gv, [[0, 0], [1, 1], [1, 1]])
+    # negative ids wrap like the forward (rows + i)
+    gb, gv = oracle.scatter_dim0_vjp(np.ones((3, 2), np.float32), 3, [-1, 0, 2])
+    np.testing.assert_array_equal(gb, [[0, 0], [1, 1], [0, 0]])
+    np.testing.assert_array_equal(gv, [[0, 0], [1, 1], [1, 1]])
+
+
+def test_scatter_dim0_matches_numpy_assignment(oracle):
+    rng = np.random.default_rng(7)
+    a = rng.standard_normal((5, 3)).astype(np.float32)
+    vals = rng.standard_normal((3, 3)).astype(np.float32)
+    want = a.copy()
+    want[[4, 1, 4]] = vals
+    np.testing.assert_array_equal(oracle.t_scatter_dim0(a, [4, 1, 4], vals), want)
+
+
+def test_masked_select_forward_kats(oracle):
+    base = np.array([[1, 2, 3], [4, 5, 6]], np.float32)
+    mask = np.array([[1, 0, 1], [0, 1, 0]], np.float32)
+    np.testing.assert_array_equal(oracle.t_masked_select(base, mask), [1, 3, 5])
+    np.testing.assert_array_equal(oracle.t_masked_select(base, np.array([1, 0, 0], np.float32)),
+                                  [1, 4])
+    a = np.random.default_rng(3).standard_normal((4, 5)).astype(np.float32)
+    np.testing.assert_array_equal(oracle.t_masked_select(a, (a > 0).astype(np.float32)), a[a > 0])
+
+
+def test_masked_select_drops_picked_nan(oracle):
+    """The NaN sentinel of lib.rs:952 also drops a picked NaN of x; a NaN mask
+    entry is nonzero and picks."""
+    x = np.array([1.0, np.nan, 3.0], np.float32)
+    np.testing.assert_array_equal(oracle.t_masked_select(x, np.ones(3, np.float32)), [1, 3])
+    np.testing.assert_array_equal(
+        oracle.t_masked_select(np.array([1, 2], np.float32), np.array([np.nan, 0], np.float32)), [1])
+
+
+def test_masked_select_vjp_kats(oracle):
+    # broadcast row mask [1, 0, 1]: picks (0,0), (0,2), (1,0), (1,2)
+    gx = oracle.masked_select_vjp(np.array([10, 20, 30, 40], np.float32), (2, 3),
+                                  np.array([1, 0, 1], np.float32))
+    np.testing.assert_array_equal(gx, [[10, 0, 20], [30, 0, 40]])
+    # a column broadcast against a [2, 3] mask picks each element twice
+    col = np.array([[7.0], [9.0]], np.float32)
+    mc = np.array([[1, 1, 0], [0, 1, 1]], np.float32)
+    np.testing.assert_array_equal(oracle.t_masked_select(col, mc), [7, 7, 9, 9])
+    gx = oracle.masked_select_vjp(np.array([1, 2, 3, 4], np.float32), (2, 1), mc)
+    np.testing.assert_array_equal(gx, [[3], [7]])
+
+
+def test_masked_select_vjp_matches_dense_multiply(oracle):
+    rng = np.random.default_rng(11)
+    up = rng.standard_normal((2, 3)).astype(np.float32)
+    mask = (rng.standard_normal((2, 3)) > 0).astype(np.float32)
+    gx = oracle.masked_select_vjp(up[mask > 0], (2, 3), mask)
+    np.testing.assert_array_equal(gx, mask * up)
+
+
+def test_masked_select_vjp_rejects_short_grad(oracle):
+    with pytest.raises(oracle.OutOfBounds):
+        oracle.masked_select_vjp(np.array([1.0], np.float32), (2,), np.ones(2, np.float32))
