@@ -352,6 +352,21 @@ oxc_status oxc_embedding_bwd(const float* dout, const int64_t* ids, float* dtabl
                              int64_t cols, int32_t* err_flag, void* workspace,
                              size_t workspace_bytes, void* stream);
 
+/* ---- dim-0 scatter and its VJP: row selection ------------------------------
+ * Replaces the host loops of Tensor::scatter_dim0 (crates/oxi-tensor/src/lib.rs:
+ * 895-933, Python Tensor.scatter) and of the ops::scatter_dim0 VJP
+ * (crates/oxi-autograd/src/ops.rs:531-598).  out[i] (rows of `inner` floats,
+ * i < n) = a[map[i]] when map[i] >= 0, else b[i] when b is not null, else
+ * zeros.  The caller resolves last-write-wins into `map` (int64, on the
+ * device): forward map[r] = last writer of r or -1 with a = values, b = base;
+ * d/dbase map[r] = r for unwritten rows, -1 for written ones, a = g, b = null;
+ * d/dvalues map[p] = row of p for last writers, -1 for overwritten slots,
+ * a = g, b = null.  map[i] >= a_rows is recorded in err_flag (int32[4]) and
+ * that row is skipped.  Bit-exact (copies). */
+oxc_status oxc_select_rows(const float* a, int64_t a_rows, const int64_t* map, int64_t n,
+                           const float* b, float* out, int64_t inner, int32_t* err_flag,
+                           void* stream);
+
 /* ---- LayerNorm backward without a caller workspace ------------------------
  * No counterpart in the reference: an addition for callers that cannot call
  * cudaMalloc (a host that owns all device memory through its own pool, or a

@@ -304,3 +304,86 @@ def scale_(g, scale):
     N.check(N.load().oxc_binary_scalar(2, ctypes.byref(v), float(scale), 0, ctypes.byref(v),
                                        _stream()), "scale_")
     return g
+
+
+# ---- dim-0 scatter (Tensor::scatter_dim0) and its VJP ------------------------------------------
+
+def scatter_dim0_maps(rows, indices):
+    """Row maps of one scatter (host work, no device access).
+
+    The reference resolves last-write-wins with host loops over the index
+    list (crates/oxi-autograd/src/ops.rs:531-559); the same resolution here
+    yields the three ``oxc_select_rows`` maps:
+    ``fwd[r]`` = last writer of row r or -1 (keep ``base``);
+    ``keep[r]`` = r for unwritten rows, -1 for written ones (d/dbase);
+    ``win[p]`` = row of slot p when p is that row's last write, else -1
+    (d/dvalues).  Indices are validated first with the reference's message
+    (lib.rs:911-919); negative ids count from the end."""
+    import numpy as np
+    ids = [int(i) for i in indices]
+    for i in ids:
+        r = rows + i if i < 0 else i
+        if r < 0 or r >= rows:
+            raise RuntimeError(f"out of bounds: index {i} out of range for dim 0 of size {rows}")
+    resolved = np.array([rows + i if i < 0 else i for i in ids], dtype=np.int64)
+    fwd = np.full(rows, -1, dtype=np.int64)
+    fwd[resolved] = np.arange(len(ids), dtype=np.int64)  # repeated rows: the last slot stays
+    keep = np.where(fwd < 0, np.arange(rows, dtype=np.int64), -1)
+    win = np.where(fwd[resolved] == np.arange(len(ids)), resolved, -1) if ids else resolved
+    return fwd, keep, win
+
+
+def _select_rows(a, a_rows, idx_map, n, b, inner, device):
+    """One oxc_select_rows launch.  The maps come from scatter_dim0_maps, which
+    validated every index on the host, so no error flag is read back (the
+    call stays asynchronous)."""
+    out = torch.empty((n, inner), dtype=torch.float32, device=device)
+    m = torch.as_tensor(idx_map, dtype=torch.int64).to(device)
+    N.check(N.load().oxc_select_rows(a.data_ptr() if a is not None else None, a_rows, m.data_ptr(),
+                                     n, b.data_ptr() if b is not None else None, out.data_ptr(),
+                                     inner, None, _stream()), "select_rows")
+    return out
+
+
+class _ScatterDim0(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, base, values, maps):
+        fwd, keep, win = maps
+        rows, inner = base.shape[0], base[0].numel() if base.shape[0] else 0
+        out = _select_rows(values.contiguous(), values.shape[0], fwd, rows, base.contiguous(),
+                           inner, base.device)
+        ctx.maps, ctx.rows, ctx.inner = (keep, win), rows, inner
+        ctx.base_shape, ctx.values_shape = base.shape, values.shape
+        return out.reshape(base.shape)
+
+    @staticmethod
+    def backward(ctx, g):
+        keep, win = ctx.maps
+        g = g.contiguous()
+        gb = gv = None
+        if ctx.needs_input_grad[0]:
+            gb = _select_rows(g, ctx.rows, keep, ctx.rows, None, ctx.inner,
+                              g.device).reshape(ctx.base_shape)
+        if ctx.needs_input_grad[1]:
+            gv = _select_rows(g, ctx.rows, win, len(win), None, ctx.inner,
+                              g.device).reshape(ctx.values_shape)
+        return gb, gv, None
+
+
+def scatter_dim0(base, indices, values):
+    """Tensor::scatter_dim0 (crates/oxi-tensor/src/lib.rs:895-933; Python
+    ``Tensor.scatter``): a copy of ``base`` whose rows ``indices[p]`` take
+    ``values[p]``, the last write winning on repeated rows.  Its VJP is the
+    reference's (crates/oxi-autograd/src/ops.rs:531-598): ``base`` gets the
+    upstream grad with written rows zeroed, ``values`` gets the grad of the row
+    each slot finally wrote and zero for overwritten slots.  One
+    ``oxc_select_rows`` launch per result."""
+    _require_cuda_f32("base", base)
+    _require_cuda_f32("values", values)
+    if base.dim() == 0:
+        raise ValueError("invalid argument: scatter_dim0 requires at least a 1-D tensor")
+    want = (len(indices),) + tuple(base.shape[1:])
+    if tuple(values.shape) != want:
+        raise ValueError(f"shape mismatch: {list(values.shape)} vs {list(want)}")
+    maps = scatter_dim0_maps(base.shape[0], indices)
+    return _ScatterDim0.apply(base, values, maps)

@@ -89,3 +89,41 @@ def test_masked_select_vjp_matches_dense_multiply(oracle):
 def test_masked_select_vjp_rejects_short_grad(oracle):
     with pytest.raises(oracle.OutOfBounds):
         oracle.masked_select_vjp(np.array([1.0], np.float32), (2,), np.ones(2, np.float32))
+
+
+# ---- the library's host-side scatter planning against the oracle ---------------------------------
+
+def _apply(a, idx_map, b, inner_shape):
+    """oxc_select_rows restated: out[i] = a[map[i]] if map[i] >= 0 else (b[i] or 0)."""
+    out = np.zeros((len(idx_map),) + inner_shape, np.float32)
+    for i, r in enumerate(idx_map):
+        if r >= 0:
+            out[i] = a[r]
+        elif b is not None:
+            out[i] = b[i]
+    return out
+
+
+@pytest.mark.parametrize("rows,indices", [
+    (3, [2, 0, 2]), (3, [-1, 0, 2]), (5, [4, 1, 4]), (4, []), (6, [5, 5, 5, -6, 0, 3, -3]),
+    (1, [0, 0]), (7, list(range(7))), (7, list(range(-1, -8, -1)))])
+def test_library_scatter_maps_reproduce_oracle(oracle, rows, indices):
+    from oxitorch_b200 import tensor_ops as T
+    rng = np.random.default_rng(rows * 31 + len(indices))
+    base = rng.standard_normal((rows, 2, 3)).astype(np.float32)
+    values = rng.standard_normal((len(indices), 2, 3)).astype(np.float32)
+    g = rng.standard_normal((rows, 2, 3)).astype(np.float32)
+    fwd, keep, win = T.scatter_dim0_maps(rows, indices)
+    np.testing.assert_array_equal(_apply(values, fwd, base, (2, 3)),
+                                  oracle.t_scatter_dim0(base, indices, values))
+    gb, gv = oracle.scatter_dim0_vjp(g, rows, indices)
+    np.testing.assert_array_equal(_apply(g, keep, None, (2, 3)), gb)
+    np.testing.assert_array_equal(_apply(g, win, None, (2, 3)), gv)
+
+
+def test_library_scatter_maps_reject_out_of_range():
+    from oxitorch_b200 import tensor_ops as T
+    with pytest.raises(RuntimeError, match="index 5 out of range for dim 0 of size 2"):
+        T.scatter_dim0_maps(2, [5])
+    with pytest.raises(RuntimeError, match="index -3 out of range for dim 0 of size 2"):
+        T.scatter_dim0_maps(2, [0, -3])
