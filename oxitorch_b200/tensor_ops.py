@@ -333,25 +333,28 @@ def scatter_dim0_maps(rows, indices):
     return fwd, keep, win
 
 
-def _select_rows(a, a_rows, idx_map, n, b, inner, device):
-    """One oxc_select_rows launch.  The maps come from scatter_dim0_maps, which
-    validated every index on the host, so no error flag is read back (the
-    call stays asynchronous)."""
+def _select_rows(a, a_rows, dmap, b, inner, device):
+    """One oxc_select_rows launch over the device map ``dmap``.  The maps come
+    from scatter_dim0_maps, which validated every index on the host, so no
+    error flag is read back (the call stays asynchronous)."""
+    n = dmap.numel()
     out = torch.empty((n, inner), dtype=torch.float32, device=device)
-    m = torch.as_tensor(idx_map, dtype=torch.int64).to(device)
-    N.check(N.load().oxc_select_rows(a.data_ptr() if a is not None else None, a_rows, m.data_ptr(),
-                                     n, b.data_ptr() if b is not None else None, out.data_ptr(),
-                                     inner, None, _stream()), "select_rows")
+    N.check(N.load().oxc_select_rows(a.data_ptr() if a is not None else None, a_rows,
+                                     dmap.data_ptr(), n, b.data_ptr() if b is not None else None,
+                                     out.data_ptr(), inner, None, _stream()), "select_rows")
     return out
 
 
 class _ScatterDim0(torch.autograd.Function):
     @staticmethod
     def forward(ctx, base, values, maps):
-        fwd, keep, win = maps
+        import numpy as np
         rows, inner = base.shape[0], base[0].numel() if base.shape[0] else 0
-        out = _select_rows(values.contiguous(), values.shape[0], fwd, rows, base.contiguous(),
-                           inner, base.device)
+        # the three maps cross to the device in one copy; the VJP reuses them
+        dmaps = torch.as_tensor(np.concatenate(maps)).to(base.device)
+        fwd, keep, win = dmaps[:rows], dmaps[rows:2 * rows], dmaps[2 * rows:]
+        out = _select_rows(values.contiguous(), values.shape[0], fwd, base.contiguous(), inner,
+                           base.device)
         ctx.maps, ctx.rows, ctx.inner = (keep, win), rows, inner
         ctx.base_shape, ctx.values_shape = base.shape, values.shape
         return out.reshape(base.shape)
@@ -362,11 +365,9 @@ class _ScatterDim0(torch.autograd.Function):
         g = g.contiguous()
         gb = gv = None
         if ctx.needs_input_grad[0]:
-            gb = _select_rows(g, ctx.rows, keep, ctx.rows, None, ctx.inner,
-                              g.device).reshape(ctx.base_shape)
+            gb = _select_rows(g, ctx.rows, keep, None, ctx.inner, g.device).reshape(ctx.base_shape)
         if ctx.needs_input_grad[1]:
-            gv = _select_rows(g, ctx.rows, win, len(win), None, ctx.inner,
-                              g.device).reshape(ctx.values_shape)
+            gv = _select_rows(g, ctx.rows, win, None, ctx.inner, g.device).reshape(ctx.values_shape)
         return gb, gv, None
 
 
