@@ -321,6 +321,19 @@ def scatter_dim0_vjp(g, rows, indices):
     return gb, gv
 
 
+def narrow_dim0_vjp(g, orig_shape, offset, length):
+    """The VJP closure of ops::narrow_dim0 (crates/oxi-autograd/src/ops.rs:427-442):
+    ``offset`` zero rows, the upstream grad, then ``max(0, rows - offset -
+    length)`` zero rows, joined by ``concat_rows`` (:445-455) into rows of the
+    original row width; returned in the original shape."""
+    g = f32(g)
+    width = int(np.prod(orig_shape[1:], dtype=np.int64)) if len(orig_shape) > 1 else 1
+    after = max(0, orig_shape[0] - offset - length)
+    parts = [np.zeros((offset, width), np.float32), g.reshape(-1, width) if g.size else
+             np.zeros((0, width), np.float32), np.zeros((after, width), np.float32)]
+    return np.concatenate(parts).reshape(orig_shape)
+
+
 def t_masked_select(x, mask):
     """Tensor::masked_select (crates/oxi-tensor/src/lib.rs:939-960): the
     elements of ``x`` where the broadcast ``mask`` is nonzero, in row-major

@@ -388,3 +388,54 @@ def scatter_dim0(base, indices, values):
         raise ValueError(f"shape mismatch: {list(values.shape)} vs {list(want)}")
     maps = scatter_dim0_maps(base.shape[0], indices)
     return _ScatterDim0.apply(base, values, maps)
+
+
+# ---- narrow along dim 0 (Python slicing) and its zero-padding VJP ----------------------------
+
+def _slice_bounds(rows, lo, hi):
+    """layout::normalize_slice for step 1 (crates/oxi-tensor/src/layout.rs:123-145):
+    negative bounds count from the end and saturate at 0, others clamp to
+    ``rows``; ``hi`` is raised to ``lo`` at least."""
+    def resolve(v):
+        return max(0, rows + v) if v < 0 else min(v, rows)
+    lo = resolve(int(lo))
+    return lo, max(resolve(int(hi)), lo)
+
+
+def narrow_dim0_map(rows, offset, length):
+    """Row map of the narrow VJP: gx[r] = g[r - lo] for the rows the slice
+    kept, -1 (zero) elsewhere.  The reference builds the same rows with
+    ``concat_rows`` of zero blocks around g (crates/oxi-autograd/src/ops.rs:431-455)."""
+    import numpy as np
+    lo, hi = _slice_bounds(rows, offset, offset + length)
+    r = np.arange(rows, dtype=np.int64)
+    return np.where((r >= lo) & (r < hi), r - lo, -1), lo, hi
+
+
+class _NarrowDim0(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, offset, length):
+        m, lo, hi = narrow_dim0_map(x.shape[0], offset, length)
+        ctx.map, ctx.kept, ctx.shape = m, hi - lo, x.shape
+        # a view, as Tensor::narrow returns (lib.rs:620-636)
+        return x.narrow(0, lo, hi - lo)
+
+    @staticmethod
+    def backward(ctx, g):
+        inner = 1
+        for d in ctx.shape[1:]:
+            inner *= d
+        dmap = torch.as_tensor(ctx.map).to(g.device)
+        gx = _select_rows(g.contiguous(), ctx.kept, dmap, None, inner, g.device)
+        return gx.reshape(ctx.shape), None, None
+
+
+def narrow_dim0(x, offset, length):
+    """ops::narrow_dim0 (crates/oxi-autograd/src/ops.rs:427-442), the op behind
+    integer and slice indexing on dim 0 (crates/oxi-bindings/src/lib.rs:575-620):
+    rows [offset, offset + length) as a view; the VJP writes the upstream grad
+    back at those rows and zeros elsewhere, one ``oxc_select_rows`` launch."""
+    _require_cuda_f32("x", x)
+    if x.dim() == 0:
+        raise ValueError("invalid argument: dim 0 out of range for 0-D tensor")
+    return _NarrowDim0.apply(x, int(offset), int(length))

@@ -84,3 +84,18 @@ def test_select_rows_abi_records_a_map_past_the_source():
     np.testing.assert_array_equal(got[2], [0, 0, 0, 0])
     assert L.oxc_select_rows(a.data_ptr(), 3, None, 3, None, out.data_ptr(), 4, None, s) \
         == N.ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("shape,offset,length", [((4, 3), 1, 2), ((512, 1024), 100, 300),
+                                                 ((9, 5, 3), 8, 4), ((6, 4), 2, 0)])
+def test_narrow_dim0_view_and_zero_padding_vjp(oracle, shape, offset, length):
+    from oxitorch_b200 import tensor_ops as T
+    rng = np.random.default_rng(shape[0] + offset)
+    x = rng.standard_normal(shape).astype(np.float32)
+    xd = _dev(x, True)
+    y = T.narrow_dim0(xd, offset, length)
+    np.testing.assert_array_equal(_host(y), x[offset:offset + length])
+    g = rng.standard_normal(tuple(y.shape)).astype(np.float32)
+    y.backward(_dev(g))
+    np.testing.assert_array_equal(_host(xd.grad),
+                                  oracle.narrow_dim0_vjp(g, shape, offset, y.shape[0]))

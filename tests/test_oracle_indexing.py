@@ -127,3 +127,23 @@ def test_library_scatter_maps_reject_out_of_range():
         T.scatter_dim0_maps(2, [5])
     with pytest.raises(RuntimeError, match="index -3 out of range for dim 0 of size 2"):
         T.scatter_dim0_maps(2, [0, -3])
+
+
+def test_narrow_dim0_vjp_pads_with_zero_rows(oracle):
+    g = np.array([[1, 2, 3], [4, 5, 6]], np.float32)
+    np.testing.assert_array_equal(oracle.narrow_dim0_vjp(g, (4, 3), 1, 2),
+                                  [[0, 0, 0], [1, 2, 3], [4, 5, 6], [0, 0, 0]])
+    np.testing.assert_array_equal(oracle.narrow_dim0_vjp(g[:1].reshape(1, 3, 1), (3, 3, 1), 2, 1),
+                                  np.array([0, 0, 0, 0, 0, 0, 1, 2, 3], np.float32).reshape(3, 3, 1))
+
+
+@pytest.mark.parametrize("rows,offset,length", [(4, 1, 2), (5, 0, 5), (5, 4, 1), (6, 2, 0),
+                                                (3, 1, 5), (7, 0, 1)])
+def test_library_narrow_map_reproduces_oracle(oracle, rows, offset, length):
+    from oxitorch_b200 import tensor_ops as T
+    m, lo, hi = T.narrow_dim0_map(rows, offset, length)
+    kept = hi - lo
+    assert kept == len(range(rows)[offset:offset + length])
+    g = np.random.default_rng(rows + offset).standard_normal((kept, 2, 2)).astype(np.float32)
+    np.testing.assert_array_equal(_apply(g, m, None, (2, 2)),
+                                  oracle.narrow_dim0_vjp(g, (rows, 2, 2), offset, kept))
