@@ -361,7 +361,10 @@ oxc_status oxc_embedding_bwd(const float* dout, const int64_t* ids, float* dtabl
  * device): forward map[r] = last writer of r or -1 with a = values, b = base;
  * d/dbase map[r] = r for unwritten rows, -1 for written ones, a = g, b = null;
  * d/dvalues map[p] = row of p for last writers, -1 for overwritten slots,
- * a = g, b = null.  map[i] >= a_rows is recorded in err_flag (int32[4]) and
+ * a = g, b = null.  The same call gives the ops::narrow_dim0 VJP
+ * (crates/oxi-autograd/src/ops.rs:427-455, concat_rows of zero blocks around
+ * g): map[r] = r - lo for the kept rows, -1 elsewhere, a = g, b = null.
+ * map[i] >= a_rows is recorded in err_flag (int32[4]) and
  * that row is skipped.  Bit-exact (copies). */
 oxc_status oxc_select_rows(const float* a, int64_t a_rows, const int64_t* map, int64_t n,
                            const float* b, float* out, int64_t inner, int32_t* err_flag,
