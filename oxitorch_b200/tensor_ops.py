@@ -327,7 +327,7 @@ def scatter_dim0_maps(rows, indices):
             raise RuntimeError(f"out of bounds: index {i} out of range for dim 0 of size {rows}")
     resolved = np.array([rows + i if i < 0 else i for i in ids], dtype=np.int64)
     fwd = np.full(rows, -1, dtype=np.int64)
-    fwd[resolved] = np.arange(len(ids), dtype=np.int64)  # repeated rows: the last slot stays
+    np.maximum.at(fwd, resolved, np.arange(len(ids), dtype=np.int64))  # the last slot of a row wins
     keep = np.where(fwd < 0, np.arange(rows, dtype=np.int64), -1)
     win = np.where(fwd[resolved] == np.arange(len(ids)), resolved, -1) if ids else resolved
     return fwd, keep, win
