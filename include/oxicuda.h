@@ -370,6 +370,34 @@ oxc_status oxc_select_rows(const float* a, int64_t a_rows, const int64_t* map, i
                            const float* b, float* out, int64_t inner, int32_t* err_flag,
                            void* stream);
 
+/* ---- masked_select: boolean-mask indexing and its VJP -------------------------
+ * Replaces Tensor::masked_select (crates/oxi-tensor/src/lib.rs:939-960) and the
+ * host walk of the ops::masked_select VJP (crates/oxi-autograd/src/ops.rs:
+ * 610-665).  x and mask are views of the broadcast grid's shape (broadcast
+ * dims with stride 0); picks follow the grid's row-major order.
+ * oxc_masked_select_count: per-chunk pick counts turned into offsets in the
+ *   workspace (int64), the total at index ceil(n / 4096) (n = grid points).
+ *   by_mask = 0: the forward's picks (mask != 0 and x not NaN: the
+ *   reference's NaN sentinel drops picked NaNs); by_mask = 1: the VJP's
+ *   (mask != 0; x may be null).
+ * oxc_masked_select_fwd: out[total] = the picked x values (after a by_mask = 0
+ *   count).
+ * oxc_masked_select_bwd: gfull (dense, grid-shaped) = g[rank] at every point
+ *   the mask picks, 0 elsewhere (after a by_mask = 1 count); ranks >= ng
+ *   give 0.
+ * oxc_broadcast_fold: gx[x_shape] = the sum of gfull over the grid dims where
+ *   x has size 1, each x element folded in grid order from +0.0 in f32 (the
+ *   reference's accumulation order for elements picked more than once). */
+size_t oxc_masked_select_workspace_size(int64_t n);
+oxc_status oxc_masked_select_count(const oxc_view* x, const oxc_view* mask, int32_t by_mask,
+                                   void* workspace, size_t workspace_bytes, void* stream);
+oxc_status oxc_masked_select_fwd(const oxc_view* x, const oxc_view* mask, const void* workspace,
+                                 float* out, void* stream);
+oxc_status oxc_masked_select_bwd(const float* g, int64_t ng, const oxc_view* mask,
+                                 const void* workspace, float* gfull, void* stream);
+oxc_status oxc_broadcast_fold(const float* gfull, const int64_t* grid_shape, const int64_t* x_shape,
+                              int32_t ndim, float* gx, void* stream);
+
 /* ---- LayerNorm backward without a caller workspace ------------------------
  * No counterpart in the reference: an addition for callers that cannot call
  * cudaMalloc (a host that owns all device memory through its own pool, or a

@@ -114,6 +114,11 @@ SIGNATURES = {
     "oxc_embedding_bwd_workspace_size": (_SZ, [_I64, _I64, _I64]),
     "oxc_embedding_bwd": (_I32, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _SZ, _P]),
     "oxc_select_rows": (_I32, [_P, _I64, _P, _I64, _P, _P, _I64, _P, _P]),
+    "oxc_masked_select_workspace_size": (_SZ, [_I64]),
+    "oxc_masked_select_count": (_I32, [_VP, _VP, _I32, _P, _SZ, _P]),
+    "oxc_masked_select_fwd": (_I32, [_VP, _VP, _P, _P, _P]),
+    "oxc_masked_select_bwd": (_I32, [_P, _I64, _VP, _P, _P, _P]),
+    "oxc_broadcast_fold": (_I32, [_P, _P, _P, _I32, _P, _P]),
     "oxc_layer_norm_bwd_noalloc": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32,
                                           _I32, _P]),
     "oxc_sgd_step": (_I32, [_P, _P, _P, _I64, _F32, _F32, _I32, _P]),

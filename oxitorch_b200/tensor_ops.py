@@ -439,3 +439,83 @@ def narrow_dim0(x, offset, length):
     if x.dim() == 0:
         raise ValueError("invalid argument: dim 0 out of range for 0-D tensor")
     return _NarrowDim0.apply(x, int(offset), int(length))
+
+
+# ---- masked_select (boolean-mask indexing) and its VJP ---------------------------------------
+
+_MS_CHUNK = 4096  # grid points per count chunk of oxc_masked_select_count
+
+
+def _ms_count(xv, mv, n, by_mask, device):
+    """Pick offsets per chunk in a workspace; returns (workspace, total picks).
+    Reading the total waits for the device: the output's length depends on it."""
+    L = N.load()
+    ws = torch.empty(max(1, L.oxc_masked_select_workspace_size(n) // 8), dtype=torch.int64,
+                     device=device)
+    N.check(L.oxc_masked_select_count(None if xv is None else ctypes.byref(xv), ctypes.byref(mv),
+                                      by_mask, ws.data_ptr(), ws.numel() * 8, _stream()),
+            "masked_select")
+    return ws, int(ws[(n + _MS_CHUNK - 1) // _MS_CHUNK].item())
+
+
+class _MaskedSelect(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, mask, shape):
+        xe, me = x.expand(shape), mask.expand(shape)
+        n = xe.numel()
+        xv, mv = N.make_view(xe), N.make_view(me)
+        ws, total = _ms_count(xv, mv, n, 0, x.device)
+        out = torch.empty(total, dtype=torch.float32, device=x.device)
+        if total:
+            N.check(N.load().oxc_masked_select_fwd(ctypes.byref(xv), ctypes.byref(mv),
+                                                   ws.data_ptr(), out.data_ptr(), _stream()),
+                    "masked_select")
+        ctx.save_for_backward(mask)
+        ctx.shape, ctx.x_shape = tuple(shape), tuple(x.shape)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        (mask,) = ctx.saved_tensors
+        shape, x_shape = ctx.shape, ctx.x_shape
+        me = mask.expand(shape)
+        mv = N.make_view(me)
+        n = me.numel()
+        ws, picks = _ms_count(None, mv, n, 1, g.device)
+        g = g.contiguous()
+        if picks != g.numel():
+            # the reference reads past the end of g here (a picked NaN of x
+            # left the forward shorter than the mask's picks)
+            raise RuntimeError(f"out of bounds: masked_select grad has {g.numel()} elements "
+                               f"for {picks} picks")
+        gfull = torch.empty(shape, dtype=torch.float32, device=g.device)
+        if n:
+            N.check(N.load().oxc_masked_select_bwd(g.data_ptr() if g.numel() else None, g.numel(),
+                                                   ctypes.byref(mv), ws.data_ptr(), gfull.data_ptr(),
+                                                   _stream()), "masked_select backward")
+        aligned = (1,) * (len(shape) - len(x_shape)) + x_shape
+        if aligned == shape:
+            return gfull.reshape(x_shape), None, None
+        gx = torch.empty(x_shape, dtype=torch.float32, device=g.device)
+        gs = (ctypes.c_int64 * max(1, len(shape)))(*shape)
+        xs = (ctypes.c_int64 * max(1, len(shape)))(*aligned)
+        N.check(N.load().oxc_broadcast_fold(gfull.data_ptr(), gs, xs, len(shape), gx.data_ptr(),
+                                            _stream()), "masked_select backward")
+        return gx, None, None
+
+
+def masked_select(x, mask):
+    """Tensor::masked_select (crates/oxi-tensor/src/lib.rs:939-960): the
+    elements of ``x`` where the broadcast ``mask`` is nonzero, as a 1-D tensor
+    in row-major order of the broadcast grid (a picked NaN of ``x`` is
+    dropped, as the reference's NaN sentinel drops it).  The VJP is the
+    reference's (crates/oxi-autograd/src/ops.rs:610-665): each grad element goes
+    back to the x element it was picked from, elements picked more than once
+    through broadcasting accumulating in grid order.  The mask is not
+    differentiated."""
+    _require_cuda_f32("x", x)
+    _require_cuda_f32("mask", mask)
+    shape = _broadcast_shape(tuple(x.shape), tuple(mask.shape))
+    if len(shape) > N.MAX_DIMS:
+        raise NotImplementedError(f"not implemented: tensors of rank {len(shape)} > {N.MAX_DIMS}")
+    return _MaskedSelect.apply(x, mask.detach(), shape)

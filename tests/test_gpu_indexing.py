@@ -12,7 +12,7 @@ pytestmark = pytest.mark.gpu
 
 def _dev(a, grad=False):
     import torch
-    return torch.from_numpy(np.ascontiguousarray(a)).cuda().requires_grad_(grad)
+    return torch.from_numpy(np.array(a, order="C", copy=True)).cuda().requires_grad_(grad)
 
 
 def _host(t):
@@ -99,3 +99,48 @@ def test_narrow_dim0_view_and_zero_padding_vjp(oracle, shape, offset, length):
     y.backward(_dev(g))
     np.testing.assert_array_equal(_host(xd.grad),
                                   oracle.narrow_dim0_vjp(g, shape, offset, y.shape[0]))
+
+
+MASKED = [
+    ((2, 3), (2, 3)),          # the reference's basic case
+    ((2, 3), (3,)),            # a row mask broadcast over x
+    ((2, 1), (2, 3)),          # x broadcast: picks accumulate
+    ((3, 1, 5), (1, 4, 1)),    # both broadcast, x folded over one dim
+    ((1, 6, 1), (5, 1, 7)),    # x folded over two dims in grid order
+    ((300, 200), (300, 200)),  # several count chunks
+    ((4,), ()),                # a 0-d mask
+    ((0, 3), (0, 3)),          # an empty grid
+]
+
+
+@pytest.mark.parametrize("xs,ms", MASKED)
+def test_masked_select_forward_and_vjp_bitexact(oracle, xs, ms):
+    from oxitorch_b200 import tensor_ops as T
+    rng = np.random.default_rng(len(xs) * 10 + len(ms))
+    x = rng.standard_normal(xs).astype(np.float32)
+    mask = np.asarray(rng.random(ms) > 0.4, dtype=np.float32)
+    mask = np.where(np.asarray(rng.random(ms) > 0.8), mask * np.float32(-2.5), mask).astype(np.float32)
+    xd = _dev(x, True)
+    out = T.masked_select(xd, _dev(mask))
+    want = oracle.t_masked_select(x, mask)
+    np.testing.assert_array_equal(_host(out), want)
+    g = rng.standard_normal(want.shape).astype(np.float32)
+    out.backward(_dev(g))
+    np.testing.assert_array_equal(_host(xd.grad), oracle.masked_select_vjp(g, xs, mask))
+
+
+def test_masked_select_reference_cases():
+    import torch
+    from oxitorch_b200 import tensor_ops as T
+    base = torch.tensor([[1.0, 2, 3], [4, 5, 6]], device="cuda")
+    m = torch.tensor([[1.0, 0, 1], [0, 1, 0]], device="cuda")
+    np.testing.assert_array_equal(_host(T.masked_select(base, m)), [1, 3, 5])
+    col = torch.tensor([[7.0], [9.0]], device="cuda", requires_grad=True)
+    picked = T.masked_select(col, torch.tensor([[1.0, 1, 0], [0, 1, 1]], device="cuda"))
+    np.testing.assert_array_equal(_host(picked), [7, 7, 9, 9])
+    picked.backward(torch.tensor([1.0, 2, 3, 4], device="cuda"))
+    np.testing.assert_array_equal(_host(col.grad), [[3], [7]])
+    nan_x = torch.tensor([1.0, float("nan"), 3.0], device="cuda")
+    np.testing.assert_array_equal(_host(T.masked_select(nan_x, torch.ones(3, device="cuda"))), [1, 3])
+    with pytest.raises(ValueError, match="shape mismatch"):
+        T.masked_select(base, torch.ones(4, device="cuda"))
