@@ -519,3 +519,8 @@ def masked_select(x, mask):
     if len(shape) > N.MAX_DIMS:
         raise NotImplementedError(f"not implemented: tensors of rank {len(shape)} > {N.MAX_DIMS}")
     return _MaskedSelect.apply(x, mask.detach(), shape)
+
+
+# The Python surface's name for the dim-0 scatter (``Tensor.scatter(indices,
+# values)``, crates/oxi-bindings/src/lib.rs:650), with the base tensor first.
+scatter = scatter_dim0
