@@ -410,7 +410,10 @@ oxc_status oxc_broadcast_fold(const float* gfull, const int64_t* grid_shape, con
  * OXC_ERR_INVALID_ARGUMENT.  The first call on a device looks up the array's
  * device address (make it before any stream capture); all calls on a device
  * share the array, so calls that overlap on the GPU race and must be
- * serialised by the caller.  Allocates nothing. */
+ * serialised by the caller.  The looked-up address is cached per device for
+ * the life of the process and does not survive cudaDeviceReset: a process
+ * that resets a device must not call this entry point on it again.
+ * Allocates nothing. */
 #define OXC_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 oxc_status oxc_layer_norm_bwd_noalloc(const float* x, const float* w, const float* b,
                                       const float* mean, const float* rstd, const float* dy,

@@ -13,7 +13,10 @@
 //     process exits;
 //   - the first call on a device looks up the array's device address
 //     (cudaGetSymbolAddress) with that device current, once per device; make
-//     that first call before any stream capture;
+//     that first call before any stream capture.  The address is cached per
+//     device for the life of the process; cudaDeviceReset unloads the module
+//     that holds the array, so a process that resets a device must not call
+//     this entry point on it again (the cached address would be stale);
 //   - all calls on a device share the one array: calls whose kernels overlap
 //     on the GPU (different streams, or concurrent host threads) race on it
 //     and must be serialised by the caller;

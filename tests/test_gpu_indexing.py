@@ -87,8 +87,16 @@ def test_select_rows_abi_records_a_map_past_the_source():
 
 
 @pytest.mark.parametrize("shape,offset,length", [((4, 3), 1, 2), ((512, 1024), 100, 300),
-                                                 ((9, 5, 3), 8, 4), ((6, 4), 2, 0)])
+                                                 ((9, 5, 3), 8, 4), ((6, 4), 2, 0),
+                                                 ((5, 3), 0, 2), ((7, 2, 2), 6, 1)])
 def test_narrow_dim0_view_and_zero_padding_vjp(oracle, shape, offset, length):
+    """Offset 0 (x[0:k]) and the last row (x[-1], which the binding's select
+    normalises to offset rows - 1 before narrow_dim0 sees it) are included.
+    At offset 0 the reference's VJP fails instead: its concat_rows takes the
+    row width from the first block, the empty zeros_before, and from_vec then
+    rejects [rows, 0] with the data of g (crates/oxi-autograd/src/ops.rs:
+    427-455).  This path returns the zero-padded gradient there, the result
+    the reference computes for every other offset."""
     from oxitorch_b200 import tensor_ops as T
     rng = np.random.default_rng(shape[0] + offset)
     x = rng.standard_normal(shape).astype(np.float32)

@@ -176,23 +176,3 @@ def test_upload_download_round_trip(nbytes, offset):
     assert np.array_equal(out, host)
     assert L.oxc_upload(raw.data_ptr(), host.ctypes.data, 0, _stream()) == 0
     assert L.oxc_upload(None, host.ctypes.data, 4, _stream()) == 1
-
-
-def test_utils_data_loader_epochs_match_oracle():
-    """utils.data.DataLoader over a TensorDataset: pass e builds the device
-    loader with seed = transform seed = base + e (python/oxitorch/utils/
-    data.py:217-264), so its batches are the oracle's epoch 0 of that seed;
-    the generic path (a sampler) collates to CUDA tensors."""
-    from oxitorch_b200.utils import data as D
-    rng = np.random.default_rng(8)
-    x = rng.standard_normal((70, 3, 4, 4)).astype(np.float32)
-    y = rng.integers(0, 10, 70).astype(np.float32)
-    loader = D.DataLoader(D.TensorDataset(x, y), batch_size=16, shuffle=True, drop_last=True, seed=40)
-    for e in range(2):
-        want = O.loader_epoch([x, y], 16, True, True, 40 + e, None, 40 + e, 0)
-        _epoch_equal(list(loader), want)
-    got = list(D.DataLoader(D.TensorDataset(x, y), batch_size=3, sampler=[5, 0, 69, 2, -1]))
-    assert np.array_equal(got[0][0].cpu().numpy(), x[[5, 0, 69]])
-    assert np.array_equal(got[1][1].cpu().numpy(), y[[2, -1]])
-    with pytest.raises(IndexError, match="index 70 is out of bounds for axis 0 with size 70"):
-        list(D.DataLoader(D.TensorDataset(x, y), batch_size=2, sampler=[1, 70]))

@@ -13,7 +13,7 @@ earlier calls must not matter).
 import numpy as np
 import pytest
 
-from parity import RTOL, ATOL, assert_close
+from parity import assert_bitexact
 
 pytestmark = pytest.mark.gpu
 
@@ -70,10 +70,13 @@ def test_noalloc_matches_workspace_entry_point_twice(rows, cols, act):
     N.check(L.oxc_layer_norm_fwd(x.data_ptr(), w.data_ptr(), b.data_ptr(), y.data_ptr(),
                                  mean.data_ptr(), rstd.data_ptr(), rows, cols, 1e-5, act, stream))
     want = [t.cpu().numpy() for t in _bwd_with_workspace(L, N, x, dy, w, b, mean, rstd, act, stream)]
-    for call in range(2):  # two calls in a row share (and reuse) the fixed scratch
+    # Two calls in a row share (and reuse) the fixed scratch.  The same kernels
+    # run with the same CTA and partial geometry as the workspace entry point,
+    # so the results must be identical bit for bit, not merely close.
+    for call in range(2):
         got = [t.cpu().numpy() for t in _bwd_noalloc(L, N, x, dy, w, b, mean, rstd, act, stream)]
         for name, g, r in zip(("dx", "dweight", "dbias"), got, want):
-            assert_close(g, r, rtol=RTOL, atol=ATOL, what=f"call {call}: {name}")
+            assert_bitexact(g, r, what=f"call {call}: {name}")
 
 
 def test_noalloc_rejects_sizes_beyond_the_fixed_scratch():
