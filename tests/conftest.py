@@ -4,6 +4,7 @@
 exports); `-m gpu` runs the CUDA parity tests on a B200.
 """
 
+import json
 import os
 import sys
 
@@ -35,3 +36,17 @@ def golden():
 def native():
     from oxitorch_b200 import _native
     return _native.load(require_device=True)
+
+
+def pytest_sessionfinish(session, exitstatus):
+    """With $OXC_STRICT_REPORT set, writes every parity check's count of
+    elements beyond the bare tolerance (tests/parity.py STRICT_LOG) there."""
+    path = os.environ.get("OXC_STRICT_REPORT")
+    if not path:
+        return
+    try:
+        import parity
+    except ImportError:
+        return
+    with open(path, "w") as f:
+        json.dump(parity.STRICT_LOG, f, indent=0)

@@ -27,10 +27,17 @@ Tolerances (from the project's parity contract):
 """
 
 import contextlib
+import os
 
 import numpy as np
 
 LIBM_ULPS = 4
+
+# One record per assert_close call: how many elements exceed the BARE
+# tolerance (rtol as passed; atol 1e-6, or the Sigma|terms| * 1e-6 of a sum
+# output, `strict_atol`), i.e. pass only because of the reference-defined
+# budgets above.  tests/conftest.py writes them to $OXC_STRICT_REPORT.
+STRICT_LOG = []
 
 
 @contextlib.contextmanager
@@ -60,6 +67,20 @@ def _absdiff(a, b):
         return np.where(a == b, 0.0, np.abs(a - b))
 
 
+def reference_budget_parts(oracle, run, libm=("tanh",), ulps=LIBM_ULPS):
+    """(outputs, summation-order budgets, libm budgets) of the oracle run
+    `run`; see reference_budget."""
+    base = run()
+    with precise_sums(oracle):
+        exact = run()
+    sums = [_absdiff(e, b) for b, e in zip(base, exact)]
+    if libm:
+        _, lb = libm_budget(oracle, run, libm, ulps)
+    else:
+        lb = [np.zeros(np.shape(b), np.float64) for b in base]
+    return base, sums, lb
+
+
 def reference_budget(oracle, run, libm=("tanh",), ulps=LIBM_ULPS):
     """(outputs, budgets) of the oracle run `run` (a callable returning a tuple
     of arrays).  The budget of each element is what the reference's result is
@@ -67,14 +88,8 @@ def reference_budget(oracle, run, libm=("tanh",), ulps=LIBM_ULPS):
       |run() - run() with f64-folded sums|   (its own left-to-right f32 sums)
     + max over +-ulps of |run() - run() with `libm` results shifted| (libm ulps).
     """
-    base = run()
-    with precise_sums(oracle):
-        exact = run()
-    budget = [_absdiff(e, b) for b, e in zip(base, exact)]
-    if libm:
-        _, lb = libm_budget(oracle, run, libm, ulps)
-        budget = [a + b for a, b in zip(budget, lb)]
-    return base, budget
+    base, sums, lb = reference_budget_parts(oracle, run, libm, ulps)
+    return base, [a + b for a, b in zip(sums, lb)]
 
 
 def max_vjp_budget(oracle, run):
@@ -108,7 +123,39 @@ ATOL = 1e-6
 RTOL_BIG = 1e-4
 
 
-def assert_close(got, want, rtol=RTOL, atol=ATOL, what=""):
+def _current_test():
+    return os.environ.get("PYTEST_CURRENT_TEST", "").split(" ")[0]
+
+
+def strict_breakdown(got, want, rtol, strict_atol, parts, what=""):
+    """Attributes the elements that exceed the bare tolerance
+    (strict_atol + rtol |want|) to the budgets that admit them, in order:
+    `parts` is [(name, per-element budget), ...].  Appends the counts to
+    STRICT_LOG and returns them."""
+    got = np.asarray(got, dtype=np.float64)
+    want = np.asarray(want, dtype=np.float64)
+    with np.errstate(invalid="ignore"):
+        err = np.where(got == want, 0.0, np.abs(got - want))
+        lim = np.broadcast_to(np.asarray(strict_atol, np.float64), want.shape) + rtol * np.abs(want)
+        over = ~np.isnan(want) & ~(err <= lim)
+        counts = {"bare": int(over.sum())}
+        rest = over
+        for name, b in parts:
+            lim = lim + np.broadcast_to(np.asarray(b, np.float64), want.shape)
+            admitted = rest & (err <= lim)
+            counts[name] = int(admitted.sum())
+            rest = rest & ~admitted
+        counts["unadmitted"] = int(rest.sum())
+    rec = {"test": _current_test(), "what": what, "n": int(want.size), "rtol": rtol,
+           "breakdown": counts}
+    STRICT_LOG.append(rec)
+    return counts
+
+
+def assert_close(got, want, rtol=RTOL, atol=ATOL, what="", strict_atol=None):
+    """|got - want| <= atol + rtol |want| element-wise.  `strict_atol` is the
+    bare absolute tolerance of this output (1e-6, or 1e-6 x Sigma|terms| for a
+    sum); the number of elements beyond it is recorded in STRICT_LOG."""
     got = np.asarray(got, dtype=np.float64)
     want = np.asarray(want, dtype=np.float64)
     assert got.shape == want.shape, f"{what}: shape {got.shape} != {want.shape}"
@@ -121,6 +168,12 @@ def assert_close(got, want, rtol=RTOL, atol=ATOL, what=""):
         lim = atol + rtol * np.abs(want)
         # exact equality always passes (infinities included)
         bad = fin & ~(err <= lim) & (got != want)
+        slim = (np.broadcast_to(np.asarray(ATOL if strict_atol is None else strict_atol,
+                                           np.float64), want.shape) + rtol * np.abs(want))
+        over = fin & ~(err <= slim) & (got != want)
+        worst = float(np.max(np.where(over, err / slim, 0.0), initial=0.0))
+    STRICT_LOG.append({"test": _current_test(), "what": what, "n": int(want.size), "rtol": rtol,
+                       "over_bare": int(over.sum()), "worst_err_over_bare": worst})
     if bad.any():
         i = np.unravel_index(np.argmax(np.where(bad, np.nan_to_num(err - lim, nan=np.inf), -np.inf)),
                              want.shape)

@@ -34,6 +34,12 @@ def test_reference_arm_json_line(workload):
     assert d["steps"] == 1 and d["warmup"] == 3 and d["n_gpus"] == 1
     assert d["unit"] == "GB/s" and d["higher_is_better"] is True and d["value"] > 0
     assert "workload" in d["config"]
+    assert d["config"]["rows_per_sample"] >= 1 and d["config"]["processes"] >= 1
+    if workload is None:
+        # the default line carries every other BASELINE config's reference figure
+        assert set(d["per_workload"]) == {"rms", "ce", "embedding", "mlp_block"}
+        for entry in d["per_workload"].values():
+            assert entry["value"] > 0 and entry["config"]["rows_per_sample"] >= 1
     cb = d["cpu_baseline"]
     assert cb["value"] == d["value"] and cb["cores"] >= 1 and cb["kind"] in ("port", "reference")
     assert cb["sample"]

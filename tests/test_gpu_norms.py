@@ -46,12 +46,14 @@ def _check_rms(x, w, dy, y, dx, dw, ref, rstd):
     assert_close(dx, dx_ref, atol=ATOL + bdx, what="dx")
     t1 = x * rstd[:, None]
     scale = np.abs(dy.astype(np.float64) * t1).sum(0)
-    assert_close(dw, dw_ref, atol=ATOL * np.maximum(scale, 1.0) + bdw, what="dw")
+    assert_close(dw, dw_ref, atol=ATOL * np.maximum(scale, 1.0) + bdw, what="dw",
+                 strict_atol=ATOL * np.maximum(scale, 1.0))
     # f64 yardstick: the kernel's dw is within 1e-6 * sum|terms| of the exact value
     x64 = x.astype(np.float64)
     inv64 = 1.0 / np.sqrt((x64 * x64).mean(1) + 1e-6)
     dw64 = (dy.astype(np.float64) * x64 * inv64[:, None]).sum(0)
-    assert_close(dw, dw64, rtol=RTOL, atol=ATOL * np.maximum(scale, 1.0), what="dw vs f64")
+    assert_close(dw, dw64, rtol=RTOL, atol=ATOL * np.maximum(scale, 1.0), what="dw vs f64",
+                 strict_atol=ATOL * np.maximum(scale, 1.0))
 
 
 @pytest.mark.parametrize("name", ["rms_4x4096", "rms_7x1001", "rms_3x4"])
@@ -77,11 +79,10 @@ def test_rms_norm_vs_oracle(oracle, m, n):
 
 def test_rms_norm_config1_full_size(oracle):
     """x [4096, 4096] ~ N(0,1), w ~ U(0.5,1.5), eps 1e-6."""
+    import bench
     from oxitorch_b200 import functional as F
-    rng = np.random.default_rng(1)
-    x = rng.standard_normal((4096, 4096), dtype=np.float32)
-    w = rng.uniform(0.5, 1.5, 4096).astype(np.float32)
-    dy = rng.standard_normal((4096, 4096), dtype=np.float32)
+    inp = bench.config_inputs(1)  # the arrays the benchmark times
+    x, w, dy = inp["x"], inp["w"], inp["dy"]
     ref = _oracle_rms(oracle, x, w, dy)
     y, rstd = F.rms_norm_fwd(_dev(x), _dev(w), 1e-6)
     dx, dw = F.rms_norm_bwd(_dev(x), _dev(w), rstd, _dev(dy))
@@ -166,9 +167,11 @@ def _check_ln(x, w, dy, got, ref, gelu):
     t1 = (x - mean[:, None]) * rstd[:, None]
     g_scale = np.abs(dy.astype(np.float64)) * gf
     cdw = (g_scale * (4 * 2.0 ** -24 * np.abs(mean) * rstd)[:, None]).sum(0)
-    assert_close(dw, dw_ref, atol=ATOL * np.maximum((g_scale * np.abs(t1)).sum(0), 1.0) + bdw + cdw,
-                 what="dw")
-    assert_close(db, db_ref, atol=ATOL * np.maximum(g_scale.sum(0), 1.0) + bdb, what="db")
+    sdw = ATOL * np.maximum((g_scale * np.abs(t1)).sum(0), 1.0)
+    sdb = ATOL * np.maximum(g_scale.sum(0), 1.0)
+    assert_close(dw, dw_ref, atol=sdw + bdw + cdw, what="dw", strict_atol=sdw)
+    assert_close(db, db_ref, atol=sdb + bdb, what="db", strict_atol=sdb)
+    return cen, cdx, cdw, sdw, sdb
 
 
 @pytest.mark.parametrize("name,gelu", [("lngelu_4x4096", True), ("lngelu_5x777", True),
@@ -222,17 +225,36 @@ def test_layer_norm_pilot_fallback_rows(oracle, m, n, gelu):
     _check_ln(xk, w, dyk, _ln_dev(xk, w, b, dyk, gelu), ref, gelu)
 
 
-def test_layer_norm_gelu_config2_rows(oracle):
-    """BASELINE config 2 shapes (cols 4096, eps 1e-5, seed 2) on 1024 of the
-    16384 rows (the composed oracle runs three times for the libm budget)."""
-    rng = np.random.default_rng(2)
-    m, n = 1024, 4096
-    x = rng.standard_normal((m, n), dtype=np.float32)
-    w = rng.uniform(0.5, 1.5, n).astype(np.float32)
-    b = (rng.standard_normal(n, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
-    dy = rng.standard_normal((m, n), dtype=np.float32)
-    ref = _oracle_ln(oracle, x, w, b, dy, True)
-    _check_ln(x, w, dy, _ln_dev(x, w, b, dy, True), ref, True)
+def test_layer_norm_gelu_config2_full_size(oracle):
+    """BASELINE config 2 at the size and on the arrays the benchmark times
+    (bench.config_inputs(2): x [16384, 4096], numpy PCG64(2)): every row and
+    column, so the VJP's persistent geometry (about 111 rows per CTA and its
+    dweight/dbias partials) is the benchmarked one.  Besides the pass/fail
+    check, the elements beyond the bare tolerance (rtol 1e-5, atol 1e-6;
+    1e-6 x Sigma|terms| for dweight/dbias) are attributed to the budget that
+    admits them: the reference's own summation order, then the libm (tanh)
+    ulps, then the centring term."""
+    import bench
+    from parity import reference_budget_parts, strict_breakdown
+    inp = bench.config_inputs(2)
+    x, w, b, dy = inp["x"], inp["w"], inp["b"], inp["dy"]
+    assert x.shape == (16384, 4096)
+
+    def run():
+        xt, wt, bt = (oracle.from_numpy(x, True), oracle.from_numpy(w, True),
+                      oracle.from_numpy(b, True))
+        y = oracle.gelu(oracle.layer_norm(xt, wt, bt, 1e-5))
+        y.backward(dy)
+        return y.numpy(), xt.grad.numpy(), wt.grad.numpy(), bt.grad.numpy()
+    base, sums, libm = reference_budget_parts(oracle, run, ("tanh",))
+    got = _ln_dev(x, w, b, dy, True)
+    budget = [a + c for a, c in zip(sums, libm)]
+    cen, cdx, cdw, sdw, sdb = _check_ln(x, w, dy, got, (base, budget), True)
+    for i, (name, strict, centre) in enumerate((("y", ATOL, cen), ("dx", ATOL, cdx),
+                                                ("dw", sdw, cdw), ("db", sdb, 0.0))):
+        strict_breakdown(got[i], base[i], RTOL, strict,
+                         [("summation_order", sums[i]), ("libm_tanh", libm[i]),
+                          ("centring", centre)], what=f"config 2 {name}")
 
 
 @pytest.mark.parametrize("n", [4096, 4094])

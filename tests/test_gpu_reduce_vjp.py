@@ -125,6 +125,6 @@ def test_unbroadcast_vs_oracle(oracle, gshape, target):
     last_axis_summed = len(target) == len(gshape) and target[-1] == 1 and gshape[-1] != 1
     if last_axis_summed:
         assert_close(got, want, rtol=RTOL, atol=ATOL * np.abs(g).sum() / max(want.size, 1),
-                     what="unbroadcast")
+                     what="unbroadcast", strict_atol=ATOL * np.abs(g).sum() / max(want.size, 1))
     else:
         assert_bitexact(got, want, "unbroadcast")

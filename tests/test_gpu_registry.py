@@ -303,7 +303,7 @@ def test_reduce_long_rows_both_geometries(oracle, shape):
             scale = {"sum": terms.sum(1), "mean": terms.mean(1),
                      "norm": np.sqrt((terms * terms).sum(1))}[kind]
             assert_close(got, want, rtol=RTOL, atol=ATOL * np.maximum(scale, 1.0) + budget,
-                         what=what)
+                         what=what, strict_atol=ATOL * np.maximum(scale, 1.0))
 
 
 def test_reduce_column_mode_is_the_reference_order(oracle):

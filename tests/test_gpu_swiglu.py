@@ -75,7 +75,8 @@ def test_swiglu_vs_oracle_layouts(oracle, m, n, transposed_gate):
     assert_bitexact(_host(mx), oracle.t_reduce("max", hh, 1, False), "row max")
     assert_bitexact(_host(am), oracle.t_reduce("argmax", hh, 1, False), "row argmax")
     want_s = oracle.t_reduce("sum", hh, 1, False)
-    assert_close(_host(s), want_s, atol=ATOL * np.abs(hh).sum(1) + 1e-6, what="row sum")
+    assert_close(_host(s), want_s, atol=ATOL * np.abs(hh).sum(1) + 1e-6, what="row sum",
+                 strict_atol=ATOL * np.abs(hh).sum(1) + 1e-6)
     want_sq = float((_host(dg).astype(np.float64) ** 2).sum() + (_host(du).astype(np.float64) ** 2).sum())
     assert abs(float(_host(sq)) - want_sq) <= 1e-12 * want_sq + 1e-30
 
@@ -130,7 +131,7 @@ def test_swiglu_gate_layouts_many_strips(oracle, layout, with_up):
     want_s = oracle.t_reduce("sum", hh, 1, False)
     assert np.isnan(_host(s)[~fin]).all()
     assert_close(_host(s)[fin], want_s[fin], atol=ATOL * np.abs(hh[fin]).sum(1) + 1e-6,
-                 what="row sum")
+                 what="row sum", strict_atol=ATOL * np.abs(hh[fin]).sum(1) + 1e-6)
     parts = [_host(res[0])] + ([_host(res[1])] if with_up else [])
     want_sq = sum(float(np.nansum(p.astype(np.float64) ** 2)) for p in parts)
     got_sq = float(_host(res[-1]))
@@ -157,16 +158,12 @@ def test_decoder_mlp_block_config5(oracle):
     import torch
     from oxitorch_b200 import functional as F
     from oxitorch_b200 import tensor_ops as T
+    import bench
     M, D, H = 65536, 4096, 11008
-    gen = torch.Generator(device="cuda")
-    gen.manual_seed(5)
-    x = torch.randn(M, D, device="cuda", generator=gen)
-    w = (torch.rand(1, D, device="cuda", generator=gen) + 0.5).broadcast_to(M, D)
-    gate_buf = torch.randn(H, M, device="cuda", generator=gen)
-    gate = gate_buf.t()                                    # strides [1, 65536]
-    up = torch.randn(M, H, device="cuda", generator=gen)
-    dy = torch.randn(M, D, device="cuda", generator=gen)
-    dh = torch.randn(M, H, device="cuda", generator=gen)
+    inp = {k: torch.from_numpy(v).cuda() for k, v in bench.config_inputs(5).items()}
+    x, up, dy, dh = inp["x"], inp["up"], inp["dy"], inp["dh"]
+    w = inp["w"].broadcast_to(M, D)
+    gate = inp["gate_buf"].t()                             # strides [1, 65536]
     assert gate.stride() == (1, M) and w.stride() == (0, 1)
 
     y, rstd = F.rms_norm_fwd(x, w, 1e-6)
@@ -198,7 +195,8 @@ def test_decoder_mlp_block_config5(oracle):
     assert_bitexact(_host(hm[rows]), oracle.t_reduce("max", hr, 1, False), "row max")
     assert_bitexact(_host(ha[rows]), oracle.t_reduce("argmax", hr, 1, False), "row argmax")
     assert_close(_host(hs[rows]), oracle.t_reduce("sum", hr, 1, False),
-                 atol=ATOL * np.abs(hr).sum(1) + 1e-6, what="row sum")
+                 atol=ATOL * np.abs(hr).sum(1) + 1e-6, what="row sum",
+                 strict_atol=ATOL * np.abs(hr).sum(1) + 1e-6)
 
     # dweight over all rows vs float64 (REF semantics: sum dy * x * inv)
     dw64 = torch.zeros(D, dtype=torch.float64, device="cuda")
@@ -210,7 +208,8 @@ def test_decoder_mlp_block_config5(oracle):
         dw64 += t.sum(0)
         absw += t.abs().sum(0)
     assert_close(_host(dw), dw64.cpu().numpy(), rtol=RTOL_BIG,
-                 atol=ATOL * np.maximum(absw.cpu().numpy(), 1.0), what="dweight vs f64")
+                 atol=ATOL * np.maximum(absw.cpu().numpy(), 1.0), what="dweight vs f64",
+                 strict_atol=ATOL * np.maximum(absw.cpu().numpy(), 1.0))
     # L2 over {dx, dg, du} vs float64 torch
     want = sum(float((t.double() ** 2).sum().item()) for t in (dx, dg, du)) ** 0.5
     assert abs(l2 - want) <= 1e-6 * want, (l2, want)
