@@ -227,6 +227,10 @@ oxc_status oxc_unary(int32_t op, const oxc_view* in, const oxc_view* out, void* 
  * rounded to f32 and broadcast either way. */
 oxc_status oxc_binary_scalar(int32_t op, const oxc_view* a, float scalar, int32_t scalar_first,
                              const oxc_view* out, void* stream);
+/* Tensor::contiguous (crates/oxi-tensor/src/lib.rs:220-240): copies a strided
+ * or broadcast view into the dense row-major `out` of the same shape, bit for
+ * bit, on the elementwise engine (transposed views through its tiled paths). */
+oxc_status oxc_contiguous(const oxc_view* in, const oxc_view* out, void* stream);
 
 /* ---- reductions ----------------------------------------------------------
  * Tensor::reduce(kind, dim, keepdim) (crates/oxi-tensor/src/lib.rs:519-576,
@@ -295,6 +299,17 @@ oxc_status oxc_softmax_fwd(const float* x, float* y, int64_t rows, int64_t cols,
                            void* stream);
 oxc_status oxc_softmax_bwd(const float* y, const float* dy, float* dx, int64_t rows, int64_t cols,
                            int32_t log, void* stream);
+/* F.softmax / F.log_softmax over any `dim` (negative counts from the end) of a
+ * view of any strides (python/oxitorch/nn/functional.py:211-222, whose max and
+ * sum are Tensor::reduce strips along dim, crates/oxi-tensor/src/lib.rs:
+ * 519-576).  y / dx are dense row-major with x's shape; dy is a view of that
+ * shape.  Same per-element arithmetic as oxc_softmax_fwd / _bwd, which these
+ * call for dense rows along the last dim.  A zero-length dim is
+ * InvalidArgument, as the reference's max over it. */
+oxc_status oxc_softmax_dim_fwd(const oxc_view* x, int64_t dim, int32_t log, float* y,
+                               void* stream);
+oxc_status oxc_softmax_dim_bwd(const float* y, const oxc_view* dy, int64_t dim, int32_t log,
+                               float* dx, void* stream);
 
 /* ---- cross-entropy, mean reduction: F.cross_entropy --------------------------
  * (functional.py:277-293).  logits [rows, cols]; targets int64 [rows] (negative
@@ -351,6 +366,34 @@ oxc_status oxc_embedding_bwd(const float* dout, const int64_t* ids, float* dtabl
                              int64_t vocab_total, int64_t vocab_offset, int64_t rows,
                              int64_t cols, int32_t* err_flag, void* workspace,
                              size_t workspace_bytes, void* stream);
+
+/* ---- index_select along any dim, and its VJP --------------------------------
+ * oxc_index_select replaces Tensor::index_select (crates/oxi-tensor/src/lib.rs:
+ * 665-703) for any dim and any strides of x: out (dense row-major, x's shape
+ * with dim -> n) = x[..., ids[k], ...].  ids int64 [n] on the device; negative
+ * ids count from the end; an id out of range gives zeros and is recorded in
+ * err_flag (int32[4]; oxc_check_error_flag then reports OutOfBounds with the
+ * reference's "index i out of range for dim d of size len").
+ * oxc_gather_dim0 replaces Tensor::gather_dim0 (lib.rs:857-886): index_select
+ * on dim 0, InvalidArgument for a 0-D x.
+ * oxc_index_select_bwd replaces scatter_index_select, the VJP of
+ * ops::index_select (crates/oxi-autograd/src/ops.rs:498-517, 741-769): gx
+ * (dense, `shape`, ndim dims) is zero except gx[o, ids[k], i] = sum of
+ * g[o, k, i] over the occurrences k of each index, in position order from 0.0.
+ * Slices of fewer than 128 floats (inner dims) are summed sequentially per
+ * element, bit-identical to the reference; wider slices use the embedding VJP's
+ * pipeline (bit-identical for indices occurring at most 128 times, else summed
+ * in 128-occurrence pieces). */
+oxc_status oxc_index_select(const oxc_view* x, int64_t dim, const int64_t* ids, int64_t n,
+                            float* out, int32_t* err_flag, void* stream);
+oxc_status oxc_gather_dim0(const oxc_view* x, const int64_t* ids, int64_t n, float* out,
+                           int32_t* err_flag, void* stream);
+size_t oxc_index_select_bwd_workspace_size(const int64_t* shape, int32_t ndim, int64_t dim,
+                                           int64_t n);
+oxc_status oxc_index_select_bwd(const float* g, const int64_t* ids, int64_t n,
+                                const int64_t* shape, int32_t ndim, int64_t dim, float* gx,
+                                int32_t* err_flag, void* workspace, size_t workspace_bytes,
+                                void* stream);
 
 /* ---- dim-0 scatter and its VJP: row selection ------------------------------
  * Replaces the host loops of Tensor::scatter_dim0 (crates/oxi-tensor/src/lib.rs:

@@ -88,6 +88,7 @@ SIGNATURES = {
     "oxc_cmp": (_I32, [_I32, _VP, _VP, _VP, _P]),
     "oxc_unary": (_I32, [_I32, _VP, _VP, _P]),
     "oxc_binary_scalar": (_I32, [_I32, _VP, _F32, _I32, _VP, _P]),
+    "oxc_contiguous": (_I32, [_VP, _VP, _P]),
     "oxc_reduce_workspace_size": (_SZ, [_I32, _VP, _I64]),
     "oxc_reduce": (_I32, [_I32, _VP, _I64, _I32, _VP, _P, _SZ, _P]),
     "oxc_reduce_bwd_workspace_size": (_SZ, [_I32, _VP, _I64]),
@@ -105,6 +106,8 @@ SIGNATURES = {
                                   _P, _SZ, _P]),
     "oxc_softmax_fwd": (_I32, [_P, _P, _I64, _I64, _I32, _P]),
     "oxc_softmax_bwd": (_I32, [_P, _P, _P, _I64, _I64, _I32, _P]),
+    "oxc_softmax_dim_fwd": (_I32, [_VP, _I64, _I32, _P, _P]),
+    "oxc_softmax_dim_bwd": (_I32, [_P, _VP, _I64, _I32, _P, _P]),
     "oxc_cross_entropy_fwd": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P]),
     "oxc_cross_entropy_bwd": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
     "oxc_swiglu_fwd": (_I32, [_VP, _VP, _P, _P, _P, _P, _P]),
@@ -113,6 +116,10 @@ SIGNATURES = {
     "oxc_embedding_fwd": (_I32, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P]),
     "oxc_embedding_bwd_workspace_size": (_SZ, [_I64, _I64, _I64]),
     "oxc_embedding_bwd": (_I32, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _SZ, _P]),
+    "oxc_index_select": (_I32, [_VP, _I64, _P, _I64, _P, _P, _P]),
+    "oxc_gather_dim0": (_I32, [_VP, _P, _I64, _P, _P, _P]),
+    "oxc_index_select_bwd_workspace_size": (_SZ, [_P, _I32, _I64, _I64]),
+    "oxc_index_select_bwd": (_I32, [_P, _P, _I64, _P, _I32, _I64, _P, _P, _P, _SZ, _P]),
     "oxc_select_rows": (_I32, [_P, _I64, _P, _I64, _P, _P, _I64, _P, _P]),
     "oxc_masked_select_workspace_size": (_SZ, [_I64]),
     "oxc_masked_select_count": (_I32, [_VP, _VP, _I32, _P, _SZ, _P]),

@@ -171,8 +171,9 @@ oxc_status oxc_check_error_flag(int32_t* flag_dev, void* stream, int64_t timeout
   const int32_t zero[4] = {0, 0, 0, 0};
   e = cudaMemcpy(flag_dev, zero, sizeof(zero), cudaMemcpyHostToDevice);
   if (e != cudaSuccess) return cuda_fail(e, "oxc_check_error_flag");
-  return fail(OXC_ERR_OUT_OF_BOUNDS, "out of bounds: index %lld out of range for dim 0 of size %d",
-              (long long)idx, host[3]);
+  // flag[0] is 1 + the indexed dim (kernels indexing dim 0 store 1)
+  return fail(OXC_ERR_OUT_OF_BOUNDS, "out of bounds: index %lld out of range for dim %d of size %d",
+              (long long)idx, host[0] - 1, host[3]);
 }
 
 oxc_status oxc_kernel_error(uint32_t* bits, int32_t clear) {

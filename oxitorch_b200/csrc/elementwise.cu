@@ -36,6 +36,10 @@ namespace oxc {
 
 enum ElemKind { EK_UNARY = 0, EK_BINARY = 1, EK_CMP = 2 };
 
+// Unary op id past the reference registry's 19: the identity, which turns the
+// elementwise engine into a strided copy (Tensor::contiguous).
+constexpr int kUnaryCopy = 19;
+
 __device__ __forceinline__ float rust_signum(float a) {
   return isnan(a) ? a : (signbit(a) ? -1.0f : 1.0f);
 }
@@ -60,7 +64,8 @@ __device__ __forceinline__ float unary_op(int op, float a) {
     case 15: return roundf(a);
     case 16: return rust_signum(a);
     case 17: return __fmul_rn(a, a);
-    default: return __fdiv_rn(1.0f, a);
+    case 18: return __fdiv_rn(1.0f, a);
+    default: return a;  // kUnaryCopy: the bits of a, for oxc_contiguous
   }
 }
 
@@ -115,7 +120,8 @@ __device__ __forceinline__ void apply_tile(int kind, int op, const float (&a)[N]
     switch (op) {
       OXC_U(0) OXC_U(1) OXC_U(2) OXC_U(3) OXC_U(4) OXC_U(5) OXC_U(6) OXC_U(7) OXC_U(8) OXC_U(9)
       OXC_U(10) OXC_U(11) OXC_U(12) OXC_U(13) OXC_U(14) OXC_U(15) OXC_U(16) OXC_U(17)
-      default: apply_n<EK_UNARY, 18, N>(a, b, r); return;
+      OXC_U(18)
+      default: apply_n<EK_UNARY, 19, N>(a, b, r); return;
     }
   } else if (kind == EK_BINARY) {
     switch (op) {
@@ -526,6 +532,11 @@ oxc_status oxc_unary(int32_t op, const oxc_view* in, const oxc_view* out, void* 
   if (op < 0 || op > 18) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: unknown unary op id %d", op);
   return run_elementwise(EK_UNARY, op, in, nullptr, nullptr, 0, out,
                          static_cast<cudaStream_t>(stream), "oxc_unary");
+}
+
+oxc_status oxc_contiguous(const oxc_view* in, const oxc_view* out, void* stream) {
+  return run_elementwise(EK_UNARY, kUnaryCopy, in, nullptr, nullptr, 0, out,
+                         static_cast<cudaStream_t>(stream), "oxc_contiguous");
 }
 
 oxc_status oxc_binary(int32_t op, const oxc_view* a, const oxc_view* b, const oxc_view* out,

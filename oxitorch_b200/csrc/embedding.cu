@@ -187,11 +187,14 @@ __device__ __forceinline__ void store_acc(float* dst, int cols, int c_base,
 // Block j of the sorted array: partial sums of the (at most two) pieces of
 // rows that occur more than kSplitP times.  Slot 2j: the row covering
 // position j*P (if split); slot 2j+1: a split row that starts inside block j.
+// With outer > 1 (index_select's VJP along an inner dim) the same segments
+// serve every outer index o (blockIdx.z): its dout rows start at o * n * cols,
+// its table rows at o * rows * cols and its pieces at o * 2 * nblocks * cols.
 template <int VW, int VPT, int MAXT>
 __global__ void __launch_bounds__(MAXT) emb_split_kernel(
     const float* __restrict__ dout, const int32_t* __restrict__ skeys,
     const int32_t* __restrict__ spos, const int32_t* __restrict__ offsets, int64_t n,
-    int64_t rows, int cols, float* __restrict__ parts) {
+    int64_t rows, int cols, float* __restrict__ parts, int64_t outer) {
   // emb_rows_kernel may start on the rows that need no pieces while this grid
   // runs (it was launched after the sort and offsets had completed)
   pdl_launch_dependents();
@@ -200,41 +203,49 @@ __global__ void __launch_bounds__(MAXT) emb_split_kernel(
   if (b0 >= n) return;
   const int64_t keys2[2] = {skeys[b0], skeys[b1 - 1]};
   const int nvec = cols / VW;
-  for (int side = 0; side < 2; ++side) {
-    const int64_t r = keys2[side];
-    if (r >= rows) continue;
-    if (side == 1 && r == keys2[0]) continue;
-    const int64_t s0 = offsets[r], s1 = offsets[r + 1];
-    if (s1 - s0 <= kSplitP) continue;
-    const int64_t p0 = max(s0, b0), p1 = min(s1, b1);
-    float* dst = parts + (2 * j + side) * (int64_t)cols;
-    for (int c_base = blockIdx.y * VPT * blockDim.x; c_base < nvec;
-         c_base += gridDim.y * VPT * blockDim.x) {
-      float acc[VPT][VW];
+  const int64_t nblocks = (n + kSplitP - 1) / kSplitP;
+  for (int64_t o = blockIdx.z; o < outer; o += gridDim.z) {
+    const float* od = dout + o * n * (int64_t)cols;
+    for (int side = 0; side < 2; ++side) {
+      const int64_t r = keys2[side];
+      if (r >= rows) continue;
+      if (side == 1 && r == keys2[0]) continue;
+      const int64_t s0 = offsets[r], s1 = offsets[r + 1];
+      if (s1 - s0 <= kSplitP) continue;
+      const int64_t p0 = max(s0, b0), p1 = min(s1, b1);
+      float* dst = parts + (o * 2 * nblocks + 2 * j + side) * (int64_t)cols;
+      for (int c_base = blockIdx.y * VPT * blockDim.x; c_base < nvec;
+           c_base += gridDim.y * VPT * blockDim.x) {
+        float acc[VPT][VW];
 #pragma unroll
-      for (int i = 0; i < VPT; ++i)
+        for (int i = 0; i < VPT; ++i)
 #pragma unroll
-        for (int e = 0; e < VW; ++e) acc[i][e] = 0.0f;
-      sum_positions<VW, VPT>(dout, spos, p0, p1, cols, c_base, acc);
-      store_acc<VW, VPT>(dst, cols, c_base, acc, false);
+          for (int e = 0; e < VW; ++e) acc[i][e] = 0.0f;
+        sum_positions<VW, VPT>(od, spos, p0, p1, cols, c_base, acc);
+        store_acc<VW, VPT>(dst, cols, c_base, acc, false);
+      }
     }
   }
 }
 
 template <int VW, int VPT, int MAXT>
 __global__ void __launch_bounds__(MAXT) emb_rows_kernel(
-    const float* __restrict__ dout, const int32_t* __restrict__ spos,
-    const int32_t* __restrict__ offsets, const float* __restrict__ parts, int64_t rows, int cols,
-    float* __restrict__ dtable) {
+    const float* __restrict__ dout_all, const int32_t* __restrict__ spos,
+    const int32_t* __restrict__ offsets, const float* __restrict__ parts_all, int64_t rows,
+    int cols, float* __restrict__ dtable, int64_t n, int64_t outer) {
   // Launched as a programmatic dependent of emb_split_kernel: rows with at
   // most kSplitP occurrences read only the sort's output and run while the
   // split grid is still working; rows made of pieces wait for it (pdl_wait)
   // before reading `parts`, and every CTA waits once more before it exits,
   // so this grid never completes ahead of the split grid.
   const int nvec = cols / VW;
+  const int64_t nblocks = (n + kSplitP - 1) / kSplitP;
+  for (int64_t o = blockIdx.z; o < outer; o += gridDim.z)
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float* dout = dout_all + o * n * (int64_t)cols;
+    const float* parts = parts_all + o * 2 * nblocks * (int64_t)cols;
     const int64_t s0 = offsets[r], s1 = offsets[r + 1];
-    float* dst = dtable + r * (int64_t)cols;
+    float* dst = dtable + (o * rows + r) * (int64_t)cols;
     for (int c_base = blockIdx.y * VPT * blockDim.x; c_base < nvec;
          c_base += gridDim.y * VPT * blockDim.x) {
       float acc[VPT][VW];
@@ -288,6 +299,105 @@ __global__ void __launch_bounds__(MAXT) emb_rows_kernel(
   pdl_wait();
 }
 
+// ---- index_select along any dim (Tensor::index_select, lib.rs:665-703) ----------
+
+// Records the first bad id of an index_select along `dim`: flag[0] = 1 + dim.
+__device__ __forceinline__ void isel_record_bad(int32_t* flag, int64_t value, int64_t size,
+                                                int dim) {
+  if (flag && atomicCAS(flag, 0, 1 + dim) == 0) {
+    flag[1] = (int32_t)(uint32_t)((uint64_t)value & 0xffffffffu);
+    flag[2] = (int32_t)(uint32_t)((uint64_t)value >> 32);
+    flag[3] = (int32_t)size;
+  }
+}
+
+// Resolved index in [0, len) (negative ids count from the end), or -1.
+__device__ __forceinline__ int64_t isel_resolve(int64_t id, int64_t len) {
+  const int64_t r = id < 0 ? id + len : id;
+  return (r >= 0 && r < len) ? r : -1;
+}
+
+// Contiguous x viewed as [outer, len, inner] with inner >= 32: one CTA per
+// output slice (o, k), which copies x[o, ids[k], :] (128-bit when VW = 4).
+template <int VW>
+__global__ void __launch_bounds__(256) isel_rows_kernel(
+    const float* __restrict__ x, const int64_t* __restrict__ ids, float* __restrict__ out,
+    int64_t outer, int64_t len, int64_t n, int64_t inner, int dim, int32_t* err) {
+  const int64_t nvec = inner / VW, slices = outer * n;
+  for (int64_t row = blockIdx.x; row < slices; row += gridDim.x) {
+    const int64_t o = row / n, k = row - o * n;
+    const int64_t r = isel_resolve(ids[k], len);
+    if (r < 0 && threadIdx.x == 0) isel_record_bad(err, ids[k], len, dim);
+    float* dst = out + row * inner;
+    if constexpr (VW == 4) {
+      float4* d4 = reinterpret_cast<float4*>(dst);
+      const float4* s4 = reinterpret_cast<const float4*>(x + (o * len + (r < 0 ? 0 : r)) * inner);
+      for (int64_t v = threadIdx.x; v < nvec; v += blockDim.x)
+        st_stream(d4 + v, r < 0 ? make_float4(0, 0, 0, 0) : ld_keep(s4 + v));
+    } else {
+      const float* src = x + (o * len + (r < 0 ? 0 : r)) * inner;
+      for (int64_t c = threadIdx.x; c < inner; c += blockDim.x)
+        st_stream(dst + c, r < 0 ? 0.0f : ld_keep(src + c));
+    }
+  }
+}
+
+// Any strides: one thread per output element.  g.n is the output shape
+// (n[dim] = number of ids), g.st the strides of x.
+struct ISelGrid {
+  int nd, dim;
+  int64_t len;
+  int64_t n[OXC_MAX_DIMS];
+  int64_t st[OXC_MAX_DIMS];
+};
+
+__global__ void __launch_bounds__(256) isel_elem_kernel(const float* __restrict__ x,
+                                                        const int64_t* __restrict__ ids,
+                                                        ISelGrid g, float* __restrict__ out,
+                                                        int64_t total, int32_t* err) {
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    int64_t rem = e, off = 0;
+    bool bad = false;
+    for (int d = g.nd - 1; d >= 0; --d) {
+      const int64_t q = rem / g.n[d];
+      int64_t idx = rem - q * g.n[d];
+      rem = q;
+      if (d == g.dim) {
+        const int64_t r = isel_resolve(ids[idx], g.len);
+        if (r < 0) {
+          isel_record_bad(err, ids[idx], g.len, g.dim);
+          bad = true;
+        }
+        idx = r < 0 ? 0 : r;
+      }
+      off += idx * g.st[d];
+    }
+    out[e] = bad ? 0.0f : __ldg(x + off);
+  }
+}
+
+// The VJP for slices narrower than a float4 chunk row (inner < 128): one
+// thread per gx element (o, r, i) sums g[o, k, i] over the occurrences k of
+// row r in position order, from 0.0 -- the reference's accumulation order
+// (crates/oxi-autograd/src/ops.rs:756-763), so every element is bit-identical.
+__global__ void __launch_bounds__(256) isel_bwd_narrow_kernel(
+    const float* __restrict__ g, const int32_t* __restrict__ spos,
+    const int32_t* __restrict__ offsets, int64_t outer, int64_t len, int64_t n, int64_t inner,
+    float* __restrict__ gx) {
+  const int64_t total = outer * len * inner;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = e % inner, t = e / inner;
+    const int64_t r = t % len, o = t / len;
+    const int64_t s0 = offsets[r], s1 = offsets[r + 1];
+    const float* go = g + o * n * inner + i;
+    float acc = 0.0f;
+    for (int64_t p = s0; p < s1; ++p) acc = __fadd_rn(acc, __ldg(go + (int64_t)spos[p] * inner));
+    gx[e] = acc;
+  }
+}
+
 struct EmbLayout {
   size_t keys_in, vals_in, keys_out, vals_out, offsets, parts, cub, total;
   size_t cub_bytes;
@@ -296,7 +406,8 @@ struct EmbLayout {
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-static oxc_status emb_layout(int64_t n, int64_t rows, int64_t cols, EmbLayout* L) {
+static oxc_status emb_layout(int64_t n, int64_t rows, int64_t cols, EmbLayout* L,
+                             int64_t outer = 1) {
   int end_bit = 1;
   while (end_bit < 31 && ((int64_t)1 << end_bit) <= rows) ++end_bit;  // keys in [0, rows]
   size_t cub_bytes = 0;
@@ -311,7 +422,7 @@ static oxc_status emb_layout(int64_t n, int64_t rows, int64_t cols, EmbLayout* L
   L->keys_out = off; off += align256((size_t)n * 4);
   L->vals_out = off; off += align256((size_t)n * 4);
   L->offsets = off; off += align256((size_t)(rows + 1) * 4);
-  L->parts = off; off += align256((size_t)2 * nblocks * cols * 4);
+  L->parts = off; off += align256((size_t)2 * nblocks * cols * 4 * (size_t)outer);
   L->cub = off; off += align256(cub_bytes);
   L->total = off;
   L->cub_bytes = cub_bytes;
@@ -425,16 +536,195 @@ oxc_status oxc_embedding_bwd(const float* dout, const int64_t* ids, float* dtabl
   const dim3 gsplit((unsigned)nblocks, (unsigned)chunks), grow(grows, (unsigned)chunks);
   if (v4) {
     emb_split_kernel<4, 1, kEmbChunkThreads><<<gsplit, block, 0, s>>>(
-        dout, keys_out, vals_out, offsets, n, rows, (int)cols, parts);
+        dout, keys_out, vals_out, offsets, n, rows, (int)cols, parts, (int64_t)1);
     launch_dependent(emb_rows_kernel<4, 1, kEmbChunkThreads>, grow, block, s, dout, vals_out,
-                     offsets, (const float*)parts, rows, (int)cols, dtable);
+                     offsets, (const float*)parts, rows, (int)cols, dtable, n, (int64_t)1);
   } else {
     emb_split_kernel<1, 4, kEmbChunkThreads><<<gsplit, block, 0, s>>>(
-        dout, keys_out, vals_out, offsets, n, rows, (int)cols, parts);
+        dout, keys_out, vals_out, offsets, n, rows, (int)cols, parts, (int64_t)1);
     launch_dependent(emb_rows_kernel<1, 4, kEmbChunkThreads>, grow, block, s, dout, vals_out,
-                     offsets, (const float*)parts, rows, (int)cols, dtable);
+                     offsets, (const float*)parts, rows, (int)cols, dtable, n, (int64_t)1);
   }
   return check_launch("oxc_embedding_bwd");
+}
+
+oxc_status oxc_index_select(const oxc_view* x, int64_t dim, const int64_t* ids, int64_t n,
+                            float* out, int32_t* err_flag, void* stream) {
+  const char* fn = "index_select";
+  if (!x) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: null view", fn);
+  if (x->ndim < 0 || x->ndim > OXC_MAX_DIMS)
+    return fail(OXC_ERR_NOT_IMPLEMENTED, "not implemented: %s: rank %d > %d", fn, x->ndim,
+                OXC_MAX_DIMS);
+  if (x->ndim == 0)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: dim %lld out of range for 0-D tensor",
+                (long long)dim);
+  const int nd = x->ndim;
+  const int64_t d = dim < 0 ? dim + nd : dim;
+  if (d < 0 || d >= nd)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: dim %lld out of range for %d-D tensor",
+                (long long)dim, nd);
+  if (n < 0) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: negative id count", fn);
+  int64_t total = 1, outer = 1, inner = 1;
+  for (int i = 0; i < nd; ++i) {
+    if (x->shape[i] < 0) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: negative dim", fn);
+    total *= i == d ? n : x->shape[i];
+    if (i < d) outer *= x->shape[i];
+    if (i > d) inner *= x->shape[i];
+  }
+  if (total == 0) return OXC_OK;
+  const int64_t len = x->shape[d];
+  if (!x->data || !ids || !out)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: null pointer", fn);
+  bool contiguous = true;
+  for (int64_t i = nd - 1, expect = 1; i >= 0; --i) {
+    if (x->shape[i] != 1 && x->strides[i] != expect) contiguous = false;
+    expect *= x->shape[i];
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t cap = (int64_t)sm_count() * 16;
+  if (contiguous && inner >= 32) {
+    const bool v4 = inner % 4 == 0 && aligned16(x->data) && aligned16(out);
+    const int64_t per = v4 ? inner / 4 : inner;
+    const int block = (int)std::min<int64_t>(256, std::max<int64_t>(32, ((per + 31) / 32) * 32));
+    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(outer * n, cap));
+    if (v4)
+      isel_rows_kernel<4><<<grid, block, 0, s>>>(x->data, ids, out, outer, len, n, inner, (int)d,
+                                                 err_flag);
+    else
+      isel_rows_kernel<1><<<grid, block, 0, s>>>(x->data, ids, out, outer, len, n, inner, (int)d,
+                                                 err_flag);
+    return check_launch("oxc_index_select");
+  }
+  ISelGrid g;
+  g.nd = nd;
+  g.dim = (int)d;
+  g.len = len;
+  for (int i = 0; i < nd; ++i) {
+    g.n[i] = i == d ? n : x->shape[i];
+    g.st[i] = x->strides[i];
+  }
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, cap * 4));
+  isel_elem_kernel<<<grid, 256, 0, s>>>(x->data, ids, g, out, total, err_flag);
+  return check_launch("oxc_index_select");
+}
+
+oxc_status oxc_gather_dim0(const oxc_view* x, const int64_t* ids, int64_t n, float* out,
+                           int32_t* err_flag, void* stream) {
+  if (x && x->ndim == 0)
+    return fail(OXC_ERR_INVALID_ARGUMENT,
+                "invalid argument: gather_dim0 requires at least a 1-D tensor");
+  return oxc_index_select(x, 0, ids, n, out, err_flag, stream);
+}
+
+// [outer, len, inner] of `shape` around `dim`, or an error.
+static oxc_status isel_geometry(const int64_t* shape, int32_t ndim, int64_t dim, int64_t* outer,
+                                int64_t* len, int64_t* inner, int64_t* d_out) {
+  if (!shape || ndim <= 0 || ndim > OXC_MAX_DIMS)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: index_select backward: rank %d",
+                (int)ndim);
+  const int64_t d = dim < 0 ? dim + ndim : dim;
+  if (d < 0 || d >= ndim)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: dim %lld out of range for %d-D tensor",
+                (long long)dim, (int)ndim);
+  *outer = 1;
+  *inner = 1;
+  for (int i = 0; i < ndim; ++i) {
+    if (shape[i] < 0)
+      return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: index_select backward: negative dim");
+    if (i < d) *outer *= shape[i];
+    if (i > d) *inner *= shape[i];
+  }
+  *len = shape[d];
+  *d_out = d;
+  return OXC_OK;
+}
+
+size_t oxc_index_select_bwd_workspace_size(const int64_t* shape, int32_t ndim, int64_t dim,
+                                           int64_t n) {
+  int64_t outer, len, inner, d;
+  if (isel_geometry(shape, ndim, dim, &outer, &len, &inner, &d) != OXC_OK) return 0;
+  if (n <= 0 || len <= 0 || inner <= 0 || outer <= 0) return 0;
+  EmbLayout L;
+  if (emb_layout(n, len, inner, &L, inner >= 128 ? outer : 0) != OXC_OK) return 0;
+  return L.total;
+}
+
+oxc_status oxc_index_select_bwd(const float* g, const int64_t* ids, int64_t n,
+                                const int64_t* shape, int32_t ndim, int64_t dim, float* gx,
+                                int32_t* err_flag, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+  int64_t outer, len, inner, d;
+  oxc_status st = isel_geometry(shape, ndim, dim, &outer, &len, &inner, &d);
+  if (st) return st;
+  if (n < 0) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: index_select backward: negative id count");
+  if (n > 0x7fffffff || len >= 0x7fffffff || inner > 0x7fffffff)
+    return fail(OXC_ERR_NOT_IMPLEMENTED, "not implemented: index_select backward: sizes beyond 2^31");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t total = outer * len * inner;
+  if (total == 0) return OXC_OK;
+  if (!gx) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: index_select backward: null pointer");
+  if (n == 0) {
+    cudaError_t e = cudaMemsetAsync(gx, 0, (size_t)total * sizeof(float), s);
+    return e == cudaSuccess ? OXC_OK : cuda_fail(e, "oxc_index_select_bwd");
+  }
+  if (!g || !ids)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: index_select backward: null pointer");
+  const bool wide = inner >= 128;
+  EmbLayout L;
+  st = emb_layout(n, len, inner, &L, wide ? outer : 0);
+  if (st) return st;
+  if (!workspace || workspace_bytes < L.total)
+    return fail(OXC_ERR_INVALID_ARGUMENT,
+                "invalid argument: index_select backward needs a %zu-byte workspace, got %zu",
+                L.total, workspace_bytes);
+  char* ws = static_cast<char*>(workspace);
+  int32_t* keys_in = reinterpret_cast<int32_t*>(ws + L.keys_in);
+  int32_t* vals_in = reinterpret_cast<int32_t*>(ws + L.vals_in);
+  int32_t* keys_out = reinterpret_cast<int32_t*>(ws + L.keys_out);
+  int32_t* vals_out = reinterpret_cast<int32_t*>(ws + L.vals_out);
+  int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
+  float* parts = reinterpret_cast<float*>(ws + L.parts);
+  const unsigned g1 = (unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)sm_count() * 8);
+  emb_prepare_kernel<<<g1, 256, 0, s>>>(ids, n, len, 0, len, keys_in, vals_in, err_flag);
+  st = check_launch("oxc_index_select_bwd (prepare)");
+  if (st) return st;
+  size_t cub_bytes = L.cub_bytes;
+  cudaError_t e = cub::DeviceRadixSort::SortPairs(ws + L.cub, cub_bytes, keys_in, keys_out,
+                                                  vals_in, vals_out, (int)n, 0, L.end_bit, s);
+  if (e != cudaSuccess) return cuda_fail(e, "oxc_index_select_bwd (sort)");
+  const unsigned g2 = (unsigned)std::min<int64_t>((n + 1 + 255) / 256, (int64_t)sm_count() * 8);
+  emb_offsets_kernel<<<g2, 256, 0, s>>>(keys_out, n, len, offsets);
+  st = check_launch("oxc_index_select_bwd (offsets)");
+  if (st) return st;
+  if (!wide) {
+    const unsigned grid =
+        (unsigned)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, (int64_t)sm_count() * 32));
+    isel_bwd_narrow_kernel<<<grid, 256, 0, s>>>(g, vals_out, offsets, outer, len, n, inner, gx);
+    return check_launch("oxc_index_select_bwd");
+  }
+  // wide slices: the embedding VJP's kernels, one z-slice per outer index
+  const bool v4 = inner % 4 == 0 && aligned16(g) && aligned16(gx);
+  const int64_t nblocks = (n + kSplitP - 1) / kSplitP;
+  const unsigned zs = (unsigned)std::min<int64_t>(outer, 65535);
+  const unsigned grows = (unsigned)std::min<int64_t>(len, std::max<int64_t>(1, (int64_t)sm_count() * 32 / zs));
+  const int vpt = v4 ? 1 : 4, vw = v4 ? 4 : 1;
+  const int64_t per_thread = (int64_t)vpt * vw;
+  const int block = (int)std::min<int64_t>(
+      kEmbChunkThreads, std::max<int64_t>(32, ((inner / per_thread + 31) / 32) * 32));
+  const int64_t chunks = std::min<int64_t>(65535, (inner + block * per_thread - 1) / (block * per_thread));
+  const dim3 gsplit((unsigned)nblocks, (unsigned)chunks, zs), grow(grows, (unsigned)chunks, zs);
+  if (v4) {
+    emb_split_kernel<4, 1, kEmbChunkThreads><<<gsplit, block, 0, s>>>(
+        g, keys_out, vals_out, offsets, n, len, (int)inner, parts, outer);
+    launch_dependent(emb_rows_kernel<4, 1, kEmbChunkThreads>, grow, block, s, g, vals_out,
+                     offsets, (const float*)parts, len, (int)inner, gx, n, outer);
+  } else {
+    emb_split_kernel<1, 4, kEmbChunkThreads><<<gsplit, block, 0, s>>>(
+        g, keys_out, vals_out, offsets, n, len, (int)inner, parts, outer);
+    launch_dependent(emb_rows_kernel<1, 4, kEmbChunkThreads>, grow, block, s, g, vals_out,
+                     offsets, (const float*)parts, len, (int)inner, gx, n, outer);
+  }
+  return check_launch("oxc_index_select_bwd");
 }
 
 }  // extern "C"

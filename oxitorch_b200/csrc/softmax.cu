@@ -428,6 +428,222 @@ __global__ void __launch_bounds__(512) ce_bwd_rows_kernel(const float* __restric
   }
 }
 
+// ---- softmax / log_softmax over any dim of a strided view ---------------------
+//
+// The reference composes both over any `dim` (functional.py:211-222): max and
+// sum along `dim` are Tensor::reduce strips (lib.rs:519-576), so every
+// logical row -- one index of every other dim -- is reduced on its own.  Here
+// a logical row r (r in [0, outer * inner), other dims in logical order) has
+// its elements at x + row_off(r) + j * xs, j < len; the output y is dense in
+// x's logical shape, so row r's element j lands at
+// (r / inner) * len * inner + r % inner + j * inner.
+//   inner == 1 (the reduced dim is the last logical dim, x not dense):
+//     softmax_dim_rows_*: one CTA per row, as the contiguous row kernels;
+//   inner > 1: softmax_dim_cols_*: a CTA takes 32 consecutive logical rows
+//     (one per lane, so loads and stores of a warp are consecutive in memory
+//     whenever the innermost other dim is) and its warps split `len`; the
+//     per-warp (max, sum) partials are merged in warp order.
+struct DimRows {
+  int nd;                      // the other dims, collapsed, outermost first
+  int64_t n[OXC_MAX_DIMS];     // their sizes
+  int64_t st[OXC_MAX_DIMS];    // their strides in x (forward) or dy (backward)
+  int64_t len, xs;             // length of the reduced dim, its stride in x / dy
+  int64_t inner;               // product of the logical dims after the reduced one
+};
+
+__device__ __forceinline__ int64_t dim_row_off(const DimRows& g, int64_t r) {
+  int64_t off = 0;
+  for (int d = g.nd - 1; d >= 0; --d) {
+    const int64_t q = r / g.n[d];
+    off += (r - q * g.n[d]) * g.st[d];
+    r = q;
+  }
+  return off;
+}
+
+__device__ __forceinline__ int64_t dim_out_off(const DimRows& g, int64_t r) {
+  const int64_t o = r / g.inner;
+  return o * g.len * g.inner + (r - o * g.inner);
+}
+
+template <bool LOG>
+__global__ void __launch_bounds__(512) softmax_dim_rows_fwd_kernel(const float* __restrict__ x,
+                                                                   float* __restrict__ y,
+                                                                   DimRows g, int64_t rows) {
+  __shared__ float scratch[66];
+  const int64_t len = g.len, xs = g.xs;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float* xr = x + dim_row_off(g, row);
+    float* yr = y + row * len;
+    MaxSum a{-INFINITY, 0.0f};
+    int64_t c = threadIdx.x;
+    for (; c + 3 * (int64_t)blockDim.x < len; c += 4 * blockDim.x) {
+      float q[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) q[u] = ld_keep(xr + (c + u * blockDim.x) * xs);
+      ms_fold<4>(a, q);
+    }
+    for (; c < len; c += blockDim.x) {
+      const float q[1] = {ld_keep(xr + c * xs)};
+      ms_fold<1>(a, q);
+    }
+    MaxSum st = block_maxsum(a, scratch);
+    if (st.m == -INFINITY) st.s = NAN;
+    const float logs = LOG ? logf(st.s) : 0.0f;
+    const float inv = LOG ? 0.0f : __frcp_rn(st.s);
+    for (c = threadIdx.x; c < len; c += blockDim.x) {
+      const float q = ld_keep(xr + c * xs);
+      st_stream(yr + c, LOG ? (q - st.m) - logs : expf(q - st.m) * inv);
+    }
+  }
+}
+
+template <bool LOG>
+__global__ void __launch_bounds__(512) softmax_dim_rows_bwd_kernel(const float* __restrict__ y,
+                                                                   const float* __restrict__ dy,
+                                                                   float* __restrict__ dx,
+                                                                   DimRows g, int64_t rows) {
+  __shared__ float scratch[33];
+  const int64_t len = g.len, gs = g.xs;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float* yr = y + row * len;
+    const float* gr = dy + dim_row_off(g, row);
+    float* dr = dx + row * len;
+    float acc = 0.0f;
+    for (int64_t c = threadIdx.x; c < len; c += blockDim.x)
+      acc += LOG ? ld_keep(gr + c * gs) : ld_keep(gr + c * gs) * ld_keep(yr + c);
+    const float sum = block_sum(acc, scratch);
+    for (int64_t c = threadIdx.x; c < len; c += blockDim.x) {
+      const float gv = ld_keep(gr + c * gs), q = ld_keep(yr + c);
+      st_stream(dr + c, LOG ? gv - expf(q) * sum : q * (gv - sum));
+    }
+  }
+}
+
+constexpr int kDimMaxWarps = 32;
+
+template <bool LOG>
+__global__ void __launch_bounds__(1024) softmax_dim_cols_fwd_kernel(const float* __restrict__ x,
+                                                                    float* __restrict__ y,
+                                                                    DimRows g, int64_t rows) {
+  __shared__ float pm[kDimMaxWarps][33], ps[kDimMaxWarps][33];
+  const int lane = threadIdx.x, w = threadIdx.y, nw = blockDim.y;
+  const int64_t len = g.len, xs = g.xs, inner = g.inner;
+  for (int64_t r0 = (int64_t)blockIdx.x * 32; r0 < rows; r0 += (int64_t)gridDim.x * 32) {
+    const int64_t r = r0 + lane;
+    const bool live = r < rows;
+    const float* xr = x + (live ? dim_row_off(g, r) : 0);
+    MaxSum a{-INFINITY, 0.0f};
+    if (live) {
+      int64_t j = w;
+      for (; j + 3 * nw < len; j += 4 * nw) {
+        float q[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) q[u] = ld_keep(xr + (j + u * nw) * xs);
+        ms_fold<4>(a, q);
+      }
+      for (; j < len; j += nw) {
+        const float q[1] = {ld_keep(xr + j * xs)};
+        ms_fold<1>(a, q);
+      }
+    }
+    pm[w][lane] = a.m;
+    ps[w][lane] = a.s;
+    __syncthreads();
+    MaxSum t{-INFINITY, 0.0f};
+    for (int k = 0; k < nw; ++k) t = ms_merge(t, MaxSum{pm[k][lane], ps[k][lane]});
+    if (t.m == -INFINITY) t.s = NAN;
+    __syncthreads();  // the partials are read; the next tile may overwrite them
+    if (!live) continue;
+    const float logs = LOG ? logf(t.s) : 0.0f;
+    const float inv = LOG ? 0.0f : __frcp_rn(t.s);
+    float* yr = y + dim_out_off(g, r);
+    for (int64_t j = w; j < len; j += nw) {
+      const float q = ld_keep(xr + j * xs);
+      st_stream(yr + j * inner, LOG ? (q - t.m) - logs : expf(q - t.m) * inv);
+    }
+  }
+}
+
+template <bool LOG>
+__global__ void __launch_bounds__(1024) softmax_dim_cols_bwd_kernel(const float* __restrict__ y,
+                                                                    const float* __restrict__ dy,
+                                                                    float* __restrict__ dx,
+                                                                    DimRows g, int64_t rows) {
+  __shared__ float ps[kDimMaxWarps][33];
+  const int lane = threadIdx.x, w = threadIdx.y, nw = blockDim.y;
+  const int64_t len = g.len, gs = g.xs, inner = g.inner;
+  for (int64_t r0 = (int64_t)blockIdx.x * 32; r0 < rows; r0 += (int64_t)gridDim.x * 32) {
+    const int64_t r = r0 + lane;
+    const bool live = r < rows;
+    const float* gr = dy + (live ? dim_row_off(g, r) : 0);
+    const int64_t oo = live ? dim_out_off(g, r) : 0;
+    const float* yr = y + oo;
+    float acc = 0.0f;
+    if (live)
+      for (int64_t j = w; j < len; j += nw)
+        acc += LOG ? ld_keep(gr + j * gs) : ld_keep(gr + j * gs) * ld_keep(yr + j * inner);
+    ps[w][lane] = acc;
+    __syncthreads();
+    float sum = 0.0f;
+    for (int k = 0; k < nw; ++k) sum += ps[k][lane];
+    __syncthreads();
+    if (!live) continue;
+    float* dr = dx + oo;
+    for (int64_t j = w; j < len; j += nw) {
+      const float gv = ld_keep(gr + j * gs), q = ld_keep(yr + j * inner);
+      st_stream(dr + j * inner, LOG ? gv - expf(q) * sum : q * (gv - sum));
+    }
+  }
+}
+
+// Fills g for a softmax over `dim` of `v` (shape/strides), the other dims
+// collapsed where their strides chain.  Returns the logical row count.
+static int64_t dim_rows(const oxc_view* v, int d, DimRows* g) {
+  int64_t n[OXC_MAX_DIMS], st[OXC_MAX_DIMS];
+  int k = 0;
+  int64_t rows = 1;
+  g->inner = 1;
+  for (int i = 0; i < v->ndim; ++i) {
+    if (i == d) continue;
+    rows *= v->shape[i];
+    if (i > d) g->inner *= v->shape[i];
+    if (v->shape[i] == 1) continue;
+    if (k > 0 && st[k - 1] == v->strides[i] * v->shape[i]) {
+      n[k - 1] *= v->shape[i];
+      st[k - 1] = v->strides[i];
+      continue;
+    }
+    n[k] = v->shape[i];
+    st[k] = v->strides[i];
+    ++k;
+  }
+  if (k == 0) {  // a single logical row
+    n[0] = 1;
+    st[0] = 0;
+    k = 1;
+  }
+  g->nd = k;
+  for (int i = 0; i < k; ++i) {
+    g->n[i] = n[i];
+    g->st[i] = st[i];
+  }
+  g->len = v->shape[d];
+  g->xs = v->strides[d];
+  return rows;
+}
+
+static void dim_cols_launch_geometry(int64_t rows, int64_t len, dim3* grid, dim3* block) {
+  const int64_t tiles = (rows + 31) / 32;
+  const int64_t want_warps = (int64_t)sm_count() * 48;  // warps to keep HBM busy
+  int64_t nw = (want_warps + tiles - 1) / tiles;
+  nw = std::max<int64_t>(4, std::min<int64_t>(nw, kDimMaxWarps));
+  nw = std::max<int64_t>(1, std::min<int64_t>(nw, len));
+  *block = dim3(32, (unsigned)nw);
+  const int64_t per_sm = std::max<int64_t>(1, 64 / nw);
+  *grid = dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, (int64_t)sm_count() * per_sm)));
+}
+
 static unsigned row_grid(int64_t rows) {
   const int64_t cap = (int64_t)sm_count() * 64;
   return (unsigned)(rows < cap ? rows : cap);
@@ -488,6 +704,83 @@ oxc_status oxc_softmax_bwd(const float* y, const float* dy, float* dx, int64_t r
     else softmax_bwd_kernel<1, false><<<grid, block, 0, s>>>(y, dy, dx, rows, (int)cols);
   }
   return check_launch("oxc_softmax_bwd");
+}
+
+static oxc_status dim_check(const char* fn, const oxc_view* v, int64_t dim, int* d) {
+  if (!v) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: null view", fn);
+  if (v->ndim < 0 || v->ndim > OXC_MAX_DIMS)
+    return fail(OXC_ERR_NOT_IMPLEMENTED, "not implemented: %s: rank %d > %d", fn, v->ndim,
+                OXC_MAX_DIMS);
+  if (v->ndim == 0)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: dim %lld out of range for 0-D tensor",
+                (long long)dim);
+  const int64_t dd = dim < 0 ? dim + v->ndim : dim;
+  if (dd < 0 || dd >= v->ndim)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: dim %lld out of range for %d-D tensor",
+                (long long)dim, v->ndim);
+  for (int i = 0; i < v->ndim; ++i)
+    if (v->shape[i] < 0) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: negative dim", fn);
+  if (v->shape[dd] == 0)
+    return fail(OXC_ERR_INVALID_ARGUMENT,
+                "invalid argument: cannot compute max/min over a zero-length dim");
+  *d = (int)dd;
+  return OXC_OK;
+}
+
+oxc_status oxc_softmax_dim_fwd(const oxc_view* x, int64_t dim, int32_t log, float* y,
+                               void* stream) {
+  const char* fn = log ? "log_softmax" : "softmax";
+  int d = 0;
+  oxc_status st = dim_check(fn, x, dim, &d);
+  if (st) return st;
+  DimRows g;
+  const int64_t rows = dim_rows(x, d, &g);
+  if (rows == 0) return OXC_OK;
+  if (!x->data || !y) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: null pointer", fn);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // dense rows along the last dim: the contiguous row kernels
+  if (g.inner == 1 && g.xs == 1 && g.nd == 1 && (g.st[0] == g.len || rows == 1))
+    return oxc_softmax_fwd(x->data, y, rows, g.len, log, stream);
+  if (g.inner == 1) {
+    const unsigned grid = row_grid(rows);
+    const int block = row_block(g.len);
+    if (log) softmax_dim_rows_fwd_kernel<true><<<grid, block, 0, s>>>(x->data, y, g, rows);
+    else softmax_dim_rows_fwd_kernel<false><<<grid, block, 0, s>>>(x->data, y, g, rows);
+    return check_launch("oxc_softmax_dim_fwd");
+  }
+  dim3 grid, block;
+  dim_cols_launch_geometry(rows, g.len, &grid, &block);
+  if (log) softmax_dim_cols_fwd_kernel<true><<<grid, block, 0, s>>>(x->data, y, g, rows);
+  else softmax_dim_cols_fwd_kernel<false><<<grid, block, 0, s>>>(x->data, y, g, rows);
+  return check_launch("oxc_softmax_dim_fwd");
+}
+
+oxc_status oxc_softmax_dim_bwd(const float* y, const oxc_view* dy, int64_t dim, int32_t log,
+                               float* dx, void* stream) {
+  const char* fn = log ? "log_softmax backward" : "softmax backward";
+  int d = 0;
+  oxc_status st = dim_check(fn, dy, dim, &d);
+  if (st) return st;
+  DimRows g;
+  const int64_t rows = dim_rows(dy, d, &g);
+  if (rows == 0) return OXC_OK;
+  if (!y || !dy->data || !dx)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: null pointer", fn);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (g.inner == 1 && g.xs == 1 && g.nd == 1 && (g.st[0] == g.len || rows == 1))
+    return oxc_softmax_bwd(y, dy->data, dx, rows, g.len, log, stream);
+  if (g.inner == 1) {
+    const unsigned grid = row_grid(rows);
+    const int block = row_block(g.len);
+    if (log) softmax_dim_rows_bwd_kernel<true><<<grid, block, 0, s>>>(y, dy->data, dx, g, rows);
+    else softmax_dim_rows_bwd_kernel<false><<<grid, block, 0, s>>>(y, dy->data, dx, g, rows);
+    return check_launch("oxc_softmax_dim_bwd");
+  }
+  dim3 grid, block;
+  dim_cols_launch_geometry(rows, g.len, &grid, &block);
+  if (log) softmax_dim_cols_bwd_kernel<true><<<grid, block, 0, s>>>(y, dy->data, dx, g, rows);
+  else softmax_dim_cols_bwd_kernel<false><<<grid, block, 0, s>>>(y, dy->data, dx, g, rows);
+  return check_launch("oxc_softmax_dim_bwd");
 }
 
 oxc_status oxc_cross_entropy_fwd(const float* logits, const int64_t* targets, float* loss,

@@ -47,10 +47,24 @@ def _rows_cols(x):
     return rows, cols
 
 
+def dense(t):
+    """t itself when it is dense row-major, else a dense copy made on the
+    device by oxc_contiguous (the reference's Tensor::contiguous,
+    crates/oxi-tensor/src/lib.rs:220-240): strided and transposed views reach
+    the fused row kernels through one copy kernel of this library."""
+    if t.is_contiguous():
+        return t
+    _require_cuda_f32("tensor", t)
+    out = torch.empty(t.shape, dtype=torch.float32, device=t.device)
+    N.check(N.load().oxc_contiguous(ctypes.byref(N.make_view(t)), ctypes.byref(N.make_view(out)),
+                                    _stream()), "contiguous")
+    return out
+
+
 def _row_major(name, t):
-    if not t.is_contiguous():
-        raise ValueError(f"invalid argument: {name} must be contiguous for the fused row kernels")
-    return t
+    """The fused row kernels read dense rows: a strided view is copied first
+    (the reference's compositions accept any view and produce dense results)."""
+    return dense(t)
 
 
 def _vector(name, t, cols):
@@ -88,6 +102,7 @@ def rms_norm_fwd(x, weight, eps=1e-6):
 
 def rms_norm_bwd(x, weight, rstd, dy, grad_mode="ref"):
     """Returns (dx, dweight)."""
+    x = _row_major("x", x)
     rows, cols = _rows_cols(x)
     weight = _vector("weight", weight, cols)
     dy = _row_major("dy", dy)
@@ -105,6 +120,7 @@ def rms_norm_bwd(x, weight, rstd, dy, grad_mode="ref"):
 class _RMSNorm(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, weight, eps, grad_mode):
+        x = dense(x)
         y, rstd = rms_norm_fwd(x, weight, eps)
         ctx.save_for_backward(x, weight, rstd)
         ctx.grad_mode = grad_mode
@@ -113,7 +129,7 @@ class _RMSNorm(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy):
         x, weight, rstd = ctx.saved_tensors
-        dx, dw = rms_norm_bwd(x, weight, rstd, dy.contiguous(), ctx.grad_mode)
+        dx, dw = rms_norm_bwd(x, weight, rstd, dense(dy), ctx.grad_mode)
         return dx, dw.reshape(weight.shape), None, None
 
 
@@ -145,6 +161,7 @@ def layer_norm_fwd(x, weight, bias, eps=1e-5, act=N.ACT_NONE):
 
 def layer_norm_bwd(x, weight, bias, mean, rstd, dy, act=N.ACT_NONE, grad_mode="ref"):
     """Returns (dx, dweight, dbias)."""
+    x = _row_major("x", x)
     rows, cols = _rows_cols(x)
     weight = _vector("weight", weight, cols)
     bias = _vector("bias", bias, cols)
@@ -164,6 +181,7 @@ def layer_norm_bwd(x, weight, bias, mean, rstd, dy, act=N.ACT_NONE, grad_mode="r
 class _LayerNorm(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, weight, bias, eps, act, grad_mode):
+        x = dense(x)
         y, mean, rstd = layer_norm_fwd(x, weight, bias, eps, act)
         ctx.save_for_backward(x, weight, bias, mean, rstd)
         ctx.act, ctx.grad_mode = act, grad_mode
@@ -172,7 +190,7 @@ class _LayerNorm(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy):
         x, weight, bias, mean, rstd = ctx.saved_tensors
-        dx, dw, db = layer_norm_bwd(x, weight, bias, mean, rstd, dy.contiguous(), ctx.act,
+        dx, dw, db = layer_norm_bwd(x, weight, bias, mean, rstd, dense(dy), ctx.act,
                                     ctx.grad_mode)
         return dx, dw.reshape(weight.shape), db.reshape(bias.shape), None, None, None
 
@@ -190,54 +208,58 @@ def layer_norm_gelu(x, weight, bias, eps=1e-5, grad_mode="ref"):
 
 # ---- softmax / log_softmax ----------------------------------------------------------
 
-def _last_dim_only(dim, x):
-    if dim not in (-1, x.dim() - 1):
-        raise NotImplementedError("not implemented: softmax over a dim other than the last")
+def _softmax_dim(dim, x):
+    if x.dim() == 0:
+        raise ValueError(f"invalid argument: dim {dim} out of range for 0-D tensor")
+    d = dim + x.dim() if dim < 0 else dim
+    if not 0 <= d < x.dim():
+        raise ValueError(f"invalid argument: dim {dim} out of range for {x.dim()}-D tensor")
+    return d
 
 
-def softmax_fwd(x, log=False):
+def softmax_fwd(x, log=False, dim=-1):
+    """y (dense, x's shape) = softmax or log_softmax of x over `dim`; x may be
+    any strided view.  Dense rows along the last dim run the row kernels,
+    other layouts the strided-row or column kernels (oxc_softmax_dim_fwd)."""
     _require_cuda_f32("x", x)
-    x = _row_major("x", x)
-    rows, cols = _rows_cols(x)
-    y = torch.empty_like(x)
-    N.check(N.load().oxc_softmax_fwd(x.data_ptr(), y.data_ptr(), rows, cols, int(log), _stream()),
-            "softmax")
+    d = _softmax_dim(dim, x)
+    y = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+    N.check(N.load().oxc_softmax_dim_fwd(ctypes.byref(N.make_view(x)), d, int(log), y.data_ptr(),
+                                         _stream()), "softmax")
     return y
 
 
-def softmax_bwd(y, dy, log=False):
-    rows, cols = _rows_cols(y)
-    dy = _row_major("dy", dy)
-    dx = torch.empty_like(y)
-    N.check(N.load().oxc_softmax_bwd(y.data_ptr(), dy.data_ptr(), dx.data_ptr(), rows, cols,
-                                     int(log), _stream()), "softmax backward")
+def softmax_bwd(y, dy, log=False, dim=-1):
+    """dx (dense) from the forward output y (dense) and dy (any view)."""
+    d = _softmax_dim(dim, y)
+    dx = torch.empty(y.shape, dtype=torch.float32, device=y.device)
+    N.check(N.load().oxc_softmax_dim_bwd(y.data_ptr(), ctypes.byref(N.make_view(dy)), d, int(log),
+                                         dx.data_ptr(), _stream()), "softmax backward")
     return dx
 
 
 class _Softmax(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, log):
-        y = softmax_fwd(x, log)
+    def forward(ctx, x, log, dim):
+        y = softmax_fwd(x, log, dim)
         ctx.save_for_backward(y)
-        ctx.log = log
+        ctx.log, ctx.dim = log, dim
         return y
 
     @staticmethod
     def backward(ctx, dy):
         (y,) = ctx.saved_tensors
-        return softmax_bwd(y, dy.contiguous(), ctx.log), None
+        return softmax_bwd(y, dy, ctx.log, ctx.dim), None, None
 
 
 def softmax(x, dim=-1):
-    """F.softmax (functional.py:211-215), numerically stable, over the last dim."""
-    _last_dim_only(dim, x)
-    return _Softmax.apply(x, False)
+    """F.softmax (functional.py:211-215), numerically stable, over any dim."""
+    return _Softmax.apply(x, False, dim)
 
 
 def log_softmax(x, dim=-1):
-    """F.log_softmax (functional.py:218-222) over the last dim."""
-    _last_dim_only(dim, x)
-    return _Softmax.apply(x, True)
+    """F.log_softmax (functional.py:218-222) over any dim."""
+    return _Softmax.apply(x, True, dim)
 
 
 # ---- cross-entropy ----------------------------------------------------------------------
@@ -364,7 +386,7 @@ class _Embedding(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dout):
         (ids,) = ctx.saved_tensors
-        dtable, _ = embedding_bwd(ids, dout.contiguous(), ctx.rows)
+        dtable, _ = embedding_bwd(ids, dense(dout), ctx.rows)
         return None, dtable
 
 

@@ -18,7 +18,7 @@ import ctypes
 import torch
 
 from . import _native as N
-from .functional import _require_cuda_f32, _stream, _workspace
+from .functional import _require_cuda_f32, _stream, _workspace, dense
 
 BINARY_OPS = ["add", "sub", "mul", "div", "pow", "min", "max"]
 CMP_OPS = ["eq", "ne", "lt", "le", "gt", "ge"]
@@ -144,7 +144,7 @@ def reduce_backward(kind, x, dim, g):
             kshape, kshape[:d] + kshape[d + 1:]):
         raise ValueError(f"shape mismatch: gradient {list(g.shape)} for reduce output of "
                          f"{list(x.shape)} over dim {d}")
-    g = g.contiguous()
+    g = dense(g)
     dx = torch.empty(x.shape, dtype=torch.float32, device=x.device)
     L = N.load()
     xv = N.make_view(x)
@@ -292,7 +292,8 @@ def clip_grad_value_(grads, clip_value):
             continue
         _require_cuda_f32("grad", g)
         if not g.is_contiguous():
-            raise ValueError("invalid argument: clip_grad_value_ takes contiguous gradients")
+            raise ValueError("invalid argument: clip_grad_value_ clips gradients in place, "
+                             "which needs dense storage")
         N.check(L.oxc_clip_grad_value(g.data_ptr(), g.numel(), clip_value, _stream()),
                 "clip_grad_value_")
 
@@ -353,7 +354,7 @@ class _ScatterDim0(torch.autograd.Function):
         # the three maps cross to the device in one copy; the VJP reuses them
         dmaps = torch.as_tensor(np.concatenate(maps)).to(base.device)
         fwd, keep, win = dmaps[:rows], dmaps[rows:2 * rows], dmaps[2 * rows:]
-        out = _select_rows(values.contiguous(), values.shape[0], fwd, base.contiguous(), inner,
+        out = _select_rows(dense(values), values.shape[0], fwd, dense(base), inner,
                            base.device)
         ctx.maps, ctx.rows, ctx.inner = (keep, win), rows, inner
         ctx.base_shape, ctx.values_shape = base.shape, values.shape
@@ -362,7 +363,7 @@ class _ScatterDim0(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g):
         keep, win = ctx.maps
-        g = g.contiguous()
+        g = dense(g)
         gb = gv = None
         if ctx.needs_input_grad[0]:
             gb = _select_rows(g, ctx.rows, keep, None, ctx.inner, g.device).reshape(ctx.base_shape)
@@ -426,7 +427,7 @@ class _NarrowDim0(torch.autograd.Function):
         for d in ctx.shape[1:]:
             inner *= d
         dmap = torch.as_tensor(ctx.map).to(g.device)
-        gx = _select_rows(g.contiguous(), ctx.kept, dmap, None, inner, g.device)
+        gx = _select_rows(dense(g), ctx.kept, dmap, None, inner, g.device)
         return gx.reshape(ctx.shape), None, None
 
 
@@ -439,6 +440,131 @@ def narrow_dim0(x, offset, length):
     if x.dim() == 0:
         raise ValueError("invalid argument: dim 0 out of range for 0-D tensor")
     return _NarrowDim0.apply(x, int(offset), int(length))
+
+
+# ---- index_select along any dim, gather -------------------------------------------------
+
+def _index_list(indices, length, dim, device, flat=False):
+    """Validates host indices like Tensor::index_select (lib.rs:665-675):
+    negative indices count from the end, any other out-of-range index raises
+    OutOfBounds (RuntimeError) before anything is copied.  Device tensors of
+    indices are checked by the kernels (error flag)."""
+    if isinstance(indices, torch.Tensor):
+        return indices.to(device=device, dtype=torch.int64).reshape(-1).contiguous(), False
+    ids = [int(i) for i in indices]
+    for i in ids:
+        idx = length + i if i < 0 else i
+        if idx < 0 or idx >= length:
+            if flat:
+                raise RuntimeError(f"out of bounds: flat index {i} out of range for "
+                                   f"{length} elements")
+            raise RuntimeError(f"out of bounds: index {i} out of range for dim {dim} "
+                               f"of size {length}")
+    return torch.tensor(ids, dtype=torch.int64, device=device), True
+
+
+def _norm_dim(dim, nd):
+    if nd == 0:
+        raise ValueError(f"invalid argument: dim {dim} out of range for 0-D tensor")
+    d = dim + nd if dim < 0 else dim
+    if not 0 <= d < nd:
+        raise ValueError(f"invalid argument: dim {dim} out of range for {nd}-D tensor")
+    return d
+
+
+def _check_flag(flag):
+    N.check(N.load().oxc_check_error_flag(flag.data_ptr(), _stream(), -1), "index_select")
+
+
+def index_select_fwd(x, dim, ids, checked=True):
+    """out (dense) = x.index_select(dim, ids) for a device int64 ids tensor;
+    one oxc_index_select launch over x's strides."""
+    d = _norm_dim(dim, x.dim())
+    shape = list(x.shape)
+    shape[d] = ids.numel()
+    out = torch.empty(shape, dtype=torch.float32, device=x.device)
+    flag = torch.zeros(4, dtype=torch.int32, device=x.device)
+    N.check(N.load().oxc_index_select(ctypes.byref(N.make_view(x)), d, ids.data_ptr(),
+                                      ids.numel(), out.data_ptr(), flag.data_ptr(), _stream()),
+            "index_select")
+    if not checked:
+        _check_flag(flag)
+    return out
+
+
+def index_select_bwd(g, ids, shape, dim):
+    """scatter_index_select (crates/oxi-autograd/src/ops.rs:741-769): the
+    gradient of x (dense, `shape`) from g, summing duplicate indices in
+    position order."""
+    d = _norm_dim(dim, len(shape))
+    g = dense(g)
+    gx = torch.empty(tuple(shape), dtype=torch.float32, device=g.device)
+    dims = (ctypes.c_int64 * max(len(shape), 1))(*[int(v) for v in shape])
+    flag = torch.zeros(4, dtype=torch.int32, device=g.device)
+    L = N.load()
+    ws = _workspace(L.oxc_index_select_bwd_workspace_size(dims, len(shape), d, ids.numel()),
+                    g.device)
+    N.check(L.oxc_index_select_bwd(g.data_ptr(), ids.data_ptr(), ids.numel(), dims, len(shape), d,
+                                   gx.data_ptr(), flag.data_ptr(), ws.data_ptr(), ws.numel(),
+                                   _stream()), "index_select backward")
+    return gx
+
+
+class _IndexSelect(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, dim, ids, checked):
+        ctx.save_for_backward(ids)
+        ctx.dim, ctx.shape = dim, tuple(x.shape)
+        return index_select_fwd(x, dim, ids, checked)
+
+    @staticmethod
+    def backward(ctx, g):
+        (ids,) = ctx.saved_tensors
+        return index_select_bwd(g, ids, ctx.shape, ctx.dim), None, None, None
+
+
+def index_select(x, dim, indices):
+    """Tensor.index_select(dim, indices) (crates/oxi-bindings/src/lib.rs, the
+    ops::index_select node of crates/oxi-autograd/src/ops.rs:498-517): any
+    dim, any strides of x; indices a list of ints (validated here, like the
+    reference) or a device int64 tensor (validated by the kernel's error
+    flag).  Differentiable: duplicate indices accumulate."""
+    _require_cuda_f32("x", x)
+    d = _norm_dim(dim, x.dim())
+    ids, checked = _index_list(indices, x.shape[d], d, x.device)
+    return _IndexSelect.apply(x, d, ids, checked)
+
+
+def gather(x, indices):
+    """Tensor.gather(indices) (crates/oxi-bindings/src/lib.rs:645-648): the
+    differentiable index_select along dim 0."""
+    return index_select(x, 0, indices)
+
+
+def gather_dim0(x, indices):
+    """Tensor::gather_dim0 (crates/oxi-tensor/src/lib.rs:857-886): rows
+    x[indices[i], ...] (no graph node); a 0-D x is InvalidArgument."""
+    _require_cuda_f32("x", x)
+    if x.dim() == 0:
+        raise ValueError("invalid argument: gather_dim0 requires at least a 1-D tensor")
+    ids, checked = _index_list(indices, x.shape[0], 0, x.device)
+    shape = [ids.numel()] + list(x.shape[1:])
+    out = torch.empty(shape, dtype=torch.float32, device=x.device)
+    flag = torch.zeros(4, dtype=torch.int32, device=x.device)
+    N.check(N.load().oxc_gather_dim0(ctypes.byref(N.make_view(x)), ids.data_ptr(), ids.numel(),
+                                     out.data_ptr(), flag.data_ptr(), _stream()), "gather_dim0")
+    if not checked:
+        _check_flag(flag)
+    return out
+
+
+def gather_flat(x, indices):
+    """Tensor::gather_flat (crates/oxi-tensor/src/lib.rs:834-850): elements at
+    flat row-major indices of x, as a 1-D tensor (no graph node)."""
+    _require_cuda_f32("x", x)
+    flat = dense(x).reshape(-1)
+    ids, checked = _index_list(indices, flat.numel(), 0, x.device, flat=True)
+    return index_select_fwd(flat, 0, ids, checked)
 
 
 # ---- masked_select (boolean-mask indexing) and its VJP ---------------------------------------
@@ -482,7 +608,7 @@ class _MaskedSelect(torch.autograd.Function):
         mv = N.make_view(me)
         n = me.numel()
         ws, picks = _ms_count(None, mv, n, 1, g.device)
-        g = g.contiguous()
+        g = dense(g)
         if picks != g.numel():
             # the reference reads past the end of g here (a picked NaN of x
             # left the forward shorter than the mask's picks)
