@@ -419,8 +419,9 @@ def _time_ops(torch, ops):
 
 def _shard(n, rank, world, mode):
     """Rows [lo, hi) of n that this rank works on: all of them in weak mode
-    (every rank owns a full config), its balanced share in strong mode."""
-    if mode == "weak":
+    (every rank owns a full config) and in single mode (one GPU's run of the
+    config inside a multi-GPU job), its balanced share in strong mode."""
+    if mode != "strong":
         return 0, n
     from oxitorch_b200.sharded import shard_range
     return shard_range(n, rank, world)
@@ -721,12 +722,34 @@ class Embedding(Workload):
         self.n = n = hi - lo
         self.table = inp["table"]
         self.out = t.empty(n, self.d, device=dev)
-        self.dtable = t.empty_like(self.table)
         self.flag = t.zeros(4, dtype=t.int32, device=dev)
-        self.ws_bytes = self.L.oxc_embedding_bwd_workspace_size(n, self.v, self.d)
-        self.ws = t.empty(max(self.ws_bytes, 16), dtype=t.uint8, device=dev)
         self.fwd_bytes = n * 8 + 2 * n * self.d * 4
-        self.bwd_bytes = n * 8 + n * self.d * 4 + self.v * self.d * 4
+        if world == 1 or mode == "single":
+            self.world = 1  # the single-GPU VJP, no exchange
+            self.dtable = t.empty_like(self.table)
+            self.ws_bytes = self.L.oxc_embedding_bwd_workspace_size(n, self.v, self.d)
+            self.bwd_bytes = n * 8 + n * self.d * 4 + self.v * self.d * 4
+        else:
+            # token-sharded, replicated table: the compact VJP (touched rows),
+            # an all-to-all of those rows to their vocab shard's owner, and the
+            # owner's rank-order sum into its dense shard of the gradient
+            from oxitorch_b200.sharded import vocab_shard
+            self.shard_lo, self.shard_rows = vocab_shard(self.v, rank, world)
+            cap = min(n, self.v)
+            self.c_ids = t.empty(cap, dtype=t.int32, device=dev)
+            self.c_rows = t.empty(cap, self.d, device=dev)
+            self.count = t.empty(1, dtype=t.int64, device=dev)
+            self.shard_counts = t.empty(world, dtype=t.int64, device=dev)
+            self.dshard = t.empty(self.shard_rows, self.d, device=dev)
+            self.ws_bytes = self.L.oxc_embedding_bwd_compact_workspace_size(n, self.v, self.d)
+            self.ws2_bytes = self.L.oxc_embedding_exchange_reduce_workspace_size(
+                world, self.shard_rows)
+            self.ws2 = t.empty(max(self.ws2_bytes, 16), dtype=t.uint8, device=dev)
+            self.launches = 14  # + present, scan (2), meta, map, reduce (and NCCL's)
+            # this rank's share of the job's bytes: its tokens' ids and dout,
+            # and its shard of the dense table gradient
+            self.bwd_bytes = n * 8 + n * self.d * 4 + self.shard_rows * self.d * 4
+        self.ws = t.empty(max(self.ws_bytes, 16), dtype=t.uint8, device=dev)
 
     def fwd(self, dout=None):
         self.N.check(self.L.oxc_embedding_fwd(self.table.data_ptr(), self.ids.data_ptr(),
@@ -734,18 +757,35 @@ class Embedding(Workload):
                                               self.d, self.flag.data_ptr(), self.s))
 
     def bwd(self, dout=None):
-        self.N.check(self.L.oxc_embedding_bwd((dout if dout is not None else self.dout).data_ptr(),
-                                              self.ids.data_ptr(), self.dtable.data_ptr(), self.n,
-                                              self.v, 0, self.v, self.d, self.flag.data_ptr(),
-                                              self.ws.data_ptr(), self.ws_bytes, self.s))
+        dout = dout if dout is not None else self.dout
+        if self.world == 1:
+            self.N.check(self.L.oxc_embedding_bwd(dout.data_ptr(), self.ids.data_ptr(),
+                                                  self.dtable.data_ptr(), self.n, self.v, 0,
+                                                  self.v, self.d, self.flag.data_ptr(),
+                                                  self.ws.data_ptr(), self.ws_bytes, self.s))
+            return
+        self.N.check(self.L.oxc_embedding_bwd_compact(
+            dout.data_ptr(), self.ids.data_ptr(), self.n, self.v, 0, self.v, self.d,
+            self.c_ids.data_ptr(), self.c_rows.data_ptr(), self.count.data_ptr(), self.world,
+            self.shard_counts.data_ptr(), self.flag.data_ptr(), self.ws.data_ptr(),
+            self.ws_bytes, self.s))
 
     def exchange(self):
-        if self.world > 1:
-            from oxitorch_b200 import sharded
-            self.dshard = sharded.reduce_scatter_rows(self.dtable)
+        if self.world == 1:
+            return
+        from oxitorch_b200 import sharded
+        rid, rrows, rc = sharded.exchange_rows(self.c_ids, self.c_rows, self.shard_counts)
+        off = [0]
+        for c in rc:
+            off.append(off[-1] + c)
+        src_off = self.torch.tensor(off, dtype=self.torch.int64).to(self.dev, non_blocking=True)
+        self.N.check(self.L.oxc_embedding_exchange_reduce(
+            rid.data_ptr(), rrows.data_ptr(), src_off.data_ptr(), self.world, self.shard_lo,
+            self.shard_rows, self.d, self.dshard.data_ptr(), self.flag.data_ptr(),
+            self.ws2.data_ptr(), self.ws2_bytes, self.s))
 
     def e2e_io(self):
-        return [self.dout], [self.out, self.dtable]
+        return [self.dout], [self.out, self.dtable if self.world == 1 else self.dshard]
 
     def e2e_step(self, dev_in):
         self.fwd()
@@ -754,13 +794,69 @@ class Embedding(Workload):
 
     def config(self):
         return {"workload": self.DESC, "ids_per_gpu": self.n, "table": [self.v, self.d],
-                "parallelism": f"token-sharded data parallel x{self.world}, dtable reduce-scatter "
-                               "to vocab shards",
+                "parallelism": (f"token-sharded data parallel x{self.world}, replicated table; "
+                                "compact VJP + all-to-all of the touched rows to their vocab "
+                                "shard's owner + rank-order sum (sparse exchange)"
+                                if self.world > 1 else "one GPU"),
                 "inputs": self.inputs_note(),
                 "roofline_note": "the VJP is the HBM-bound phase; the gather's hot table rows are "
                                  "L2 hits, so its algorithmic bytes exceed its DRAM bytes "
                                  "(fwd_dram_gbs)",
                 "l2": "no flush: dout (2.1 GB) is larger than L2"}
+
+
+class EmbeddingVocab(Workload):
+    """The vocab-sharded scheme: every rank holds a 1/N row shard of the table
+    and all the ids; the forward is a masked gather (zeros for other shards'
+    ids) followed by an all-reduce of the [131072, 4096] output; each rank's
+    VJP writes its own shard's rows from the replicated dout, with no exchange.
+    Communication-bound by construction: reported beside the token-sharded
+    scheme, as strong scaling of the one config."""
+    DESC = ("embedding, vocab-sharded table: masked gather + all-reduce of the [131072, 4096] "
+            "output, per-shard duplicate-id VJP (BASELINE config 4)")
+    CONFIG = 4
+    KERNEL = "emb_gather_kernel + NCCL all-reduce of the output (the step is communication-bound)"
+    dominant = "fwd"
+    launches = 9
+    ROWS = ("n", "tokens")
+
+    def __init__(self, dev, rank, world, args, inp, mode="strong"):
+        super().__init__(dev, rank, world, args, inp, mode)
+        t = self.torch
+        from oxitorch_b200.sharded import vocab_shard
+        self.v, self.d = 32000, 4096
+        self.ids, self.dout = inp["ids"], inp["dout"]
+        self.n = n = self.ids.shape[0]
+        self.lo, self.rows = vocab_shard(self.v, rank, world)
+        self.table = inp["table"][self.lo:self.lo + self.rows]
+        self.out = t.empty(n, self.d, device=dev)
+        self.dshard = t.empty(self.rows, self.d, device=dev)
+        self.flag = t.zeros(4, dtype=t.int32, device=dev)
+        self.ws_bytes = self.L.oxc_embedding_bwd_workspace_size(n, self.rows, self.d)
+        self.ws = t.empty(max(self.ws_bytes, 16), dtype=t.uint8, device=dev)
+        # the job's algorithmic bytes are the one config's, shared by the ranks
+        self.fwd_bytes = (n * 8 + 2 * n * self.d * 4) // world
+        self.bwd_bytes = (n * 8 + n * self.d * 4 + self.v * self.d * 4) // world
+
+    def fwd(self):
+        self.N.check(self.L.oxc_embedding_fwd(self.table.data_ptr(), self.ids.data_ptr(),
+                                              self.out.data_ptr(), self.n, self.v, self.lo,
+                                              self.rows, self.d, self.flag.data_ptr(), self.s))
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(self.out, op=dist.ReduceOp.SUM)
+
+    def bwd(self):
+        self.N.check(self.L.oxc_embedding_bwd(self.dout.data_ptr(), self.ids.data_ptr(),
+                                              self.dshard.data_ptr(), self.n, self.v, self.lo,
+                                              self.rows, self.d, self.flag.data_ptr(),
+                                              self.ws.data_ptr(), self.ws_bytes, self.s))
+
+    def config(self):
+        return {"workload": self.DESC, "ids": self.n, "table_rows_per_gpu": self.rows,
+                "parallelism": f"vocab-sharded x{self.world}: output all-reduce "
+                               f"({self.n * self.d * 4 / 1e9:.2f} GB) in the forward",
+                "inputs": self.inputs_note()}
 
 
 class MlpBlock(Workload):
@@ -1085,8 +1181,8 @@ class Loader(Workload):
 
 
 WORKLOADS = {"ln_gelu": LnGelu, "rms": Rms, "ce": CrossEntropy, "embedding": Embedding,
-             "mlp_block": MlpBlock, "registry": Registry, "optim": Optim,
-             "loader": Loader}
+             "embedding_vocab": EmbeddingVocab, "mlp_block": MlpBlock, "registry": Registry,
+             "optim": Optim, "loader": Loader}
 
 
 # ---- timing ----------------------------------------------------------------------------------
@@ -1237,7 +1333,7 @@ def measure(name, args, rank, world, local_rank, inp, steps, warmup, mode="weak"
 
 # the input whose rows the strong-scaling split divides
 GLOBAL_ROWS_KEY = {"ln_gelu": "x", "rms": "x", "ce": "logits", "embedding": "ids",
-                   "mlp_block": "x", "registry": "up"}
+                   "embedding_vocab": "ids", "mlp_block": "x", "registry": "up"}
 
 
 def strong_scaling(name, args, rank, world, local_rank, inp, steps, warmup):
@@ -1249,7 +1345,7 @@ def strong_scaling(name, args, rank, world, local_rank, inp, steps, warmup):
     dev = torch.device("cuda", local_rank)
     t1 = None
     if rank == 0:
-        wl1 = WORKLOADS[name](dev, rank, world, args, inp, "weak")
+        wl1 = WORKLOADS[name](dev, rank, world, args, inp, "single")
         t1, _, _, _ = time_steps(wl1, steps, warmup, world, local_rank, exchange=False, solo=True)
         del wl1
     dist.barrier()
@@ -1309,6 +1405,17 @@ def run_ours(args, rank, world, local_rank):
                 orep["strong_scaling"] = strong_scaling(other, args, rank, world, local_rank,
                                                         oinp, psteps, 3)
             per_workload[other] = orep
+            if other == "embedding" and world > 1:
+                # the vocab-sharded scheme beside the token-sharded one
+                vwl, vrep = measure("embedding_vocab", args, rank, world, local_rank, oinp,
+                                    psteps, 3, mode="strong")
+                del vwl
+                if rank == 0 and orep.get("strong_scaling"):
+                    t1 = orep["strong_scaling"]["t1_ms_per_step"]
+                    vrep["strong_scaling"] = {"t1_ms_per_step": t1,
+                                              "ms_per_step": vrep["ms_per_step"],
+                                              "efficiency": t1 / (world * vrep["ms_per_step"])}
+                per_workload["embedding_vocab_sharded"] = vrep
             del oinp
             torch.cuda.synchronize()
             torch.cuda.empty_cache()

@@ -367,6 +367,36 @@ oxc_status oxc_embedding_bwd(const float* dout, const int64_t* ids, float* dtabl
                              int64_t cols, int32_t* err_flag, void* workspace,
                              size_t workspace_bytes, void* stream);
 
+/* ---- sparse exchange of a replicated table's gradient ------------------------
+ * No counterpart in the reference (it has no distributed runtime): the
+ * multi-GPU step of the embedding VJP when tokens are sharded across ranks and
+ * the table is replicated.  oxc_embedding_bwd_compact is oxc_embedding_bwd
+ * restricted to the rows that occur: out_ids int32 [min(n, rows)] receives the
+ * occurring table rows (global ids, ascending), out_rows [min(n, rows), cols]
+ * their gradients (the same sums as oxc_embedding_bwd), *count (device int64)
+ * how many, and shard_counts (device int64 [shards], optional) how many fall in
+ * each vocab shard of a `shards`-way balanced split of vocab_total rows
+ * (shard s = rows [V*s/G, V*(s+1)/G)): the send counts of an all-to-all.
+ * oxc_embedding_exchange_reduce is the owner's side after the all-to-all:
+ * recv_ids / recv_rows hold the rows received from `sources` ranks, source s
+ * at [src_offsets[s], src_offsets[s+1]) (device int64 [sources+1]); dshard
+ * [shard_rows, cols] (rows shard_lo...) becomes, per row, the sum in source
+ * order from 0.0 of the received rows (zeros where none arrived).  A received
+ * id outside the shard is recorded in err_flag. */
+size_t oxc_embedding_bwd_compact_workspace_size(int64_t n, int64_t rows, int64_t cols);
+oxc_status oxc_embedding_bwd_compact(const float* dout, const int64_t* ids, int64_t n,
+                                     int64_t vocab_total, int64_t vocab_offset, int64_t rows,
+                                     int64_t cols, int32_t* out_ids, float* out_rows,
+                                     int64_t* count, int32_t shards, int64_t* shard_counts,
+                                     int32_t* err_flag, void* workspace, size_t workspace_bytes,
+                                     void* stream);
+size_t oxc_embedding_exchange_reduce_workspace_size(int32_t sources, int64_t shard_rows);
+oxc_status oxc_embedding_exchange_reduce(const int32_t* recv_ids, const float* recv_rows,
+                                         const int64_t* src_offsets, int32_t sources,
+                                         int64_t shard_lo, int64_t shard_rows, int64_t cols,
+                                         float* dshard, int32_t* err_flag, void* workspace,
+                                         size_t workspace_bytes, void* stream);
+
 /* ---- index_select along any dim, and its VJP --------------------------------
  * oxc_index_select replaces Tensor::index_select (crates/oxi-tensor/src/lib.rs:
  * 665-703) for any dim and any strides of x: out (dense row-major, x's shape

@@ -116,6 +116,12 @@ SIGNATURES = {
     "oxc_embedding_fwd": (_I32, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P]),
     "oxc_embedding_bwd_workspace_size": (_SZ, [_I64, _I64, _I64]),
     "oxc_embedding_bwd": (_I32, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _SZ, _P]),
+    "oxc_embedding_bwd_compact_workspace_size": (_SZ, [_I64, _I64, _I64]),
+    "oxc_embedding_bwd_compact": (_I32, [_P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _I32,
+                                         _P, _P, _P, _SZ, _P]),
+    "oxc_embedding_exchange_reduce_workspace_size": (_SZ, [_I32, _I64]),
+    "oxc_embedding_exchange_reduce": (_I32, [_P, _P, _P, _I32, _I64, _I64, _I64, _P, _P, _P, _SZ,
+                                             _P]),
     "oxc_index_select": (_I32, [_VP, _I64, _P, _I64, _P, _P, _P]),
     "oxc_gather_dim0": (_I32, [_VP, _P, _I64, _P, _P, _P]),
     "oxc_index_select_bwd_workspace_size": (_SZ, [_P, _I32, _I64, _I64]),

@@ -29,6 +29,7 @@
 //   [vocab_offset, vocab_offset + rows); ids outside are zero rows forward
 //   and contribute nothing backward.
 #include <cub/device/device_radix_sort.cuh>
+#include <cub/device/device_scan.cuh>
 
 #include <algorithm>
 
@@ -228,11 +229,14 @@ __global__ void __launch_bounds__(MAXT) emb_split_kernel(
   }
 }
 
+// With `slot` (the compact VJP, outer == 1), rows without occurrences are
+// skipped and row r is written at dtable + slot[r] * cols.
 template <int VW, int VPT, int MAXT>
 __global__ void __launch_bounds__(MAXT) emb_rows_kernel(
     const float* __restrict__ dout_all, const int32_t* __restrict__ spos,
     const int32_t* __restrict__ offsets, const float* __restrict__ parts_all, int64_t rows,
-    int cols, float* __restrict__ dtable, int64_t n, int64_t outer) {
+    int cols, float* __restrict__ dtable, int64_t n, int64_t outer,
+    const int32_t* __restrict__ slot) {
   // Launched as a programmatic dependent of emb_split_kernel: rows with at
   // most kSplitP occurrences read only the sort's output and run while the
   // split grid is still working; rows made of pieces wait for it (pdl_wait)
@@ -245,7 +249,8 @@ __global__ void __launch_bounds__(MAXT) emb_rows_kernel(
     const float* dout = dout_all + o * n * (int64_t)cols;
     const float* parts = parts_all + o * 2 * nblocks * (int64_t)cols;
     const int64_t s0 = offsets[r], s1 = offsets[r + 1];
-    float* dst = dtable + (o * rows + r) * (int64_t)cols;
+    if (slot && s1 == s0) continue;
+    float* dst = dtable + (slot ? (int64_t)slot[r] : o * rows + r) * (int64_t)cols;
     for (int c_base = blockIdx.y * VPT * blockDim.x; c_base < nvec;
          c_base += gridDim.y * VPT * blockDim.x) {
       float acc[VPT][VW];
@@ -398,16 +403,116 @@ __global__ void __launch_bounds__(256) isel_bwd_narrow_kernel(
   }
 }
 
+// ---- the compact VJP and the sparse exchange of a replicated table's gradient ----
+
+// present[r] = 1 if table row r occurs, for the exclusive scan that gives
+// each occurring row its compact slot.
+__global__ void emb_present_kernel(const int32_t* __restrict__ offsets, int64_t rows,
+                                   int32_t* __restrict__ present) {
+  for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < rows;
+       r += (int64_t)gridDim.x * blockDim.x)
+    present[r] = offsets[r + 1] > offsets[r] ? 1 : 0;
+}
+
+// Compact ids (global table rows), the distinct count, and per destination
+// shard the number of distinct rows it owns (shard s = rows [V*s/G, V*(s+1)/G)
+// of the whole vocab_total-row table, this table covering [offset, offset +
+// rows)).
+__global__ void emb_compact_meta_kernel(const int32_t* __restrict__ present,
+                                        const int32_t* __restrict__ slot, int64_t rows,
+                                        int64_t vocab_total, int64_t offset, int32_t shards,
+                                        int32_t* __restrict__ out_ids,
+                                        int64_t* __restrict__ count,
+                                        int64_t* __restrict__ shard_counts) {
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (int64_t r = tid; r < rows; r += (int64_t)gridDim.x * blockDim.x)
+    if (present[r]) out_ids[slot[r]] = (int32_t)(r + offset);
+  if (tid == 0) *count = rows ? (int64_t)slot[rows - 1] + present[rows - 1] : 0;
+  if (shard_counts && tid < shards) {
+    const int64_t s = tid;
+    // rows of shard s inside this table, clamped
+    auto bound = [&](int64_t g) -> int64_t {
+      const int64_t l = vocab_total * g / shards - offset;
+      return l < 0 ? 0 : (l > rows ? rows : l);
+    };
+    const int64_t lo = bound(s), hi = bound(s + 1);
+    auto pre = [&](int64_t r) -> int64_t {
+      return r >= rows ? (rows ? (int64_t)slot[rows - 1] + present[rows - 1] : 0) : slot[r];
+    };
+    shard_counts[s] = pre(hi) - pre(lo);
+  }
+}
+
+// The owner's side of the sparse exchange: dshard[v] (v < shard_rows) is the
+// sum, in source-rank order from 0.0, of the rows received for table row
+// shard_lo + v.  map[s * shard_rows + v] = index of that row in recv_rows, or
+// -1; filled by emb_exchange_map_kernel.
+__global__ void emb_exchange_map_kernel(const int32_t* __restrict__ recv_ids,
+                                        const int64_t* __restrict__ src_off, int32_t sources,
+                                        int64_t shard_lo, int64_t shard_rows,
+                                        int32_t* __restrict__ map, int32_t* err) {
+  const int64_t total = src_off[sources];
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int s = 0;
+    while (s + 1 < sources && src_off[s + 1] <= i) ++s;
+    const int64_t v = (int64_t)recv_ids[i] - shard_lo;
+    if (v < 0 || v >= shard_rows) {
+      if (err && atomicCAS(err, 0, 1) == 0) {
+        err[1] = recv_ids[i];
+        err[2] = 0;
+        err[3] = (int32_t)shard_rows;
+      }
+      continue;
+    }
+    map[(int64_t)s * shard_rows + v] = (int32_t)i;
+  }
+}
+
+template <int VW>
+__global__ void __launch_bounds__(128) emb_exchange_reduce_kernel(
+    const float* __restrict__ recv_rows, const int32_t* __restrict__ map, int32_t sources,
+    int64_t shard_rows, int cols, float* __restrict__ dshard) {
+  const int nvec = cols / VW;
+  for (int64_t v = blockIdx.x; v < shard_rows; v += gridDim.x) {
+    int32_t idx[8];
+    const int ns = sources < 8 ? sources : 8;
+    for (int s = 0; s < ns; ++s) idx[s] = map[(int64_t)s * shard_rows + v];
+    for (int c = blockIdx.y * blockDim.x + threadIdx.x; c < nvec; c += gridDim.y * blockDim.x) {
+      float acc[VW];
+#pragma unroll
+      for (int e = 0; e < VW; ++e) acc[e] = 0.0f;
+      for (int s = 0; s < sources; ++s) {
+        const int32_t i = s < 8 ? idx[s] : map[(int64_t)s * shard_rows + v];
+        if (i < 0) continue;
+        if constexpr (VW == 4) {
+          const float4 q = ld_stream(reinterpret_cast<const float4*>(recv_rows + (int64_t)i * cols) + c);
+          acc[0] = __fadd_rn(acc[0], q.x); acc[1] = __fadd_rn(acc[1], q.y);
+          acc[2] = __fadd_rn(acc[2], q.z); acc[3] = __fadd_rn(acc[3], q.w);
+        } else {
+          acc[0] = __fadd_rn(acc[0], ld_stream(recv_rows + (int64_t)i * cols + c));
+        }
+      }
+      if constexpr (VW == 4)
+        st_stream(reinterpret_cast<float4*>(dshard + v * cols) + c,
+                  make_float4(acc[0], acc[1], acc[2], acc[3]));
+      else
+        st_stream(dshard + v * cols + c, acc[0]);
+    }
+  }
+}
+
 struct EmbLayout {
   size_t keys_in, vals_in, keys_out, vals_out, offsets, parts, cub, total;
   size_t cub_bytes;
   int end_bit;
+  size_t present, slot, scan, scan_bytes;  // the compact VJP only
 };
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 static oxc_status emb_layout(int64_t n, int64_t rows, int64_t cols, EmbLayout* L,
-                             int64_t outer = 1) {
+                             int64_t outer = 1, bool compact = false) {
   int end_bit = 1;
   while (end_bit < 31 && ((int64_t)1 << end_bit) <= rows) ++end_bit;  // keys in [0, rows]
   size_t cub_bytes = 0;
@@ -424,6 +529,17 @@ static oxc_status emb_layout(int64_t n, int64_t rows, int64_t cols, EmbLayout* L
   L->offsets = off; off += align256((size_t)(rows + 1) * 4);
   L->parts = off; off += align256((size_t)2 * nblocks * cols * 4 * (size_t)outer);
   L->cub = off; off += align256(cub_bytes);
+  L->present = L->slot = L->scan = L->scan_bytes = 0;
+  if (compact) {
+    size_t scan_bytes = 0;
+    e = cub::DeviceScan::ExclusiveSum(nullptr, scan_bytes, (const int32_t*)nullptr,
+                                      (int32_t*)nullptr, (int)std::max<int64_t>(rows, 1));
+    if (e != cudaSuccess) return cuda_fail(e, "embedding backward (scan workspace size)");
+    L->present = off; off += align256((size_t)(rows + 1) * 4);
+    L->slot = off; off += align256((size_t)(rows + 1) * 4);
+    L->scan = off; off += align256(scan_bytes);
+    L->scan_bytes = scan_bytes;
+  }
   L->total = off;
   L->cub_bytes = cub_bytes;
   L->end_bit = end_bit;
@@ -441,6 +557,68 @@ static oxc_status emb_check(const char* fn, int64_t n, int64_t vocab_total, int6
   if (n > 0x7fffffff || rows >= 0x7fffffff || cols > 0x7fffffff)
     return fail(OXC_ERR_NOT_IMPLEMENTED, "not implemented: %s: sizes beyond 2^31", fn);
   return OXC_OK;
+}
+
+// prepare -> stable radix sort of (row, position) -> segment offsets.
+static oxc_status emb_sort_phase(const int64_t* ids, int64_t n, int64_t vocab_total,
+                                 int64_t vocab_offset, int64_t rows, int32_t* err_flag, char* ws,
+                                 const EmbLayout& L, cudaStream_t s) {
+  int32_t* keys_in = reinterpret_cast<int32_t*>(ws + L.keys_in);
+  int32_t* vals_in = reinterpret_cast<int32_t*>(ws + L.vals_in);
+  int32_t* keys_out = reinterpret_cast<int32_t*>(ws + L.keys_out);
+  int32_t* vals_out = reinterpret_cast<int32_t*>(ws + L.vals_out);
+  int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
+  const unsigned g1 = (unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)sm_count() * 8);
+  emb_prepare_kernel<<<g1, 256, 0, s>>>(ids, n, vocab_total, vocab_offset, rows, keys_in, vals_in,
+                                        err_flag);
+  oxc_status st = check_launch("oxc_embedding_bwd (prepare)");
+  if (st) return st;
+  size_t cub_bytes = L.cub_bytes;
+  cudaError_t e = cub::DeviceRadixSort::SortPairs(ws + L.cub, cub_bytes, keys_in, keys_out,
+                                                  vals_in, vals_out, (int)n, 0, L.end_bit, s);
+  if (e != cudaSuccess) return cuda_fail(e, "oxc_embedding_bwd (sort)");
+  const unsigned g2 = (unsigned)std::min<int64_t>((n + 1 + 255) / 256, (int64_t)sm_count() * 8);
+  emb_offsets_kernel<<<g2, 256, 0, s>>>(keys_out, n, rows, offsets);
+  return check_launch("oxc_embedding_bwd (offsets)");
+}
+
+// hot-row pieces -> per-row sums in position order, into dtable (every row)
+// or, with `slot`, into the compact rows of the occurring ids.
+static oxc_status emb_sum_phase(const float* dout, int64_t n, int64_t rows, int64_t cols,
+                                char* ws, const EmbLayout& L, float* dtable, const int32_t* slot,
+                                cudaStream_t s) {
+  const int32_t* keys_out = reinterpret_cast<const int32_t*>(ws + L.keys_out);
+  const int32_t* vals_out = reinterpret_cast<const int32_t*>(ws + L.vals_out);
+  const int32_t* offsets = reinterpret_cast<const int32_t*>(ws + L.offsets);
+  float* parts = reinterpret_cast<float*>(ws + L.parts);
+  const bool v4 = cols % 4 == 0 && aligned16(dout) && aligned16(dtable);
+  const int64_t nblocks = (n + kSplitP - 1) / kSplitP;
+  const unsigned grows = (unsigned)std::min<int64_t>(rows, (int64_t)sm_count() * 32);
+  // Each CTA takes one column chunk of a row (blockIdx.y): kEmbChunkThreads
+  // threads with one float4 (or four floats) each.  Small CTAs keep many rows'
+  // gathers in flight on every SM: on B200 at [32000, 4096] the VJP ran at
+  // 4.7 / 4.9 / 5.0 / 5.1 / 5.0 / 4.8 TB/s with 1024 / 512 / 256 / 128 / 64 / 32
+  // threads per CTA.
+  const int vpt = v4 ? 1 : 4, vw = v4 ? 4 : 1;
+  const int64_t per_thread = (int64_t)vpt * vw;
+  const int block = (int)std::min<int64_t>(
+      kEmbChunkThreads, std::max<int64_t>(32, ((cols / per_thread + 31) / 32) * 32));
+  const int64_t chunks = std::min<int64_t>(65535, (cols + block * per_thread - 1) / (block * per_thread));
+  const dim3 gsplit((unsigned)nblocks, (unsigned)chunks), grow(grows, (unsigned)chunks);
+  if (v4) {
+    emb_split_kernel<4, 1, kEmbChunkThreads><<<gsplit, block, 0, s>>>(
+        dout, keys_out, vals_out, offsets, n, rows, (int)cols, parts, (int64_t)1);
+    launch_dependent(emb_rows_kernel<4, 1, kEmbChunkThreads>, grow, block, s, dout, vals_out,
+                     offsets, (const float*)parts, rows, (int)cols, dtable, n, (int64_t)1,
+                     slot);
+  } else {
+    emb_split_kernel<1, 4, kEmbChunkThreads><<<gsplit, block, 0, s>>>(
+        dout, keys_out, vals_out, offsets, n, rows, (int)cols, parts, (int64_t)1);
+    launch_dependent(emb_rows_kernel<1, 4, kEmbChunkThreads>, grow, block, s, dout, vals_out,
+                     offsets, (const float*)parts, rows, (int)cols, dtable, n, (int64_t)1,
+                     slot);
+  }
+  return check_launch("oxc_embedding_bwd");
 }
 
 }  // namespace oxc
@@ -501,51 +679,110 @@ oxc_status oxc_embedding_bwd(const float* dout, const int64_t* ids, float* dtabl
                 "invalid argument: embedding backward needs a %zu-byte workspace, got %zu",
                 L.total, workspace_bytes);
   char* ws = static_cast<char*>(workspace);
-  int32_t* keys_in = reinterpret_cast<int32_t*>(ws + L.keys_in);
-  int32_t* vals_in = reinterpret_cast<int32_t*>(ws + L.vals_in);
-  int32_t* keys_out = reinterpret_cast<int32_t*>(ws + L.keys_out);
-  int32_t* vals_out = reinterpret_cast<int32_t*>(ws + L.vals_out);
-  int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
-  float* parts = reinterpret_cast<float*>(ws + L.parts);
-  const unsigned g1 = (unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)sm_count() * 8);
-  emb_prepare_kernel<<<g1, 256, 0, s>>>(ids, n, vocab_total, vocab_offset, rows, keys_in, vals_in,
-                                        err_flag);
-  st = check_launch("oxc_embedding_bwd (prepare)");
+  st = emb_sort_phase(ids, n, vocab_total, vocab_offset, rows, err_flag, ws, L, s);
   if (st) return st;
-  size_t cub_bytes = L.cub_bytes;
-  cudaError_t e = cub::DeviceRadixSort::SortPairs(ws + L.cub, cub_bytes, keys_in, keys_out,
-                                                  vals_in, vals_out, (int)n, 0, L.end_bit, s);
-  if (e != cudaSuccess) return cuda_fail(e, "oxc_embedding_bwd (sort)");
-  const unsigned g2 = (unsigned)std::min<int64_t>((n + 1 + 255) / 256, (int64_t)sm_count() * 8);
-  emb_offsets_kernel<<<g2, 256, 0, s>>>(keys_out, n, rows, offsets);
-  st = check_launch("oxc_embedding_bwd (offsets)");
+  return emb_sum_phase(dout, n, rows, cols, ws, L, dtable, nullptr, s);
+}
+
+size_t oxc_embedding_bwd_compact_workspace_size(int64_t n, int64_t rows, int64_t cols) {
+  if (n <= 0 || rows <= 0 || cols <= 0) return 0;
+  EmbLayout L;
+  if (emb_layout(n, rows, cols, &L, 1, true) != OXC_OK) return 0;
+  return L.total;
+}
+
+oxc_status oxc_embedding_bwd_compact(const float* dout, const int64_t* ids, int64_t n,
+                                     int64_t vocab_total, int64_t vocab_offset, int64_t rows,
+                                     int64_t cols, int32_t* out_ids, float* out_rows,
+                                     int64_t* count, int32_t shards, int64_t* shard_counts,
+                                     int32_t* err_flag, void* workspace, size_t workspace_bytes,
+                                     void* stream) {
+  const char* fn = "embedding backward (compact)";
+  oxc_status st = emb_check(fn, n, vocab_total, vocab_offset, rows, cols);
   if (st) return st;
-  const bool v4 = cols % 4 == 0 && aligned16(dout) && aligned16(dtable);
-  const int64_t nblocks = (n + kSplitP - 1) / kSplitP;
-  const unsigned grows = (unsigned)std::min<int64_t>(rows, (int64_t)sm_count() * 32);
-  // Each CTA takes one column chunk of a row (blockIdx.y): kEmbChunkThreads
-  // threads with one float4 (or four floats) each.  Small CTAs keep many rows'
-  // gathers in flight on every SM: on B200 at [32000, 4096] the VJP ran at
-  // 4.7 / 4.9 / 5.0 / 5.1 / 5.0 / 4.8 TB/s with 1024 / 512 / 256 / 128 / 64 / 32
-  // threads per CTA.
-  const int vpt = v4 ? 1 : 4, vw = v4 ? 4 : 1;
-  const int64_t per_thread = (int64_t)vpt * vw;
-  const int block = (int)std::min<int64_t>(
-      kEmbChunkThreads, std::max<int64_t>(32, ((cols / per_thread + 31) / 32) * 32));
-  const int64_t chunks = std::min<int64_t>(65535, (cols + block * per_thread - 1) / (block * per_thread));
-  const dim3 gsplit((unsigned)nblocks, (unsigned)chunks), grow(grows, (unsigned)chunks);
-  if (v4) {
-    emb_split_kernel<4, 1, kEmbChunkThreads><<<gsplit, block, 0, s>>>(
-        dout, keys_out, vals_out, offsets, n, rows, (int)cols, parts, (int64_t)1);
-    launch_dependent(emb_rows_kernel<4, 1, kEmbChunkThreads>, grow, block, s, dout, vals_out,
-                     offsets, (const float*)parts, rows, (int)cols, dtable, n, (int64_t)1);
-  } else {
-    emb_split_kernel<1, 4, kEmbChunkThreads><<<gsplit, block, 0, s>>>(
-        dout, keys_out, vals_out, offsets, n, rows, (int)cols, parts, (int64_t)1);
-    launch_dependent(emb_rows_kernel<1, 4, kEmbChunkThreads>, grow, block, s, dout, vals_out,
-                     offsets, (const float*)parts, rows, (int)cols, dtable, n, (int64_t)1);
+  if (shards < 0 || (shard_counts && shards == 0))
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: %d shards", fn, (int)shards);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!count) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: null count", fn);
+  if (n == 0 || rows == 0 || cols == 0) {
+    cudaError_t e = cudaMemsetAsync(count, 0, sizeof(int64_t), s);
+    if (e == cudaSuccess && shard_counts)
+      e = cudaMemsetAsync(shard_counts, 0, (size_t)shards * sizeof(int64_t), s);
+    return e == cudaSuccess ? OXC_OK : cuda_fail(e, "oxc_embedding_bwd_compact");
   }
-  return check_launch("oxc_embedding_bwd");
+  if (!dout || !ids || !out_ids || !out_rows)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: null pointer", fn);
+  EmbLayout L;
+  st = emb_layout(n, rows, cols, &L, 1, true);
+  if (st) return st;
+  if (!workspace || workspace_bytes < L.total)
+    return fail(OXC_ERR_INVALID_ARGUMENT,
+                "invalid argument: %s needs a %zu-byte workspace, got %zu", fn, L.total,
+                workspace_bytes);
+  char* ws = static_cast<char*>(workspace);
+  st = emb_sort_phase(ids, n, vocab_total, vocab_offset, rows, err_flag, ws, L, s);
+  if (st) return st;
+  int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
+  int32_t* present = reinterpret_cast<int32_t*>(ws + L.present);
+  int32_t* slot = reinterpret_cast<int32_t*>(ws + L.slot);
+  const unsigned gr = (unsigned)std::min<int64_t>((rows + 255) / 256, (int64_t)sm_count() * 8);
+  emb_present_kernel<<<gr, 256, 0, s>>>(offsets, rows, present);
+  st = check_launch("oxc_embedding_bwd_compact (present)");
+  if (st) return st;
+  size_t scan_bytes = L.scan_bytes;
+  cudaError_t e = cub::DeviceScan::ExclusiveSum(ws + L.scan, scan_bytes, present, slot, (int)rows, s);
+  if (e != cudaSuccess) return cuda_fail(e, "oxc_embedding_bwd_compact (scan)");
+  const unsigned gm = std::max<unsigned>(gr, (unsigned)((shards + 255) / 256));
+  emb_compact_meta_kernel<<<gm, 256, 0, s>>>(present, slot, rows, vocab_total, vocab_offset,
+                                             shards, out_ids, count, shard_counts);
+  st = check_launch("oxc_embedding_bwd_compact (meta)");
+  if (st) return st;
+  return emb_sum_phase(dout, n, rows, cols, ws, L, out_rows, slot, s);
+}
+
+size_t oxc_embedding_exchange_reduce_workspace_size(int32_t sources, int64_t shard_rows) {
+  if (sources <= 0 || shard_rows <= 0) return 0;
+  return align256((size_t)sources * (size_t)shard_rows * sizeof(int32_t));
+}
+
+oxc_status oxc_embedding_exchange_reduce(const int32_t* recv_ids, const float* recv_rows,
+                                         const int64_t* src_offsets, int32_t sources,
+                                         int64_t shard_lo, int64_t shard_rows, int64_t cols,
+                                         float* dshard, int32_t* err_flag, void* workspace,
+                                         size_t workspace_bytes, void* stream) {
+  const char* fn = "embedding gradient exchange";
+  if (sources <= 0 || shard_rows < 0 || cols < 0 || shard_lo < 0)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: bad sizes", fn);
+  if (shard_rows >= 0x7fffffff || cols > 0x7fffffff || (int64_t)sources * shard_rows >= 0x7fffffff)
+    return fail(OXC_ERR_NOT_IMPLEMENTED, "not implemented: %s: sizes beyond 2^31", fn);
+  if (shard_rows == 0 || cols == 0) return OXC_OK;
+  if (!src_offsets || !dshard || !recv_ids || !recv_rows)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: null pointer", fn);
+  const size_t need = oxc_embedding_exchange_reduce_workspace_size(sources, shard_rows);
+  if (!workspace || workspace_bytes < need)
+    return fail(OXC_ERR_INVALID_ARGUMENT,
+                "invalid argument: %s needs a %zu-byte workspace, got %zu", fn, need,
+                workspace_bytes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t* map = static_cast<int32_t*>(workspace);
+  cudaError_t e = cudaMemsetAsync(map, 0xff, (size_t)sources * shard_rows * sizeof(int32_t), s);
+  if (e != cudaSuccess) return cuda_fail(e, "oxc_embedding_exchange_reduce");
+  const unsigned gmap = (unsigned)sm_count() * 4;
+  emb_exchange_map_kernel<<<gmap, 256, 0, s>>>(recv_ids, src_offsets, sources, shard_lo,
+                                               shard_rows, map, err_flag);
+  oxc_status st = check_launch("oxc_embedding_exchange_reduce (map)");
+  if (st) return st;
+  const bool v4 = cols % 4 == 0 && aligned16(recv_rows) && aligned16(dshard);
+  const int64_t per = v4 ? cols / 4 : cols;
+  const unsigned chunks = (unsigned)std::min<int64_t>(65535, (per + 127) / 128);
+  const dim3 grid((unsigned)std::min<int64_t>(shard_rows, (int64_t)sm_count() * 32), chunks);
+  if (v4)
+    emb_exchange_reduce_kernel<4><<<grid, 128, 0, s>>>(recv_rows, map, sources, shard_rows,
+                                                       (int)cols, dshard);
+  else
+    emb_exchange_reduce_kernel<1><<<grid, 128, 0, s>>>(recv_rows, map, sources, shard_rows,
+                                                       (int)cols, dshard);
+  return check_launch("oxc_embedding_exchange_reduce");
 }
 
 oxc_status oxc_index_select(const oxc_view* x, int64_t dim, const int64_t* ids, int64_t n,
@@ -717,12 +954,14 @@ oxc_status oxc_index_select_bwd(const float* g, const int64_t* ids, int64_t n,
     emb_split_kernel<4, 1, kEmbChunkThreads><<<gsplit, block, 0, s>>>(
         g, keys_out, vals_out, offsets, n, len, (int)inner, parts, outer);
     launch_dependent(emb_rows_kernel<4, 1, kEmbChunkThreads>, grow, block, s, g, vals_out,
-                     offsets, (const float*)parts, len, (int)inner, gx, n, outer);
+                     offsets, (const float*)parts, len, (int)inner, gx, n, outer,
+                     (const int32_t*)nullptr);
   } else {
     emb_split_kernel<1, 4, kEmbChunkThreads><<<gsplit, block, 0, s>>>(
         g, keys_out, vals_out, offsets, n, len, (int)inner, parts, outer);
     launch_dependent(emb_rows_kernel<1, 4, kEmbChunkThreads>, grow, block, s, g, vals_out,
-                     offsets, (const float*)parts, len, (int)inner, gx, n, outer);
+                     offsets, (const float*)parts, len, (int)inner, gx, n, outer,
+                     (const int32_t*)nullptr);
   }
   return check_launch("oxc_index_select_bwd");
 }

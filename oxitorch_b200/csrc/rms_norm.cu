@@ -16,6 +16,8 @@
 // writes dx.  Both are HBM-bound; the VJP keeps the column accumulators for
 // dw in registers across the rows of a persistent CTA and finishes them with
 // one deterministic column sum over the per-CTA partials.
+#include <algorithm>
+
 #include "rowvec.cuh"
 
 namespace oxc {
@@ -149,6 +151,60 @@ __global__ void __launch_bounds__(MAXT) rms_bwd_kernel(
   }
 }
 
+// The REF-mode VJP as a streaming tile kernel.  With the rsqrt factor
+// detached, dx = (dy*w)*inv needs no row reduction, so a CTA takes a stripe of
+// blockDim.x float4 columns (blockIdx.x) over a block of rows (blockIdx.y):
+// every thread keeps U rows of x and dy loads in flight, streams dx out and
+// carries the dw partial of its four columns in registers; parts[blockIdx.y]
+// holds the stripe's partial, summed by the column finisher.  The same
+// per-element operations as rms_bwd_kernel; only the grouping of the dw sums
+// differs.
+template <int U>
+__global__ void __launch_bounds__(256) rms_bwd_stream_kernel(
+    const float4* __restrict__ x, const float4* __restrict__ w, const float* __restrict__ rstd,
+    const float4* __restrict__ dy, float4* __restrict__ dx, float4* __restrict__ parts,
+    int64_t rows, int64_t cols4, int64_t rows_per_cta) {
+  pdl_launch_dependents();  // the dweight finisher waits for this grid
+  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols4) return;
+  const int64_t r0 = (int64_t)blockIdx.y * rows_per_cta;
+  const int64_t r1 = min(rows, r0 + rows_per_cta);
+  const float4 wv = __ldg(w + c);
+  float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (int64_t r = r0; r < r1; r += U) {
+    float4 xv[U], gv[U];
+    float inv[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (r + u < r1) {
+        xv[u] = ld_stream(x + (r + u) * cols4 + c);
+        gv[u] = ld_stream(dy + (r + u) * cols4 + c);
+        inv[u] = __ldg(rstd + r + u);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (r + u < r1) {
+        const float i = inv[u];
+        acc.x = __fadd_rn(acc.x, __fmul_rn(gv[u].x, __fmul_rn(xv[u].x, i)));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(gv[u].y, __fmul_rn(xv[u].y, i)));
+        acc.z = __fadd_rn(acc.z, __fmul_rn(gv[u].z, __fmul_rn(xv[u].z, i)));
+        acc.w = __fadd_rn(acc.w, __fmul_rn(gv[u].w, __fmul_rn(xv[u].w, i)));
+        float4 o;
+        o.x = __fmul_rn(__fmul_rn(gv[u].x, wv.x), i);
+        o.y = __fmul_rn(__fmul_rn(gv[u].y, wv.y), i);
+        o.z = __fmul_rn(__fmul_rn(gv[u].z, wv.z), i);
+        o.w = __fmul_rn(__fmul_rn(gv[u].w, wv.w), i);
+        st_stream(dx + (r + u) * cols4 + c, o);
+      }
+    }
+  }
+  parts[(int64_t)blockIdx.y * cols4 + c] = acc;
+}
+
+constexpr int kRmsStreamThreads = 256;
+constexpr int kRmsStreamU = 4;
+
 // Number of persistent CTAs of the VJP: two per SM, at least 8 rows each.
 static int64_t rms_bwd_ctas(int64_t rows) {
   int64_t g = 2 * (int64_t)sm_count();
@@ -228,10 +284,33 @@ oxc_status oxc_rms_norm_bwd(const float* x, const float* w, const float* rstd, c
     return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: rms_norm backward: null pointer");
   const bool v4 = cols % 4 == 0 && aligned16(x) && aligned16(w) && aligned16(dy) &&
                   aligned16(dx) && aligned16(workspace);
+  float* parts = static_cast<float*>(workspace);
+  if (v4 && grad_mode == OXC_GRAD_REF) {
+    // streaming tile kernel: one wave of resident CTAs, the row blocks no more
+    // than the workspace's partial slots (rms_bwd_ctas)
+    const int64_t cols4 = cols / 4;
+    const int64_t gx = (cols4 + kRmsStreamThreads - 1) / kRmsStreamThreads;
+    const int block = (int)std::min<int64_t>(kRmsStreamThreads, ((cols4 + 31) / 32) * 32);
+    const int64_t resident =
+        (int64_t)sm_count() * occupancy((const void*)rms_bwd_stream_kernel<kRmsStreamU>, block, 0);
+    int64_t gy = std::max<int64_t>(1, resident / gx);
+    gy = std::min<int64_t>(gy, rms_bwd_ctas(rows));
+    const int64_t per = (rows + gy - 1) / gy;
+    gy = (rows + per - 1) / per;
+    if (gy > 65535 || (size_t)gy * cols * sizeof(float) > workspace_bytes)
+      return fail(OXC_ERR_OTHER, "internal: rms_norm backward partials exceed the workspace");
+    rms_bwd_stream_kernel<kRmsStreamU><<<dim3((unsigned)gx, (unsigned)gy), block, 0, s>>>(
+        reinterpret_cast<const float4*>(x), reinterpret_cast<const float4*>(w), rstd,
+        reinterpret_cast<const float4*>(dy), reinterpret_cast<float4*>(dx),
+        reinterpret_cast<float4*>(parts), rows, cols4, per);
+    st = check_launch("oxc_rms_norm_bwd");
+    if (st) return st;
+    launch_colsum_partials(parts, (int)gy, cols, dw, s);
+    return check_launch("oxc_rms_norm_bwd (dw)");
+  }
   RowGeom g = row_geom(cols, v4, 512);
   const int64_t ctas = rms_bwd_ctas(rows);
   const int64_t chunk = (rows + ctas - 1) / ctas;
-  float* parts = static_cast<float*>(workspace);
 #define LAUNCH(VW, VPT, MAXT)                                                                \
   do {                                                                                       \
     if (grad_mode == OXC_GRAD_REF)                                                           \

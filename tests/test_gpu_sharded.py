@@ -90,6 +90,92 @@ def test_sharded_layers_single_process():
         S.embedding(ids, table[:10], 50)
 
 
+def _compact(ids_np, dout_np, vocab, shards):
+    """oxc_embedding_bwd_compact on one device: (ids, rows, count, shard counts)."""
+    import torch
+    from oxitorch_b200 import _native as N
+    from oxitorch_b200 import functional as F
+    L = N.load()
+    n, d = dout_np.shape
+    ids, dout = _dev(ids_np), _dev(dout_np)
+    cap = max(1, min(n, vocab))
+    out_ids = torch.empty(cap, dtype=torch.int32, device="cuda")
+    out_rows = torch.empty(cap, d, device="cuda")
+    count = torch.empty(1, dtype=torch.int64, device="cuda")
+    sc = torch.empty(shards, dtype=torch.int64, device="cuda")
+    flag = torch.zeros(4, dtype=torch.int32, device="cuda")
+    ws = F._workspace(L.oxc_embedding_bwd_compact_workspace_size(n, vocab, d), dout.device)
+    N.check(L.oxc_embedding_bwd_compact(dout.data_ptr(), ids.data_ptr(), n, vocab, 0, vocab, d,
+                                        out_ids.data_ptr(), out_rows.data_ptr(), count.data_ptr(),
+                                        shards, sc.data_ptr(), flag.data_ptr(), ws.data_ptr(),
+                                        ws.numel(), F._stream()))
+    k = int(count.item())
+    return _host(out_ids)[:k], _host(out_rows)[:k], k, _host(sc)
+
+
+def test_embedding_sparse_exchange_emulated(oracle):
+    """The sparse gradient exchange of a replicated table, its G ranks emulated
+    on one GPU: each token shard's compact VJP is the dense VJP's touched rows
+    (bit-exact) with the right per-shard counts; the owner's
+    oxc_embedding_exchange_reduce of the rows routed to it gives the whole
+    batch's gradient rows -- bit-exact where one rank touched the row, within
+    rtol 1e-4 (duplicate-id accumulation) elsewhere."""
+    import torch
+    from oxitorch_b200 import _native as N
+    from oxitorch_b200 import functional as F
+    from oxitorch_b200 import sharded as S
+    rng = np.random.default_rng(24)
+    V, D, n, G = 3000, 512, 20000, 4
+    ids = np.minimum(rng.zipf(1.1, n) - 1, V - 1).astype(np.int64)
+    ids[::97] -= V  # negative ids count from the end
+    dout = rng.standard_normal((n, D)).astype(np.float32)
+    res = np.where(ids < 0, ids + V, ids)
+    bounds = [V * s // G for s in range(G + 1)]
+    sends = []
+    for g in range(G):
+        lo, hi = S.shard_range(n, g, G)
+        oid, orow, k, sc = _compact(ids[lo:hi], dout[lo:hi], V, G)
+        u = np.unique(res[lo:hi])
+        assert k == u.size and np.array_equal(oid, u)
+        dense, _ = F.embedding_bwd(_dev(ids[lo:hi]), _dev(dout[lo:hi]), V)
+        assert_bitexact(orow, _host(dense)[u], f"compact rows of rank {g}")
+        assert list(sc) == [int(((u >= bounds[s]) & (u < bounds[s + 1])).sum()) for s in range(G)]
+        sends.append((oid, orow, sc))
+    full = oracle.scatter_index_select(dout, 0, [int(i) for i in res], (V, D))
+    L = N.load()
+    for s in range(G):
+        rid, rrow, off = [], [], [0]
+        for oid, orow, sc in sends:  # source order
+            a = int(sc[:s].sum())
+            rid.append(oid[a:a + sc[s]])
+            rrow.append(orow[a:a + sc[s]])
+            off.append(off[-1] + int(sc[s]))
+        rid, rrow = np.concatenate(rid).astype(np.int32), np.concatenate(rrow)
+        lo, rows = S.vocab_shard(V, s, G)
+        dshard = torch.empty(rows, D, device="cuda")
+        flag = torch.zeros(4, dtype=torch.int32, device="cuda")
+        ws = F._workspace(L.oxc_embedding_exchange_reduce_workspace_size(G, rows), dshard.device)
+        N.check(L.oxc_embedding_exchange_reduce(
+            _dev(rid).data_ptr(), _dev(rrow).data_ptr(), _dev(np.array(off, np.int64)).data_ptr(),
+            G, lo, rows, D, dshard.data_ptr(), flag.data_ptr(), ws.data_ptr(), ws.numel(),
+            F._stream()))
+        got, want = _host(dshard), full[lo:lo + rows]
+        touched_by = np.zeros(rows, np.int64)
+        for g in range(G):
+            glo, ghi = S.shard_range(n, g, G)
+            u = np.unique(res[glo:ghi])
+            u = u[(u >= lo) & (u < lo + rows)] - lo
+            touched_by[u] += 1
+        counts = np.bincount(res, minlength=V)[lo:lo + rows]
+        exact = (touched_by <= 1) & (counts <= 128)
+        assert_bitexact(got[exact], want[exact], f"shard {s} rows touched by one rank")
+        scale = np.zeros((V, D))
+        np.add.at(scale, res, np.abs(dout.astype(np.float64)))
+        assert_close(got, want, rtol=1e-4, atol=1e-6 * np.maximum(scale[lo:lo + rows], 1.0),
+                     what=f"shard {s}", strict_atol=1e-6 * np.maximum(scale[lo:lo + rows], 1.0))
+        assert int(flag[0]) == 0
+
+
 # ---- real NCCL ranks ---------------------------------------------------------------------
 
 def _free_port():
@@ -177,6 +263,17 @@ def _nccl_body(rank, world, dev):
     mine = S.reduce_scatter_rows(parts_t[rank].clone())
     lo_t, hi_t = S.shard_range(1000, rank, world)
     assert_bitexact(_host(mine), _host(sum(parts_t))[lo_t:hi_t], "reduce-scattered rows")
+    # sparse exchange of a replicated table's gradient (token-sharded ids):
+    # this rank's vocab rows of the whole batch's gradient
+    v2, d2, n2 = 2000, 256, 12000
+    ids2 = np.minimum(rng.zipf(1.1, n2) - 1, v2 - 1).astype(np.int64)
+    dout2 = rng.standard_normal((n2, d2)).astype(np.float32)
+    lo2, hi2 = S.shard_range(n2, rank, world)
+    dsh = S.embedding_grad(_dev(ids2[lo2:hi2], dev), _dev(dout2[lo2:hi2], dev), v2)
+    full2, _ = F.embedding_bwd(_dev(ids2, dev), _dev(dout2, dev), v2)
+    voff, vrows = S.vocab_shard(v2, rank, world)
+    assert_close(_host(dsh), _host(full2)[voff:voff + vrows], rtol=1e-4, atol=1e-4,
+                 what="sparse-exchanged dtable shard")
     # global sum of squares over row shards
     gsh = _dev(x[lo % 100:lo % 100 + 50], dev)
     tot = S.sum_squares([gsh])

@@ -197,6 +197,44 @@ def _embedding_vocab_sharded(rank, world):
     return None
 
 
+def _embedding_sparse_exchange(rank, world):
+    """The sparse exchange of a replicated table's gradient (token-sharded
+    ids): each rank keeps the touched rows of its tokens' VJP (the oracle's
+    position-order sums), sends each to its vocab shard's owner with
+    S.exchange_rows, and the owner sums what arrives in rank order (what
+    oxc_embedding_exchange_reduce does on a GPU).  Rows touched by one rank
+    equal the whole batch's VJP bit for bit; the rest within rtol 1e-4."""
+    from oracle import oxiref as O
+    from oxitorch_b200 import sharded as S
+    rng = np.random.default_rng(15)
+    V, D, n = 23, 5, 60
+    ids = np.minimum(rng.zipf(1.3, n) - 1, V - 1).astype(np.int64)
+    dout = rng.standard_normal((n, D)).astype(np.float32)
+    lo, hi = S.shard_range(n, rank, world)
+    local = O.scatter_index_select(dout[lo:hi], 0, [int(i) for i in ids[lo:hi]], (V, D))
+    touched = np.unique(ids[lo:hi]).astype(np.int32)  # ascending: the compact order
+    bounds = [V * s // world for s in range(world + 1)]
+    counts = torch.tensor([int(((touched >= bounds[s]) & (touched < bounds[s + 1])).sum())
+                           for s in range(world)])
+    rid, rrows, rc = S.exchange_rows(torch.from_numpy(touched), torch.from_numpy(local[touched]),
+                                     counts)
+    assert sum(rc) == rid.numel() == rrows.shape[0]
+    own_lo, own_rows = S.vocab_shard(V, rank, world)
+    got = np.zeros((own_rows, D), np.float32)
+    src = np.repeat(np.arange(world), rc)
+    for s in range(world):  # rank order
+        for i in np.nonzero(src == s)[0]:
+            v = int(rid[i]) - own_lo
+            assert 0 <= v < own_rows
+            got[v] = got[v] + rrows[i].numpy()
+    full = O.scatter_index_select(dout, 0, [int(i) for i in ids], (V, D))[own_lo:own_lo + own_rows]
+    owners = [set(ids[S.shard_range(n, r, world)[0]:S.shard_range(n, r, world)[1]]) for r in range(world)]
+    single = np.array([sum((own_lo + v) in o for o in owners) <= 1 for v in range(own_rows)])
+    assert np.array_equal(got[single], full[single])
+    np.testing.assert_allclose(got, full, rtol=1e-4, atol=1e-6)
+    return None
+
+
 def _sum_squares(rank, world):
     """Whole-tensor sum of squares over row shards: f64 partials, summed."""
     from oxitorch_b200 import sharded as S
@@ -247,6 +285,11 @@ def test_cross_entropy_global_mean(world):
 @pytest.mark.parametrize("world", [2, 3])
 def test_embedding_vocab_shards_sum_exact(world):
     _run(world, "_embedding_vocab_sharded")
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_embedding_sparse_gradient_exchange(world):
+    _run(world, "_embedding_sparse_exchange")
 
 
 def test_sum_squares_over_shards():
