@@ -397,6 +397,34 @@ oxc_status oxc_embedding_exchange_reduce(const int32_t* recv_ids, const float* r
                                          float* dshard, int32_t* err_flag, void* workspace,
                                          size_t workspace_bytes, void* stream);
 
+/* ---- multi-GPU collectives for a native host ---------------------------------
+ * No counterpart in the reference (it has no distributed runtime; plan.md:325
+ * lists one as a stretch goal).  The exchanges of the sharded layer path --
+ * the all-reduce of weight-gradient and loss partials (f32) and of sums of
+ * squares (f64), the reduce-scatter of a table gradient, and the variable
+ * all-to-all of the sparse embedding exchange -- for a host that does not run
+ * Python.  NCCL over NVLink / NVSwitch, loaded at run time from libnccl.so.2
+ * (OXC_ERR_OTHER when it cannot be loaded).  One communicator per process and
+ * GPU: rank 0 makes an id (oxc_comm_unique_id), the host hands its
+ * OXC_COMM_ID_BYTES bytes to every rank out of band, and each rank calls
+ * oxc_comm_init with its device current.  Every rank issues the same calls in
+ * the same order; each call is asynchronous on `stream`.  oxc_comm_alltoallv
+ * sends send_counts[p] elements of elem_bytes to rank p (consecutive in
+ * `send`) and receives recv_counts[p] from it; both count arrays are on the
+ * host. */
+typedef struct oxc_comm oxc_comm;
+#define OXC_COMM_ID_BYTES 128
+oxc_status oxc_comm_unique_id(uint8_t* id);
+oxc_status oxc_comm_init(oxc_comm** comm, const uint8_t* id, int32_t world, int32_t rank);
+oxc_status oxc_comm_destroy(oxc_comm* comm);
+oxc_status oxc_comm_allreduce_sum_f32(oxc_comm* comm, float* buf, int64_t n, void* stream);
+oxc_status oxc_comm_allreduce_sum_f64(oxc_comm* comm, double* buf, int64_t n, void* stream);
+oxc_status oxc_comm_reduce_scatter_f32(oxc_comm* comm, const float* in, float* out,
+                                       int64_t count_per_rank, void* stream);
+oxc_status oxc_comm_alltoallv(oxc_comm* comm, const void* send, const int64_t* send_counts,
+                              void* recv, const int64_t* recv_counts, int64_t elem_bytes,
+                              void* stream);
+
 /* ---- index_select along any dim, and its VJP --------------------------------
  * oxc_index_select replaces Tensor::index_select (crates/oxi-tensor/src/lib.rs:
  * 665-703) for any dim and any strides of x: out (dense row-major, x's shape

@@ -122,6 +122,13 @@ SIGNATURES = {
     "oxc_embedding_exchange_reduce_workspace_size": (_SZ, [_I32, _I64]),
     "oxc_embedding_exchange_reduce": (_I32, [_P, _P, _P, _I32, _I64, _I64, _I64, _P, _P, _P, _SZ,
                                              _P]),
+    "oxc_comm_unique_id": (_I32, [_P]),
+    "oxc_comm_init": (_I32, [ctypes.POINTER(_P), _P, _I32, _I32]),
+    "oxc_comm_destroy": (_I32, [_P]),
+    "oxc_comm_allreduce_sum_f32": (_I32, [_P, _P, _I64, _P]),
+    "oxc_comm_allreduce_sum_f64": (_I32, [_P, _P, _I64, _P]),
+    "oxc_comm_reduce_scatter_f32": (_I32, [_P, _P, _P, _I64, _P]),
+    "oxc_comm_alltoallv": (_I32, [_P, _P, _P, _P, _P, _I64, _P]),
     "oxc_index_select": (_I32, [_VP, _I64, _P, _I64, _P, _P, _P]),
     "oxc_gather_dim0": (_I32, [_VP, _P, _I64, _P, _P, _P]),
     "oxc_index_select_bwd_workspace_size": (_SZ, [_P, _I32, _I64, _I64]),

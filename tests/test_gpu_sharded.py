@@ -155,10 +155,12 @@ def test_embedding_sparse_exchange_emulated(oracle):
         dshard = torch.empty(rows, D, device="cuda")
         flag = torch.zeros(4, dtype=torch.int32, device="cuda")
         ws = F._workspace(L.oxc_embedding_exchange_reduce_workspace_size(G, rows), dshard.device)
+        # device copies held in names: a temporary freed before the launch
+        # could hand its memory to the next copy
+        d_rid, d_rrow, d_off = _dev(rid), _dev(rrow), _dev(np.array(off, np.int64))
         N.check(L.oxc_embedding_exchange_reduce(
-            _dev(rid).data_ptr(), _dev(rrow).data_ptr(), _dev(np.array(off, np.int64)).data_ptr(),
-            G, lo, rows, D, dshard.data_ptr(), flag.data_ptr(), ws.data_ptr(), ws.numel(),
-            F._stream()))
+            d_rid.data_ptr(), d_rrow.data_ptr(), d_off.data_ptr(), G, lo, rows, D,
+            dshard.data_ptr(), flag.data_ptr(), ws.data_ptr(), ws.numel(), F._stream()))
         got, want = _host(dshard), full[lo:lo + rows]
         touched_by = np.zeros(rows, np.int64)
         for g in range(G):
@@ -208,6 +210,7 @@ def _nccl_rank(rank, world, port, q):
 
 def _nccl_body(rank, world, dev):
     import torch
+    import torch.distributed as dist
     from oxitorch_b200 import functional as F
     from oxitorch_b200 import sharded as S
     rng = np.random.default_rng(23)  # the same data on every rank
@@ -274,11 +277,47 @@ def _nccl_body(rank, world, dev):
     voff, vrows = S.vocab_shard(v2, rank, world)
     assert_close(_host(dsh), _host(full2)[voff:voff + vrows], rtol=1e-4, atol=1e-4,
                  what="sparse-exchanged dtable shard")
+    # the C-ABI communicator (oxc_comm_*), the route of a native host
+    import ctypes
+    from oxitorch_b200 import _native as N
+    L = N.load()
+    idbuf = (ctypes.c_uint8 * 128)()
+    if rank == 0:
+        N.check(L.oxc_comm_unique_id(idbuf))
+    obj = [bytes(idbuf)]
+    dist.broadcast_object_list(obj, src=0)
+    idbuf = (ctypes.c_uint8 * 128).from_buffer_copy(obj[0])
+    comm = ctypes.c_void_p()
+    N.check(L.oxc_comm_init(ctypes.byref(comm), idbuf, world, rank))
+    s_ = torch.cuda.current_stream().cuda_stream
+    a = _dev(np.arange(4099, dtype=np.float32) * (rank + 1), dev)
+    b = a.clone()
+    N.check(L.oxc_comm_allreduce_sum_f32(comm, a.data_ptr(), a.numel(), s_))
+    dist.all_reduce(b)
+    assert_bitexact(_host(a), _host(b), "oxc_comm_allreduce_sum_f32")
+    d64 = torch.full((7,), float(rank + 1), dtype=torch.float64, device=dev)
+    N.check(L.oxc_comm_allreduce_sum_f64(comm, d64.data_ptr(), 7, s_))
+    assert float(d64[0]) == world * (world + 1) / 2
+    rs_in = _dev(np.arange(world * 33, dtype=np.float32), dev)
+    rs_out = torch.empty(33, device=dev)
+    N.check(L.oxc_comm_reduce_scatter_f32(comm, rs_in.data_ptr(), rs_out.data_ptr(), 33, s_))
+    assert_bitexact(_host(rs_out), world * np.arange(rank * 33, rank * 33 + 33, dtype=np.float32),
+                    "oxc_comm_reduce_scatter_f32")
+    # all-to-all: rank r sends r + p + 1 int32 values (all = 100 r + p) to rank p
+    sc = [rank + p + 1 for p in range(world)]
+    rc = [p + rank + 1 for p in range(world)]
+    send = _dev(np.concatenate([np.full(c, 100 * rank + p, np.int32) for p, c in enumerate(sc)]), dev)
+    recv = torch.empty(sum(rc), dtype=torch.int32, device=dev)
+    N.check(L.oxc_comm_alltoallv(comm, send.data_ptr(), (ctypes.c_int64 * world)(*sc),
+                                 recv.data_ptr(), (ctypes.c_int64 * world)(*rc), 4, s_))
+    want = np.concatenate([np.full(c, 100 * p + rank, np.int32) for p, c in enumerate(rc)])
+    assert np.array_equal(_host(recv), want)
+    torch.cuda.synchronize()
+    N.check(L.oxc_comm_destroy(comm))
     # global sum of squares over row shards
     gsh = _dev(x[lo % 100:lo % 100 + 50], dev)
     tot = S.sum_squares([gsh])
     parts = [None] * world
-    import torch.distributed as dist
     dist.all_gather_object(parts, float(np.sum(x[lo % 100:lo % 100 + 50].astype(np.float64) ** 2)))
     assert_close(np.array([tot.item()]), np.array([sum(parts)]), rtol=1e-9, atol=0,
                  what="global sum of squares")
