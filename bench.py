@@ -438,6 +438,8 @@ class Workload:
     launches = 0           # our kernels per step
     ROWS = ("rows", "rows")  # (attribute holding the rows per GPU step, unit)
     CONFIG = None          # BASELINE config index of the inputs
+    GRAPHS = True          # fwd/bwd phases replayed as CUDA graphs in the timed loop
+    VARIANTS = 2           # distinct steps (buffer slots) a graph is captured for
 
     def __init__(self, dev, rank, world, args, inp=None, mode="weak"):
         import torch
@@ -454,6 +456,10 @@ class Workload:
         if work is not None:
             work.wait()
             self.pending[self.slot] = None
+
+    def graph_key(self):
+        """Identifies the buffers of the current step (its captured graphs)."""
+        return self.slot
 
     def drain(self):
         for k in range(2):
@@ -585,9 +591,17 @@ class Rms(Workload):
         self.fwd_bytes = R * (8 * C + 4) + 4 * C
         self.bwd_bytes = R * (12 * C + 4) + 8 * C
 
+    VARIANTS = 6  # 3 input sets x 2 gradient slots
+
+    def begin(self, i):
+        super().begin(i)
+        self.cur = i % self.SETS  # the set this step reads
+
+    def graph_key(self):
+        return (self.cur, self.slot)
+
     def fwd(self, x=None):
-        if x is None:  # the timed loop: next set
-            self.cur = (self.cur + 1) % self.SETS
+        if x is None:  # the timed loop: this step's set
             x, _, y, _ = self.sets[self.cur]
         else:          # e2e: the uploaded input, set 0's outputs
             y = self.sets[0][2]
@@ -818,6 +832,7 @@ class EmbeddingVocab(Workload):
     KERNEL = "emb_gather_kernel + NCCL all-reduce of the output (the step is communication-bound)"
     dominant = "fwd"
     launches = 9
+    GRAPHS = False  # the forward holds the output all-reduce
     ROWS = ("n", "tokens")
 
     def __init__(self, dev, rank, world, args, inp, mode="strong"):
@@ -1064,6 +1079,7 @@ class Optim(Workload):
     KERNEL = "adam_kernel (AdamW step)"
     dominant = "fwd"
     launches = 2
+    GRAPHS = False  # the step counter (bias corrections) changes every step
     E2E_LARGE = True
     ROWS = ("n", "elements")
 
@@ -1129,6 +1145,7 @@ class Loader(Workload):
     KERNEL = "image_epoch_kernel (gather + crop + flip + normalize) + label gather"
     dominant = "bwd"
     launches = 3
+    GRAPHS = False  # epochs upload their plans from the host
     ROWS = ("n", "samples")
 
     def __init__(self, dev, rank, world, args, inp=None, mode="weak"):
@@ -1209,12 +1226,20 @@ def time_steps(wl, steps, warmup, world, local_rank, exchange=True, solo=False):
     if multi:
         import torch.distributed as dist
 
+    graphs = capture_graphs(wl) if wl.GRAPHS else None
+
     def one(i, ev):
         wl.begin(i)
         ev[0].record(stream)
-        wl.fwd()
-        ev[1].record(stream)
-        wl.bwd()
+        if graphs:
+            key = wl.graph_key()
+            graphs[("fwd", key)].replay()
+            ev[1].record(stream)
+            graphs[("bwd", key)].replay()
+        else:
+            wl.fwd()
+            ev[1].record(stream)
+            wl.bwd()
         ev[2].record(stream)
         if exchange:
             wl.exchange()
@@ -1246,7 +1271,35 @@ def time_steps(wl, steps, warmup, world, local_rank, exchange=True, solo=False):
     bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in events)
     if multi:
         ms = _max_over_ranks(torch, wl.dev, world, ms)
+    wl.graphs_used = bool(graphs)
     return ms / steps, fwd_ms, bwd_ms, clocks
+
+
+def capture_graphs(wl):
+    """One CUDA graph per phase (fwd, bwd) and step variant, so the timed loop
+    launches each phase with one replay instead of a Python call per kernel
+    (configs whose steps last tens of microseconds are otherwise bound by the
+    host).  The kernels and their launch geometry are exactly the eager ones.
+    Returns None (eager launches) if a capture fails."""
+    torch = wl.torch
+    stream = torch.cuda.current_stream()
+    graphs = {}
+    try:
+        for i in range(wl.VARIANTS):
+            wl.begin(i)
+            key = wl.graph_key()
+            for phase, fn in (("fwd", wl.fwd), ("bwd", wl.bwd)):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream, capture_error_mode="thread_local"):
+                    fn()
+                graphs[(phase, key)] = g
+        wl.drain()
+        torch.cuda.synchronize()
+        return graphs
+    except Exception as e:  # noqa: BLE001 -- reported, and the loop runs eagerly
+        log(f"graph capture failed for {type(wl).__name__} ({e}); launching eagerly")
+        torch.cuda.synchronize()
+        return None
 
 
 def exchange_check(wl):
@@ -1320,6 +1373,9 @@ def measure(name, args, rank, world, local_rank, inp, steps, warmup, mode="weak"
         "gpu_launches": wl.launches * steps,
         "clocks": clocks,
     }
+    rep["config"]["launch"] = ("each phase (forward, VJP) replayed as a CUDA graph of the same "
+                               "kernels, one per step variant" if wl.graphs_used
+                               else "eager launches through the C ABI")
     if prof.get("fwd_dram_bytes_per_launch"):
         rep["roofline"]["fwd_dram_gbs"] = prof["fwd_dram_bytes_per_launch"] / (fwd_ms * 1e-3) / 1e9
     if check is not None:
@@ -1365,6 +1421,14 @@ def strong_scaling(name, args, rank, world, local_rank, inp, steps, warmup):
 def run_ours(args, rank, world, local_rank):
     import torch
     torch.cuda.set_device(local_rank)
+    # every launch of the run goes to one non-default stream, which CUDA graphs
+    # can be captured on
+    with torch.cuda.stream(torch.cuda.Stream()):
+        _run_ours(args, rank, world, local_rank)
+
+
+def _run_ours(args, rank, world, local_rank):
+    import torch
     dev = torch.device("cuda", local_rank)
     name = args.workload
     cls = WORKLOADS[name]
