@@ -427,6 +427,18 @@ def _shard(n, rank, world, mode):
     return shard_range(n, rank, world)
 
 
+class _EventWait:
+    """A pending exchange recorded as an event: wait() orders the current
+    stream after it (the interface of an async collective's work)."""
+
+    def __init__(self, event):
+        self.event = event
+
+    def wait(self):
+        import torch
+        torch.cuda.current_stream().wait_event(self.event)
+
+
 class Workload:
     """Inputs resident on the device; fwd()/bwd() launch the path's kernels on
     the current stream; exchange() issues the step's data-parallel collective
@@ -742,28 +754,21 @@ class Embedding(Workload):
             self.world = 1  # the single-GPU VJP, no exchange
             self.dtable = t.empty_like(self.table)
             self.ws_bytes = self.L.oxc_embedding_bwd_workspace_size(n, self.v, self.d)
+            self.ws = t.empty(max(self.ws_bytes, 16), dtype=t.uint8, device=dev)
             self.bwd_bytes = n * 8 + n * self.d * 4 + self.v * self.d * 4
         else:
             # token-sharded, replicated table: the compact VJP (touched rows),
             # an all-to-all of those rows to their vocab shard's owner, and the
-            # owner's rank-order sum into its dense shard of the gradient
-            from oxitorch_b200.sharded import vocab_shard
-            self.shard_lo, self.shard_rows = vocab_shard(self.v, rank, world)
-            cap = min(n, self.v)
-            self.c_ids = t.empty(cap, dtype=t.int32, device=dev)
-            self.c_rows = t.empty(cap, self.d, device=dev)
-            self.count = t.empty(1, dtype=t.int64, device=dev)
-            self.shard_counts = t.empty(world, dtype=t.int64, device=dev)
-            self.dshard = t.empty(self.shard_rows, self.d, device=dev)
-            self.ws_bytes = self.L.oxc_embedding_bwd_compact_workspace_size(n, self.v, self.d)
-            self.ws2_bytes = self.L.oxc_embedding_exchange_reduce_workspace_size(
-                world, self.shard_rows)
-            self.ws2 = t.empty(max(self.ws2_bytes, 16), dtype=t.uint8, device=dev)
+            # owner's rank-order sum into its dense shard of the gradient, on a
+            # communication stream that overlaps the next step's forward
+            from oxitorch_b200.sharded import SparseGradExchange
+            self.GRAPHS = False  # the VJP exchanges its counts with the other ranks
+            self.ex = SparseGradExchange(n, self.v, self.d, dev, slots=2)
+            self.dshard = self.ex.dshard[0]
             self.launches = 14  # + present, scan (2), meta, map, reduce (and NCCL's)
             # this rank's share of the job's bytes: its tokens' ids and dout,
             # and its shard of the dense table gradient
-            self.bwd_bytes = n * 8 + n * self.d * 4 + self.shard_rows * self.d * 4
-        self.ws = t.empty(max(self.ws_bytes, 16), dtype=t.uint8, device=dev)
+            self.bwd_bytes = n * 8 + n * self.d * 4 + self.ex.shard_rows * self.d * 4
 
     def fwd(self, dout=None):
         self.N.check(self.L.oxc_embedding_fwd(self.table.data_ptr(), self.ids.data_ptr(),
@@ -778,25 +783,13 @@ class Embedding(Workload):
                                                   self.v, self.d, self.flag.data_ptr(),
                                                   self.ws.data_ptr(), self.ws_bytes, self.s))
             return
-        self.N.check(self.L.oxc_embedding_bwd_compact(
-            dout.data_ptr(), self.ids.data_ptr(), self.n, self.v, 0, self.v, self.d,
-            self.c_ids.data_ptr(), self.c_rows.data_ptr(), self.count.data_ptr(), self.world,
-            self.shard_counts.data_ptr(), self.flag.data_ptr(), self.ws.data_ptr(),
-            self.ws_bytes, self.s))
+        self.ex.vjp(self.ids, dout, self.slot)
 
     def exchange(self):
         if self.world == 1:
             return
-        from oxitorch_b200 import sharded
-        rid, rrows, rc = sharded.exchange_rows(self.c_ids, self.c_rows, self.shard_counts)
-        off = [0]
-        for c in rc:
-            off.append(off[-1] + c)
-        src_off = self.torch.tensor(off, dtype=self.torch.int64).to(self.dev, non_blocking=True)
-        self.N.check(self.L.oxc_embedding_exchange_reduce(
-            rid.data_ptr(), rrows.data_ptr(), src_off.data_ptr(), self.world, self.shard_lo,
-            self.shard_rows, self.d, self.dshard.data_ptr(), self.flag.data_ptr(),
-            self.ws2.data_ptr(), self.ws2_bytes, self.s))
+        _, done = self.ex.exchange(self.slot)
+        self.pending[self.slot] = _EventWait(done)
 
     def e2e_io(self):
         return [self.dout], [self.out, self.dtable if self.world == 1 else self.dshard]

@@ -390,6 +390,19 @@ oxc_status oxc_embedding_bwd_compact(const float* dout, const int64_t* ids, int6
                                      int64_t* count, int32_t shards, int64_t* shard_counts,
                                      int32_t* err_flag, void* workspace, size_t workspace_bytes,
                                      void* stream);
+/* The compact VJP in two calls, so the per-shard counts can cross ranks while
+ * the sums run: _plan sorts the ids and writes out_ids, count and
+ * shard_counts (a few microseconds of work); _sum then writes out_rows.  Both
+ * take the same workspace, which carries the plan to the sums, and run in that
+ * order (same stream, or ordered by an event). */
+oxc_status oxc_embedding_bwd_compact_plan(const int64_t* ids, int64_t n, int64_t vocab_total,
+                                          int64_t vocab_offset, int64_t rows, int64_t cols,
+                                          int32_t* out_ids, int64_t* count, int32_t shards,
+                                          int64_t* shard_counts, int32_t* err_flag,
+                                          void* workspace, size_t workspace_bytes, void* stream);
+oxc_status oxc_embedding_bwd_compact_sum(const float* dout, int64_t n, int64_t rows, int64_t cols,
+                                         float* out_rows, void* workspace,
+                                         size_t workspace_bytes, void* stream);
 size_t oxc_embedding_exchange_reduce_workspace_size(int32_t sources, int64_t shard_rows);
 oxc_status oxc_embedding_exchange_reduce(const int32_t* recv_ids, const float* recv_rows,
                                          const int64_t* src_offsets, int32_t sources,

@@ -119,6 +119,9 @@ SIGNATURES = {
     "oxc_embedding_bwd_compact_workspace_size": (_SZ, [_I64, _I64, _I64]),
     "oxc_embedding_bwd_compact": (_I32, [_P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _I32,
                                          _P, _P, _P, _SZ, _P]),
+    "oxc_embedding_bwd_compact_plan": (_I32, [_P, _I64, _I64, _I64, _I64, _I64, _P, _P, _I32, _P,
+                                              _P, _P, _SZ, _P]),
+    "oxc_embedding_bwd_compact_sum": (_I32, [_P, _I64, _I64, _I64, _P, _P, _SZ, _P]),
     "oxc_embedding_exchange_reduce_workspace_size": (_SZ, [_I32, _I64]),
     "oxc_embedding_exchange_reduce": (_I32, [_P, _P, _P, _I32, _I64, _I64, _I64, _P, _P, _P, _SZ,
                                              _P]),

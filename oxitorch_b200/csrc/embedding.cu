@@ -691,12 +691,11 @@ size_t oxc_embedding_bwd_compact_workspace_size(int64_t n, int64_t rows, int64_t
   return L.total;
 }
 
-oxc_status oxc_embedding_bwd_compact(const float* dout, const int64_t* ids, int64_t n,
-                                     int64_t vocab_total, int64_t vocab_offset, int64_t rows,
-                                     int64_t cols, int32_t* out_ids, float* out_rows,
-                                     int64_t* count, int32_t shards, int64_t* shard_counts,
-                                     int32_t* err_flag, void* workspace, size_t workspace_bytes,
-                                     void* stream) {
+oxc_status oxc_embedding_bwd_compact_plan(const int64_t* ids, int64_t n, int64_t vocab_total,
+                                          int64_t vocab_offset, int64_t rows, int64_t cols,
+                                          int32_t* out_ids, int64_t* count, int32_t shards,
+                                          int64_t* shard_counts, int32_t* err_flag,
+                                          void* workspace, size_t workspace_bytes, void* stream) {
   const char* fn = "embedding backward (compact)";
   oxc_status st = emb_check(fn, n, vocab_total, vocab_offset, rows, cols);
   if (st) return st;
@@ -710,7 +709,7 @@ oxc_status oxc_embedding_bwd_compact(const float* dout, const int64_t* ids, int6
       e = cudaMemsetAsync(shard_counts, 0, (size_t)shards * sizeof(int64_t), s);
     return e == cudaSuccess ? OXC_OK : cuda_fail(e, "oxc_embedding_bwd_compact");
   }
-  if (!dout || !ids || !out_ids || !out_rows)
+  if (!ids || !out_ids)
     return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: null pointer", fn);
   EmbLayout L;
   st = emb_layout(n, rows, cols, &L, 1, true);
@@ -735,9 +734,45 @@ oxc_status oxc_embedding_bwd_compact(const float* dout, const int64_t* ids, int6
   const unsigned gm = std::max<unsigned>(gr, (unsigned)((shards + 255) / 256));
   emb_compact_meta_kernel<<<gm, 256, 0, s>>>(present, slot, rows, vocab_total, vocab_offset,
                                              shards, out_ids, count, shard_counts);
-  st = check_launch("oxc_embedding_bwd_compact (meta)");
+  return check_launch("oxc_embedding_bwd_compact (meta)");
+}
+
+oxc_status oxc_embedding_bwd_compact_sum(const float* dout, int64_t n, int64_t rows, int64_t cols,
+                                         float* out_rows, void* workspace,
+                                         size_t workspace_bytes, void* stream) {
+  const char* fn = "embedding backward (compact sums)";
+  oxc_status st = emb_check(fn, n, rows, 0, rows, cols);
   if (st) return st;
-  return emb_sum_phase(dout, n, rows, cols, ws, L, out_rows, slot, s);
+  if (n == 0 || rows == 0 || cols == 0) return OXC_OK;
+  if (!dout || !out_rows)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: null pointer", fn);
+  EmbLayout L;
+  st = emb_layout(n, rows, cols, &L, 1, true);
+  if (st) return st;
+  if (!workspace || workspace_bytes < L.total)
+    return fail(OXC_ERR_INVALID_ARGUMENT,
+                "invalid argument: %s needs a %zu-byte workspace, got %zu", fn, L.total,
+                workspace_bytes);
+  char* ws = static_cast<char*>(workspace);
+  const int32_t* slot = reinterpret_cast<const int32_t*>(ws + L.slot);
+  return emb_sum_phase(dout, n, rows, cols, ws, L, out_rows, slot, static_cast<cudaStream_t>(stream));
+}
+
+oxc_status oxc_embedding_bwd_compact(const float* dout, const int64_t* ids, int64_t n,
+                                     int64_t vocab_total, int64_t vocab_offset, int64_t rows,
+                                     int64_t cols, int32_t* out_ids, float* out_rows,
+                                     int64_t* count, int32_t shards, int64_t* shard_counts,
+                                     int32_t* err_flag, void* workspace, size_t workspace_bytes,
+                                     void* stream) {
+  if (n > 0 && rows > 0 && cols > 0 && (!dout || !out_rows))
+    return fail(OXC_ERR_INVALID_ARGUMENT,
+                "invalid argument: embedding backward (compact): null pointer");
+  oxc_status st = oxc_embedding_bwd_compact_plan(ids, n, vocab_total, vocab_offset, rows, cols,
+                                                 out_ids, count, shards, shard_counts, err_flag,
+                                                 workspace, workspace_bytes, stream);
+  if (st) return st;
+  return oxc_embedding_bwd_compact_sum(dout, n, rows, cols, out_rows, workspace, workspace_bytes,
+                                       stream);
 }
 
 size_t oxc_embedding_exchange_reduce_workspace_size(int32_t sources, int64_t shard_rows) {

@@ -210,49 +210,119 @@ def exchange_rows(send_ids, send_rows, send_counts, group=None):
     return recv_ids, recv_rows, rc
 
 
+class SparseGradExchange:
+    """The sparse exchange of a replicated [vocab_total, cols] table's gradient
+    over token-sharded ids, with its buffers held for repeated steps.
+
+    ``vjp(ids, dout, slot)`` runs the compact VJP in two calls: the plan (sort,
+    distinct ids, per-shard counts) on the current stream, then -- while the
+    sums run -- the counts' all-to-all on a side stream and their copy to the
+    host, which is the only thing the host waits for.  ``exchange(slot)``
+    sends the rows to their owners and sums them (``oxc_embedding_exchange_
+    reduce``) on a communication stream that waits for the sums; it returns
+    the rank's dense shard of the gradient and an event recorded after the
+    reduce, so the caller's next forward can overlap the exchange.  Two slots
+    let step i's exchange run while step i + 1 computes its VJP into the other
+    slot."""
+
+    def __init__(self, n, vocab_total, cols, device, group=None, slots=2):
+        from . import _native as N
+        self.N, self.L = N, N.load()
+        self.group = group
+        self.world, self.rank = _world(group), _rank(group)
+        self.n, self.v, self.d, self.dev = int(n), int(vocab_total), int(cols), device
+        cap = max(1, min(self.n, self.v))
+        t = torch
+        self.ids = [t.empty(cap, dtype=t.int32, device=device) for _ in range(slots)]
+        self.rows = [t.empty(cap, self.d, dtype=t.float32, device=device) for _ in range(slots)]
+        self.count = [t.empty(1, dtype=t.int64, device=device) for _ in range(slots)]
+        self.sc = [t.empty(self.world, dtype=t.int64, device=device) for _ in range(slots)]
+        self.rc = [t.empty(self.world, dtype=t.int64, device=device) for _ in range(slots)]
+        self.lo, self.shard_rows = vocab_shard(self.v, self.rank, self.world)
+        self.dshard = [t.empty(self.shard_rows, self.d, dtype=t.float32, device=device)
+                       for _ in range(slots)]
+        self.host_counts = [t.empty(2 * self.world, dtype=t.int64, pin_memory=True)
+                            for _ in range(slots)]
+        self.flag = t.zeros(4, dtype=t.int32, device=device)
+        self.ws_bytes = self.L.oxc_embedding_bwd_compact_workspace_size(self.n, self.v, self.d)
+        self.ws = [F._workspace(self.ws_bytes, device) for _ in range(slots)]
+        self.ws2_bytes = self.L.oxc_embedding_exchange_reduce_workspace_size(self.world,
+                                                                              self.shard_rows)
+        self.ws2 = [F._workspace(self.ws2_bytes, device) for _ in range(slots)]
+        self.side = torch.cuda.Stream(device=device)
+        self.comm = torch.cuda.Stream(device=device)
+        self.counts = [None] * slots
+        self.planned = [torch.cuda.Event() for _ in range(slots)]
+        self.summed = [torch.cuda.Event() for _ in range(slots)]
+
+    def vjp(self, ids, dout, slot=0):
+        N, L = self.N, self.L
+        cur = torch.cuda.current_stream()
+        N.check(L.oxc_embedding_bwd_compact_plan(
+            ids.data_ptr(), self.n, self.v, 0, self.v, self.d, self.ids[slot].data_ptr(),
+            self.count[slot].data_ptr(), self.world, self.sc[slot].data_ptr(),
+            self.flag.data_ptr(), self.ws[slot].data_ptr(), self.ws_bytes, cur.cuda_stream),
+            "embedding backward (compact)")
+        self.planned[slot].record(cur)
+        with torch.cuda.stream(self.side):
+            self.side.wait_event(self.planned[slot])
+            dist.all_to_all_single(self.rc[slot], self.sc[slot], group=self.group)
+            h = self.host_counts[slot]
+            h[:self.world].copy_(self.sc[slot], non_blocking=True)
+            h[self.world:].copy_(self.rc[slot], non_blocking=True)
+        N.check(L.oxc_embedding_bwd_compact_sum(
+            dout.data_ptr(), self.n, self.v, self.d, self.rows[slot].data_ptr(),
+            self.ws[slot].data_ptr(), self.ws_bytes, cur.cuda_stream),
+            "embedding backward (compact sums)")
+        self.summed[slot].record(cur)
+        self.side.synchronize()  # the counts only: the sums keep running
+        h = self.host_counts[slot]
+        self.counts[slot] = (h[:self.world].tolist(), h[self.world:].tolist())
+
+    def exchange(self, slot=0):
+        N, L = self.N, self.L
+        sc, rc = self.counts[slot]
+        nsend, nrecv = sum(sc), sum(rc)
+        with torch.cuda.stream(self.comm):
+            self.comm.wait_event(self.summed[slot])
+            rid = torch.empty(nrecv, dtype=torch.int32, device=self.dev)
+            dist.all_to_all_single(rid, self.ids[slot][:nsend], rc, sc, group=self.group)
+            rrows = torch.empty(nrecv, self.d, dtype=torch.float32, device=self.dev)
+            dist.all_to_all_single(rrows, self.rows[slot][:nsend], rc, sc, group=self.group)
+            off = [0]
+            for c in rc:
+                off.append(off[-1] + c)
+            src_off = torch.tensor(off, dtype=torch.int64).to(self.dev)
+            N.check(L.oxc_embedding_exchange_reduce(
+                rid.data_ptr(), rrows.data_ptr(), src_off.data_ptr(), self.world, self.lo,
+                self.shard_rows, self.d, self.dshard[slot].data_ptr(), self.flag.data_ptr(),
+                self.ws2[slot].data_ptr(), self.ws2_bytes, self.comm.cuda_stream),
+                "embedding gradient exchange")
+            done = torch.cuda.Event()
+            done.record(self.comm)
+        return self.dshard[slot], done
+
+
 def embedding_grad(ids, dout, vocab_total, group=None):
     """Gradient of a replicated [vocab_total, cols] table from this rank's
     tokens (ids [n], dout [n, cols]), summed over every rank's tokens; each
     rank returns the rows of its vocab shard (``vocab_shard``).  The sparse
-    exchange: the compact VJP (touched rows only), ``exchange_rows`` to the
-    shard owners, and ``oxc_embedding_exchange_reduce`` (a sum in rank order
-    per row).  A row touched by one rank's tokens only is that rank's
-    position-order sum, bit for bit; a row touched by several ranks is the sum
-    of their partials in rank order.  One rank: the plain VJP."""
-    from . import _native as N
-    world, rank = _world(group), _rank(group)
+    exchange (``SparseGradExchange``): the compact VJP (touched rows only), an
+    all-to-all of those rows to their shard's owner, and
+    ``oxc_embedding_exchange_reduce`` (a sum in rank order per row).  A row
+    touched by one rank's tokens only is that rank's position-order sum, bit
+    for bit; a row touched by several ranks is the sum of their partials in
+    rank order.  One rank: the plain VJP.  The result is ordered on the
+    current stream."""
+    world = _world(group)
     F._require_cuda_f32("dout", dout)
     dout = F.dense(dout)
-    n, cols = ids.numel(), dout.shape[-1]
     if world == 1:
         return F.embedding_bwd(ids, dout, vocab_total)[0]
-    L = N.load()
-    dev = dout.device
-    cap = max(1, min(n, vocab_total))
-    out_ids = torch.empty(cap, dtype=torch.int32, device=dev)
-    out_rows = torch.empty(cap, cols, dtype=torch.float32, device=dev)
-    count = torch.empty(1, dtype=torch.int64, device=dev)
-    shard_counts = torch.empty(world, dtype=torch.int64, device=dev)
-    flag = torch.zeros(4, dtype=torch.int32, device=dev)
-    ws = F._workspace(L.oxc_embedding_bwd_compact_workspace_size(n, vocab_total, cols), dev)
-    N.check(L.oxc_embedding_bwd_compact(dout.data_ptr(), ids.data_ptr(), n, vocab_total, 0,
-                                        vocab_total, cols, out_ids.data_ptr(), out_rows.data_ptr(),
-                                        count.data_ptr(), world, shard_counts.data_ptr(),
-                                        flag.data_ptr(), ws.data_ptr(), ws.numel(), F._stream()),
-            "embedding backward (compact)")
-    recv_ids, recv_rows, rc = exchange_rows(out_ids, out_rows, shard_counts, group)
-    off = [0]
-    for c in rc:
-        off.append(off[-1] + c)
-    src_off = torch.tensor(off, dtype=torch.int64, device=dev)
-    lo, rows = vocab_shard(vocab_total, rank, world)
-    dshard = torch.empty(rows, cols, dtype=torch.float32, device=dev)
-    ws2 = F._workspace(L.oxc_embedding_exchange_reduce_workspace_size(world, rows), dev)
-    N.check(L.oxc_embedding_exchange_reduce(recv_ids.data_ptr(), recv_rows.data_ptr(),
-                                            src_off.data_ptr(), world, lo, rows, cols,
-                                            dshard.data_ptr(), flag.data_ptr(), ws2.data_ptr(),
-                                            ws2.numel(), F._stream()),
-            "embedding gradient exchange")
+    ex = SparseGradExchange(ids.numel(), vocab_total, dout.shape[-1], dout.device, group, slots=1)
+    ex.vjp(ids, dout, 0)
+    dshard, done = ex.exchange(0)
+    torch.cuda.current_stream().wait_event(done)
     return dshard
 
 
