@@ -1462,6 +1462,12 @@ def _run_ours(args, rank, world, local_rank):
                 orep["strong_scaling"] = strong_scaling(other, args, rank, world, local_rank,
                                                         oinp, psteps, 3)
             per_workload[other] = orep
+            if other == "mlp_block":
+                # config 5 once more, composed from the generic registry (the
+                # reference's own graph of F.silu(g) * u), on the same arrays
+                rwl, rrep = measure("registry", args, rank, world, local_rank, oinp, psteps, 3)
+                del rwl
+                per_workload["registry"] = rrep
             if other == "embedding" and world > 1:
                 # the vocab-sharded scheme beside the token-sharded one
                 vwl, vrep = measure("embedding_vocab", args, rank, world, local_rank, oinp,
