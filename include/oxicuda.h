@@ -292,6 +292,13 @@ oxc_status oxc_layer_norm_bwd(const float* x, const float* w, const float* b, co
                               int64_t rows, int64_t cols, int32_t act, int32_t grad_mode,
                               void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- GELU on its own: F.gelu (python/oxitorch/nn/functional.py:194-199) ------
+ * y = gelu(x) and dx = dy * gelu'(x) over n dense floats, the tanh form
+ * evaluated as the fused LayerNorm+GELU kernels do (OXC_ACT_GELU_TANH).  The
+ * VJP takes the forward's input x. */
+oxc_status oxc_gelu_fwd(const float* x, float* y, int64_t n, void* stream);
+oxc_status oxc_gelu_bwd(const float* x, const float* dy, float* dx, int64_t n, void* stream);
+
 /* ---- softmax / log_softmax: F.softmax, F.log_softmax over the last dim -----
  * (python/oxitorch/nn/functional.py:211-222).  log != 0 selects log_softmax.
  * x, y, dy, dx: [rows, cols] row-major.  The VJP takes the forward output y. */

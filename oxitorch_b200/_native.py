@@ -104,6 +104,8 @@ SIGNATURES = {
     "oxc_layer_norm_bwd_workspace_size": (_SZ, [_I64, _I64]),
     "oxc_layer_norm_bwd": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _I32,
                                   _P, _SZ, _P]),
+    "oxc_gelu_fwd": (_I32, [_P, _P, _I64, _P]),
+    "oxc_gelu_bwd": (_I32, [_P, _P, _P, _I64, _P]),
     "oxc_softmax_fwd": (_I32, [_P, _P, _I64, _I64, _I32, _P]),
     "oxc_softmax_bwd": (_I32, [_P, _P, _P, _I64, _I64, _I32, _P]),
     "oxc_softmax_dim_fwd": (_I32, [_VP, _I64, _I32, _P, _P]),

@@ -206,6 +206,47 @@ def layer_norm_gelu(x, weight, bias, eps=1e-5, grad_mode="ref"):
     return _LayerNorm.apply(x, weight, bias, eps, N.ACT_GELU_TANH, grad_mode)
 
 
+# ---- GELU ------------------------------------------------------------------------------
+
+def gelu_fwd(x):
+    """y = gelu(x) (dense, x's shape) for any view x."""
+    _require_cuda_f32("x", x)
+    x = dense(x)
+    y = torch.empty_like(x)
+    N.check(N.load().oxc_gelu_fwd(x.data_ptr(), y.data_ptr(), x.numel(), _stream()), "gelu")
+    return y
+
+
+def gelu_bwd(x, dy):
+    """dx = dy * gelu'(x), dense."""
+    x, dy = dense(x), dense(dy)
+    if dy.shape != x.shape:
+        raise ValueError(f"shape mismatch: {list(dy.shape)} vs {list(x.shape)}")
+    dx = torch.empty_like(x)
+    N.check(N.load().oxc_gelu_bwd(x.data_ptr(), dy.data_ptr(), dx.data_ptr(), x.numel(),
+                                  _stream()), "gelu backward")
+    return dx
+
+
+class _Gelu(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x):
+        x = dense(x)
+        ctx.save_for_backward(x)
+        return gelu_fwd(x)
+
+    @staticmethod
+    def backward(ctx, dy):
+        (x,) = ctx.saved_tensors
+        return gelu_bwd(x, dy)
+
+
+def gelu(x):
+    """F.gelu (functional.py:194-199): 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))),
+    one fused kernel each way.  After a LayerNorm, ``layer_norm_gelu`` fuses both."""
+    return _Gelu.apply(x)
+
+
 # ---- softmax / log_softmax ----------------------------------------------------------
 
 def _softmax_dim(dim, x):
