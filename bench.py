@@ -462,6 +462,9 @@ class Workload:
         self.slot = 0
         self.pending = [None, None]
 
+    def close(self):
+        """Releases what other ranks hold of this workload (collective)."""
+
     def begin(self, i):
         self.slot = i % 2
         work = self.pending[self.slot]
@@ -757,15 +760,27 @@ class Embedding(Workload):
             self.ws = t.empty(max(self.ws_bytes, 16), dtype=t.uint8, device=dev)
             self.bwd_bytes = n * 8 + n * self.d * 4 + self.v * self.d * 4
         else:
-            # token-sharded, replicated table: the compact VJP (touched rows),
-            # an all-to-all of those rows to their vocab shard's owner, and the
-            # owner's rank-order sum into its dense shard of the gradient, on a
-            # communication stream that overlaps the next step's forward
-            from oxitorch_b200.sharded import SparseGradExchange
-            self.GRAPHS = False  # the VJP exchanges its counts with the other ranks
-            self.ex = SparseGradExchange(n, self.v, self.d, dev, slots=2)
+            # token-sharded, replicated table: the VJP's rows go to their vocab
+            # shard's owner, which sums them in rank order into its dense shard
+            # of the gradient on a communication stream that overlaps the next
+            # step's forward.  The fused form stores the rows into the owner's
+            # memory from the VJP kernel itself (peer memory over NVLink); where
+            # peer memory cannot be mapped, the compact VJP + NCCL all-to-all.
+            from oxitorch_b200.sharded import PeerGradExchange, SparseGradExchange
+            self.GRAPHS = False  # the exchange holds a collective
+            self.ex = None
+            if not getattr(args, "nccl_exchange", False):
+                try:
+                    self.ex = PeerGradExchange(n, self.v, self.d, dev, slots=2)
+                    self.exchange_kind = "peer"
+                    self.launches = 11  # + present, scan (2), meta, map, reduce (and NCCL's)
+                except RuntimeError as e:  # raised on every rank alike
+                    self.exchange_fallback = str(e)
+            if self.ex is None:
+                self.ex = SparseGradExchange(n, self.v, self.d, dev, slots=2)
+                self.exchange_kind = "nccl"
+                self.launches = 14
             self.dshard = self.ex.dshard[0]
-            self.launches = 14  # + present, scan (2), meta, map, reduce (and NCCL's)
             # this rank's share of the job's bytes: its tokens' ids and dout,
             # and its shard of the dense table gradient
             self.bwd_bytes = n * 8 + n * self.d * 4 + self.ex.shard_rows * self.d * 4
@@ -799,12 +814,24 @@ class Embedding(Workload):
         self.bwd(dev_in[0])
         self.exchange()
 
+    def close(self):
+        if self.world > 1 and self.exchange_kind == "peer":
+            self.ex.close()
+
+    def _exchange_desc(self):
+        if self.exchange_kind == "peer":
+            return ("fused exchange: the VJP kernel stores each touched row into its vocab "
+                    "shard owner's memory over NVLink (CUDA IPC peer memory), a stream-ordered "
+                    "barrier, the owner's rank-order sum")
+        why = getattr(self, "exchange_fallback", None)
+        return ("compact VJP + NCCL all-to-all of the touched rows to their vocab shard's owner "
+                "+ rank-order sum (sparse exchange)" + (f"; peer memory unavailable: {why}"
+                                                        if why else ""))
+
     def config(self):
         return {"workload": self.DESC, "ids_per_gpu": self.n, "table": [self.v, self.d],
                 "parallelism": (f"token-sharded data parallel x{self.world}, replicated table; "
-                                "compact VJP + all-to-all of the touched rows to their vocab "
-                                "shard's owner + rank-order sum (sparse exchange)"
-                                if self.world > 1 else "one GPU"),
+                                + self._exchange_desc() if self.world > 1 else "one GPU"),
                 "inputs": self.inputs_note(),
                 "roofline_note": "the VJP is the HBM-bound phase; the gather's hot table rows are "
                                  "L2 hits, so its algorithmic bytes exceed its DRAM bytes "
@@ -1399,6 +1426,7 @@ def strong_scaling(name, args, rank, world, local_rank, inp, steps, warmup):
         del wl1
     dist.barrier()
     wl, rep = measure(name, args, rank, world, local_rank, inp, steps, warmup, mode="strong")
+    wl.close()
     del wl
     if rank != 0:
         return None
@@ -1440,6 +1468,7 @@ def _run_ours(args, rank, world, local_rank):
                           "buffers; pass --e2e-large to measure it"}
     elif not args.skip_e2e:
         e2e = run_e2e(torch, wl, args, dev, world)
+    wl.close()
     del wl
     torch.cuda.empty_cache()
 
@@ -1457,6 +1486,7 @@ def _run_ours(args, rank, world, local_rank):
             oinp = device_inputs(WORKLOADS[other].CONFIG, dev, rank, world, args.rows)
             owl, orep = measure(other, args, rank, world, local_rank, oinp, psteps, 3,
                                 cpu_budget=3.0 if not args.no_cpu_baseline else 0.0)
+            owl.close()
             del owl
             if world > 1 and not args.no_strong:
                 orep["strong_scaling"] = strong_scaling(other, args, rank, world, local_rank,
@@ -1617,6 +1647,8 @@ def main():
                     help="rows / tokens / ids per GPU (0 = the BASELINE config's; smaller only "
                          "for profiling: other shapes draw other arrays)")
     ap.add_argument("--skip-e2e", action="store_true", help="profiling runs: no host-buffer leg")
+    ap.add_argument("--nccl-exchange", action="store_true",
+                    help="embedding at N > 1: the NCCL all-to-all exchange, not the fused one")
     ap.add_argument("--e2e-large", action="store_true",
                     help="also run the host-buffer leg of the mlp_block workload")
     args = ap.parse_args()

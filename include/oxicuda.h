@@ -445,6 +445,49 @@ oxc_status oxc_comm_alltoallv(oxc_comm* comm, const void* send, const int64_t* s
                               void* recv, const int64_t* recv_counts, int64_t elem_bytes,
                               void* stream);
 
+/* ---- the fused exchange over peer memory --------------------------------------
+ * No counterpart in the reference.  The VJP of a replicated table with
+ * token-sharded ids that delivers its rows itself: each occurring row's sum is
+ * stored straight into the receive region of the rank that owns the row's
+ * vocab shard, over NVLink (peer memory mapped with oxc_ipc_import), so the
+ * transfer overlaps the sums and nothing waits on the host.  oxc_emb_push
+ * (device memory, built once by the host) names, for this source rank, every
+ * owner's region: rows [cap][cols], ids [cap], and the owner's count slot for
+ * this source.  After every rank's oxc_embedding_bwd_push, a stream-ordered
+ * barrier across the ranks (any collective: its completion on a rank implies
+ * every rank's earlier kernels, whose peer stores are fenced at system scope,
+ * have completed), then each owner runs oxc_embedding_exchange_reduce_regions
+ * over its own regions: source s at [s * cap, s * cap + counts[s]).  A row
+ * beyond `cap` for one owner is recorded in err_flag and not sent. */
+#define OXC_PUSH_MAX_RANKS 16
+typedef struct oxc_emb_push {
+  int32_t world;
+  int32_t reserved;
+  int64_t cap;
+  int64_t lo[OXC_PUSH_MAX_RANKS + 1];  /* owner p holds table rows [lo[p], lo[p+1]) */
+  float* rows[OXC_PUSH_MAX_RANKS];
+  int32_t* ids[OXC_PUSH_MAX_RANKS];
+  int64_t* count[OXC_PUSH_MAX_RANKS];
+} oxc_emb_push;
+oxc_status oxc_embedding_bwd_push(const float* dout, const int64_t* ids, int64_t n,
+                                  int64_t vocab_total, int64_t cols, const oxc_emb_push* push,
+                                  int32_t* err_flag, void* workspace, size_t workspace_bytes,
+                                  void* stream);
+oxc_status oxc_embedding_exchange_reduce_regions(const int32_t* recv_ids, const float* recv_rows,
+                                                 const int64_t* counts, int32_t sources,
+                                                 int64_t cap, int64_t shard_lo,
+                                                 int64_t shard_rows, int64_t cols, float* dshard,
+                                                 int32_t* err_flag, void* workspace,
+                                                 size_t workspace_bytes, void* stream);
+/* Device memory shared between the processes of one node: oxc_ipc_export gives
+ * the handle of the allocation holding dev_ptr and dev_ptr's byte offset in it;
+ * oxc_ipc_import maps it into another process (peer access enabled) and
+ * returns the exported address there; oxc_ipc_close unmaps it. */
+#define OXC_IPC_HANDLE_BYTES 64
+oxc_status oxc_ipc_export(const void* dev_ptr, uint8_t* handle, int64_t* offset);
+oxc_status oxc_ipc_import(const uint8_t* handle, int64_t offset, void** dev_ptr);
+oxc_status oxc_ipc_close(void* dev_ptr, int64_t offset);
+
 /* ---- index_select along any dim, and its VJP --------------------------------
  * oxc_index_select replaces Tensor::index_select (crates/oxi-tensor/src/lib.rs:
  * 665-703) for any dim and any strides of x: out (dense row-major, x's shape

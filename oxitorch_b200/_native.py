@@ -45,6 +45,23 @@ class View(ctypes.Structure):
     ]
 
 
+PUSH_MAX_RANKS = 16
+
+
+class EmbPush(ctypes.Structure):
+    """struct oxc_emb_push: where one source rank's VJP rows go on every owner."""
+
+    _fields_ = [
+        ("world", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("cap", ctypes.c_int64),
+        ("lo", ctypes.c_int64 * (PUSH_MAX_RANKS + 1)),
+        ("rows", ctypes.c_void_p * PUSH_MAX_RANKS),
+        ("ids", ctypes.c_void_p * PUSH_MAX_RANKS),
+        ("count", ctypes.c_void_p * PUSH_MAX_RANKS),
+    ]
+
+
 class GatherColumn(ctypes.Structure):
     """struct oxc_gather_column: source rows, destination rows, bytes per row."""
 
@@ -134,6 +151,12 @@ SIGNATURES = {
     "oxc_comm_allreduce_sum_f64": (_I32, [_P, _P, _I64, _P]),
     "oxc_comm_reduce_scatter_f32": (_I32, [_P, _P, _P, _I64, _P]),
     "oxc_comm_alltoallv": (_I32, [_P, _P, _P, _P, _P, _I64, _P]),
+    "oxc_embedding_bwd_push": (_I32, [_P, _P, _I64, _I64, _I64, _P, _P, _P, _SZ, _P]),
+    "oxc_embedding_exchange_reduce_regions": (_I32, [_P, _P, _P, _I32, _I64, _I64, _I64, _I64,
+                                                     _P, _P, _P, _SZ, _P]),
+    "oxc_ipc_export": (_I32, [_P, _P, ctypes.POINTER(_I64)]),
+    "oxc_ipc_import": (_I32, [_P, _I64, ctypes.POINTER(_P)]),
+    "oxc_ipc_close": (_I32, [_P, _I64]),
     "oxc_index_select": (_I32, [_VP, _I64, _P, _I64, _P, _P, _P]),
     "oxc_gather_dim0": (_I32, [_VP, _P, _I64, _P, _P, _P]),
     "oxc_index_select_bwd_workspace_size": (_SZ, [_P, _I32, _I64, _I64]),

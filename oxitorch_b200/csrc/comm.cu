@@ -12,6 +12,7 @@
 // process that already loaded an NCCL (torch does), shares that one.  One
 // communicator per process and GPU; every rank issues the same calls in the
 // same order; every call is asynchronous on the caller's stream.
+#include <cuda.h>
 #include <dlfcn.h>
 #include <nccl.h>
 
@@ -224,6 +225,60 @@ oxc_status oxc_comm_alltoallv(oxc_comm* comm, const void* send, const int64_t* s
   const ncclResult_t r2 = api->group_end();
   if (r != ncclSuccess) return nccl_fail(api, r, fn);
   return r2 == ncclSuccess ? OXC_OK : nccl_fail(api, r2, fn);
+}
+
+// ---- device memory shared between the processes of one node (CUDA IPC) ----------
+
+static CUresult (*mem_range_fn())(CUdeviceptr*, size_t*, CUdeviceptr) {
+  using Fn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static Fn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &p, 12000, cudaEnableDefault,
+                                         &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<Fn>(p);
+  }();
+  return fn;
+}
+
+oxc_status oxc_ipc_export(const void* dev_ptr, uint8_t* handle, int64_t* offset) {
+  const char* fn = "oxc_ipc_export";
+  if (!dev_ptr || !handle || !offset)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: null pointer", fn);
+  static_assert(sizeof(cudaIpcMemHandle_t) == OXC_IPC_HANDLE_BYTES, "cudaIpcMemHandle_t size");
+  auto range = mem_range_fn();
+  if (!range) return fail(OXC_ERR_OTHER, "%s: cuMemGetAddressRange is not available", fn);
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, (CUdeviceptr)(uintptr_t)dev_ptr) != CUDA_SUCCESS)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: not device memory", fn);
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, (void*)(uintptr_t)base);
+  if (e != cudaSuccess) return cuda_fail(e, fn);
+  std::memcpy(handle, &h, sizeof h);
+  *offset = (int64_t)((uintptr_t)dev_ptr - (uintptr_t)base);
+  return OXC_OK;
+}
+
+oxc_status oxc_ipc_import(const uint8_t* handle, int64_t offset, void** dev_ptr) {
+  const char* fn = "oxc_ipc_import";
+  if (!handle || !dev_ptr || offset < 0)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: bad argument", fn);
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof h);
+  void* base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, fn);
+  *dev_ptr = static_cast<char*>(base) + offset;
+  return OXC_OK;
+}
+
+oxc_status oxc_ipc_close(void* dev_ptr, int64_t offset) {
+  if (!dev_ptr) return OXC_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(static_cast<char*>(dev_ptr) - offset);
+  return e == cudaSuccess ? OXC_OK : cuda_fail(e, "oxc_ipc_close");
 }
 
 }  // extern "C"

@@ -231,12 +231,25 @@ __global__ void __launch_bounds__(MAXT) emb_split_kernel(
 
 // With `slot` (the compact VJP, outer == 1), rows without occurrences are
 // skipped and row r is written at dtable + slot[r] * cols.
+// Owner of table row r under a push table, and r's index in the owner's
+// region for this source: the owner's rows come consecutively in the compact
+// order, so the index is r's slot minus the slot of the owner's first row.
+__device__ __forceinline__ int push_owner(const oxc_emb_push* __restrict__ push, int64_t r) {
+  int p = 0;
+  while (p + 1 < push->world && r >= push->lo[p + 1]) ++p;
+  return p;
+}
+
+// With `slot` (the compact VJP, outer == 1), rows without occurrences are
+// skipped and row r is written at dtable + slot[r] * cols; with `push` as
+// well, at its owner's region instead (peer memory), and the stores are
+// fenced at system scope before the grid completes.
 template <int VW, int VPT, int MAXT>
 __global__ void __launch_bounds__(MAXT) emb_rows_kernel(
     const float* __restrict__ dout_all, const int32_t* __restrict__ spos,
     const int32_t* __restrict__ offsets, const float* __restrict__ parts_all, int64_t rows,
     int cols, float* __restrict__ dtable, int64_t n, int64_t outer,
-    const int32_t* __restrict__ slot) {
+    const int32_t* __restrict__ slot, const oxc_emb_push* __restrict__ push, int32_t* err) {
   // Launched as a programmatic dependent of emb_split_kernel: rows with at
   // most kSplitP occurrences read only the sort's output and run while the
   // split grid is still working; rows made of pieces wait for it (pdl_wait)
@@ -251,6 +264,19 @@ __global__ void __launch_bounds__(MAXT) emb_rows_kernel(
     const int64_t s0 = offsets[r], s1 = offsets[r + 1];
     if (slot && s1 == s0) continue;
     float* dst = dtable + (slot ? (int64_t)slot[r] : o * rows + r) * (int64_t)cols;
+    if (push) {
+      const int p = push_owner(push, r);
+      const int64_t idx = (int64_t)slot[r] - slot[push->lo[p]];
+      if (idx >= push->cap) {
+        if (err && threadIdx.x == 0 && atomicCAS(err, 0, 1) == 0) {
+          err[1] = (int32_t)r;
+          err[2] = 0;
+          err[3] = (int32_t)push->cap;
+        }
+        continue;
+      }
+      dst = push->rows[p] + idx * (int64_t)cols;
+    }
     for (int c_base = blockIdx.y * VPT * blockDim.x; c_base < nvec;
          c_base += gridDim.y * VPT * blockDim.x) {
       float acc[VPT][VW];
@@ -302,6 +328,7 @@ __global__ void __launch_bounds__(MAXT) emb_rows_kernel(
     }
   }
   pdl_wait();
+  if (push) __threadfence_system();  // the peer stores are visible before the grid completes
 }
 
 // ---- index_select along any dim (Tensor::index_select, lib.rs:665-703) ----------
@@ -440,6 +467,57 @@ __global__ void emb_compact_meta_kernel(const int32_t* __restrict__ present,
       return r >= rows ? (rows ? (int64_t)slot[rows - 1] + present[rows - 1] : 0) : slot[r];
     };
     shard_counts[s] = pre(hi) - pre(lo);
+  }
+}
+
+// The push meta: every occurring row's id into its owner's id region, and
+// each owner's count of this source's rows (prefix sums at the shard bounds).
+__global__ void emb_push_meta_kernel(const int32_t* __restrict__ present,
+                                     const int32_t* __restrict__ slot, int64_t rows,
+                                     const oxc_emb_push* __restrict__ push, int32_t* err) {
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  auto pre = [&](int64_t r) -> int64_t {
+    return r >= rows ? (int64_t)slot[rows - 1] + present[rows - 1] : slot[r];
+  };
+  for (int64_t r = tid; r < rows; r += (int64_t)gridDim.x * blockDim.x) {
+    if (!present[r]) continue;
+    const int p = push_owner(push, r);
+    const int64_t idx = (int64_t)slot[r] - pre(push->lo[p]);
+    if (idx < push->cap) push->ids[p][idx] = (int32_t)r;
+  }
+  if (tid < push->world) {
+    const int64_t c = pre(push->lo[tid + 1]) - pre(push->lo[tid]);
+    if (c > push->cap && err && atomicCAS(err, 0, 1) == 0) {
+      err[1] = (int32_t)c;
+      err[2] = 0;
+      err[3] = (int32_t)push->cap;
+    }
+    *push->count[tid] = c < push->cap ? c : push->cap;
+  }
+  __threadfence_system();
+}
+
+// The owner's side of the fused exchange: region s of recv holds counts[s]
+// rows; map[s * shard_rows + v] = the region index of row shard_lo + v, or -1.
+__global__ void emb_region_map_kernel(const int32_t* __restrict__ recv_ids,
+                                      const int64_t* __restrict__ counts, int32_t sources,
+                                      int64_t cap, int64_t shard_lo, int64_t shard_rows,
+                                      int32_t* __restrict__ map, int32_t* err) {
+  const int64_t total = (int64_t)sources * cap;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t s = i / cap, k = i - s * cap;
+    if (k >= counts[s]) continue;
+    const int64_t v = (int64_t)recv_ids[i] - shard_lo;
+    if (v < 0 || v >= shard_rows) {
+      if (err && atomicCAS(err, 0, 1) == 0) {
+        err[1] = recv_ids[i];
+        err[2] = 0;
+        err[3] = (int32_t)shard_rows;
+      }
+      continue;
+    }
+    map[s * shard_rows + v] = (int32_t)i;
   }
 }
 
@@ -586,7 +664,8 @@ static oxc_status emb_sort_phase(const int64_t* ids, int64_t n, int64_t vocab_to
 // or, with `slot`, into the compact rows of the occurring ids.
 static oxc_status emb_sum_phase(const float* dout, int64_t n, int64_t rows, int64_t cols,
                                 char* ws, const EmbLayout& L, float* dtable, const int32_t* slot,
-                                cudaStream_t s) {
+                                cudaStream_t s, const oxc_emb_push* push = nullptr,
+                                int32_t* err = nullptr) {
   const int32_t* keys_out = reinterpret_cast<const int32_t*>(ws + L.keys_out);
   const int32_t* vals_out = reinterpret_cast<const int32_t*>(ws + L.vals_out);
   const int32_t* offsets = reinterpret_cast<const int32_t*>(ws + L.offsets);
@@ -610,13 +689,13 @@ static oxc_status emb_sum_phase(const float* dout, int64_t n, int64_t rows, int6
         dout, keys_out, vals_out, offsets, n, rows, (int)cols, parts, (int64_t)1);
     launch_dependent(emb_rows_kernel<4, 1, kEmbChunkThreads>, grow, block, s, dout, vals_out,
                      offsets, (const float*)parts, rows, (int)cols, dtable, n, (int64_t)1,
-                     slot);
+                     slot, push, err);
   } else {
     emb_split_kernel<1, 4, kEmbChunkThreads><<<gsplit, block, 0, s>>>(
         dout, keys_out, vals_out, offsets, n, rows, (int)cols, parts, (int64_t)1);
     launch_dependent(emb_rows_kernel<1, 4, kEmbChunkThreads>, grow, block, s, dout, vals_out,
                      offsets, (const float*)parts, rows, (int)cols, dtable, n, (int64_t)1,
-                     slot);
+                     slot, push, err);
   }
   return check_launch("oxc_embedding_bwd");
 }
@@ -820,6 +899,91 @@ oxc_status oxc_embedding_exchange_reduce(const int32_t* recv_ids, const float* r
   return check_launch("oxc_embedding_exchange_reduce");
 }
 
+oxc_status oxc_embedding_bwd_push(const float* dout, const int64_t* ids, int64_t n,
+                                  int64_t vocab_total, int64_t cols, const oxc_emb_push* push,
+                                  int32_t* err_flag, void* workspace, size_t workspace_bytes,
+                                  void* stream) {
+  const char* fn = "embedding backward (push)";
+  oxc_status st = emb_check(fn, n, vocab_total, 0, vocab_total, cols);
+  if (st) return st;
+  if (!push) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: null push table", fn);
+  if (n == 0 || vocab_total == 0 || cols == 0)
+    return fail(OXC_ERR_NOT_IMPLEMENTED,
+                "not implemented: %s: empty inputs (every rank must still signal its counts)", fn);
+  if (!dout || !ids) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: null pointer", fn);
+  EmbLayout L;
+  st = emb_layout(n, vocab_total, cols, &L, 1, true);
+  if (st) return st;
+  if (!workspace || workspace_bytes < L.total)
+    return fail(OXC_ERR_INVALID_ARGUMENT,
+                "invalid argument: %s needs a %zu-byte workspace, got %zu", fn, L.total,
+                workspace_bytes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  const int64_t rows = vocab_total;
+  st = emb_sort_phase(ids, n, vocab_total, 0, rows, err_flag, ws, L, s);
+  if (st) return st;
+  int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
+  int32_t* present = reinterpret_cast<int32_t*>(ws + L.present);
+  int32_t* slot = reinterpret_cast<int32_t*>(ws + L.slot);
+  const unsigned gr = (unsigned)std::min<int64_t>((rows + 255) / 256, (int64_t)sm_count() * 8);
+  emb_present_kernel<<<gr, 256, 0, s>>>(offsets, rows, present);
+  st = check_launch("oxc_embedding_bwd_push (present)");
+  if (st) return st;
+  size_t scan_bytes = L.scan_bytes;
+  cudaError_t e = cub::DeviceScan::ExclusiveSum(ws + L.scan, scan_bytes, present, slot, (int)rows, s);
+  if (e != cudaSuccess) return cuda_fail(e, "oxc_embedding_bwd_push (scan)");
+  emb_push_meta_kernel<<<gr, 256, 0, s>>>(present, slot, rows, push, err_flag);
+  st = check_launch("oxc_embedding_bwd_push (meta)");
+  if (st) return st;
+  // the compact rows are not kept locally: every row goes to its owner's region
+  return emb_sum_phase(dout, n, rows, cols, ws, L, nullptr, slot, s, push, err_flag);
+}
+
+oxc_status oxc_embedding_exchange_reduce_regions(const int32_t* recv_ids, const float* recv_rows,
+                                                 const int64_t* counts, int32_t sources,
+                                                 int64_t cap, int64_t shard_lo,
+                                                 int64_t shard_rows, int64_t cols, float* dshard,
+                                                 int32_t* err_flag, void* workspace,
+                                                 size_t workspace_bytes, void* stream) {
+  const char* fn = "embedding gradient exchange (regions)";
+  if (sources <= 0 || cap < 0 || shard_rows < 0 || cols < 0 || shard_lo < 0)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: bad sizes", fn);
+  if (shard_rows >= 0x7fffffff || cols > 0x7fffffff || (int64_t)sources * cap >= 0x7fffffff ||
+      (int64_t)sources * shard_rows >= 0x7fffffff)
+    return fail(OXC_ERR_NOT_IMPLEMENTED, "not implemented: %s: sizes beyond 2^31", fn);
+  if (shard_rows == 0 || cols == 0) return OXC_OK;
+  if (!counts || !dshard || (cap > 0 && (!recv_ids || !recv_rows)))
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: null pointer", fn);
+  const size_t need = oxc_embedding_exchange_reduce_workspace_size(sources, shard_rows);
+  if (!workspace || workspace_bytes < need)
+    return fail(OXC_ERR_INVALID_ARGUMENT,
+                "invalid argument: %s needs a %zu-byte workspace, got %zu", fn, need,
+                workspace_bytes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t* map = static_cast<int32_t*>(workspace);
+  cudaError_t e = cudaMemsetAsync(map, 0xff, (size_t)sources * shard_rows * sizeof(int32_t), s);
+  if (e != cudaSuccess) return cuda_fail(e, "oxc_embedding_exchange_reduce_regions");
+  if (cap > 0) {
+    emb_region_map_kernel<<<(unsigned)sm_count() * 4, 256, 0, s>>>(recv_ids, counts, sources, cap,
+                                                                   shard_lo, shard_rows, map,
+                                                                   err_flag);
+    oxc_status st = check_launch("oxc_embedding_exchange_reduce_regions (map)");
+    if (st) return st;
+  }
+  const bool v4 = cols % 4 == 0 && (cap == 0 || aligned16(recv_rows)) && aligned16(dshard);
+  const int64_t per = v4 ? cols / 4 : cols;
+  const unsigned chunks = (unsigned)std::min<int64_t>(65535, (per + 127) / 128);
+  const dim3 grid((unsigned)std::min<int64_t>(shard_rows, (int64_t)sm_count() * 32), chunks);
+  if (v4)
+    emb_exchange_reduce_kernel<4><<<grid, 128, 0, s>>>(recv_rows, map, sources, shard_rows,
+                                                       (int)cols, dshard);
+  else
+    emb_exchange_reduce_kernel<1><<<grid, 128, 0, s>>>(recv_rows, map, sources, shard_rows,
+                                                       (int)cols, dshard);
+  return check_launch("oxc_embedding_exchange_reduce_regions");
+}
+
 oxc_status oxc_index_select(const oxc_view* x, int64_t dim, const int64_t* ids, int64_t n,
                             float* out, int32_t* err_flag, void* stream) {
   const char* fn = "index_select";
@@ -990,13 +1154,13 @@ oxc_status oxc_index_select_bwd(const float* g, const int64_t* ids, int64_t n,
         g, keys_out, vals_out, offsets, n, len, (int)inner, parts, outer);
     launch_dependent(emb_rows_kernel<4, 1, kEmbChunkThreads>, grow, block, s, g, vals_out,
                      offsets, (const float*)parts, len, (int)inner, gx, n, outer,
-                     (const int32_t*)nullptr);
+                     (const int32_t*)nullptr, (const oxc_emb_push*)nullptr, (int32_t*)nullptr);
   } else {
     emb_split_kernel<1, 4, kEmbChunkThreads><<<gsplit, block, 0, s>>>(
         g, keys_out, vals_out, offsets, n, len, (int)inner, parts, outer);
     launch_dependent(emb_rows_kernel<1, 4, kEmbChunkThreads>, grow, block, s, g, vals_out,
                      offsets, (const float*)parts, len, (int)inner, gx, n, outer,
-                     (const int32_t*)nullptr);
+                     (const int32_t*)nullptr, (const oxc_emb_push*)nullptr, (int32_t*)nullptr);
   }
   return check_launch("oxc_index_select_bwd");
 }

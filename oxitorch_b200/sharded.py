@@ -303,6 +303,169 @@ class SparseGradExchange:
         return self.dshard[slot], done
 
 
+class PeerGradExchange:
+    """The fused form of the same exchange over peer memory (NVLink): the VJP
+    kernel stores every occurring row's sum straight into the receive region
+    of the rank that owns the row (``oxc_embedding_bwd_push``), so the
+    transfer overlaps the sums and the host never waits.  Each rank holds, per
+    slot, receive regions for every source rank (rows [ranks, cap, cols], ids
+    [ranks, cap], counts [ranks]); the regions are exported once with CUDA IPC
+    and mapped by every other rank.  ``exchange(slot)`` is a stream-ordered
+    barrier (a one-element all-reduce: it completes only after every rank's
+    VJP kernel, whose peer stores are fenced at system scope) followed by the
+    owner's rank-order sum (``oxc_embedding_exchange_reduce_regions``) on a
+    communication stream; it returns the dense gradient shard and an event.
+
+    Ordering across steps: a source writes a slot's regions again two steps
+    later, after the barrier of the step in between (``vjp`` waits for it),
+    which every owner enters only after its reduce of that slot (both run in
+    order on the owner's communication stream)."""
+
+    def __init__(self, n, vocab_total, cols, device, group=None, slots=2):
+        import ctypes
+        import math
+        from . import _native as N
+        self.N, self.L, self.ctypes = N, N.load(), ctypes
+        self.group = group
+        self.world, self.rank = _world(group), _rank(group)
+        if slots < 2:
+            raise ValueError("invalid argument: the fused exchange needs two slots (a source "
+                             "writes a slot again only after the owner's reduce of it)")
+        if self.world > N.PUSH_MAX_RANKS:
+            raise NotImplementedError(f"not implemented: the fused exchange over {self.world} "
+                                      f"ranks (at most {N.PUSH_MAX_RANKS})")
+        self.n, self.v, self.d, self.dev, self.slots = int(n), int(vocab_total), int(cols), \
+            device, slots
+        self.cap = math.ceil(self.v / self.world)  # rows of the largest vocab shard
+        self.lo, self.shard_rows = vocab_shard(self.v, self.rank, self.world)
+        G, cap, d = self.world, self.cap, self.d
+        t = torch
+        self.rrows = [t.empty(G * cap * d, dtype=t.float32, device=device) for _ in range(slots)]
+        self.rids = [t.empty(G * cap, dtype=t.int32, device=device) for _ in range(slots)]
+        self.rcount = [t.zeros(G, dtype=t.int64, device=device) for _ in range(slots)]
+        self.dshard = [t.empty(self.shard_rows, d, dtype=t.float32, device=device)
+                       for _ in range(slots)]
+        self.flag = t.zeros(4, dtype=t.int32, device=device)
+        self.ws_bytes = self.L.oxc_embedding_bwd_compact_workspace_size(self.n, self.v, d)
+        self.ws = [F._workspace(self.ws_bytes, device) for _ in range(slots)]
+        self.ws2_bytes = self.L.oxc_embedding_exchange_reduce_workspace_size(G, self.shard_rows)
+        self.ws2 = [F._workspace(self.ws2_bytes, device) for _ in range(slots)]
+        self.comm = torch.cuda.Stream(device=device)
+        self.token = t.zeros(1, dtype=t.float32, device=device)
+        self.passed = None  # the last exchange's barrier, on the communication stream
+        # export this rank's regions (one handle per allocation), map every other rank's
+        mine, handles = [], {}
+        try:
+            for k in range(slots):
+                entry = []
+                for buf in (self.rrows[k], self.rids[k], self.rcount[k]):
+                    h = (ctypes.c_uint8 * 64)()
+                    off = ctypes.c_int64(0)
+                    N.check(self.L.oxc_ipc_export(buf.data_ptr(), h, ctypes.byref(off)),
+                            "ipc export")
+                    key = buf.data_ptr() - off.value
+                    handles.setdefault(key, bytes(h))
+                    entry.append((handles[key], off.value))
+                mine.append(entry)
+        except RuntimeError as e:  # every rank learns of it through the gather
+            mine = str(e)
+        every = [None] * G
+        dist.all_gather_object(every, mine, group=group)
+        bad = [f"rank {p}: {e}" for p, e in enumerate(every) if isinstance(e, str)]
+        if bad:
+            raise RuntimeError("peer memory could not be exported on every rank: " + "; ".join(bad))
+        # Map every other rank's allocations, each distinct handle once (buffers
+        # of one allocation share it; a process maps a handle only once).
+        self.mapped = []  # base pointers to unmap
+        opened, base, err = {}, {}, ""
+        try:
+            for p in range(G):
+                for k in range(slots):
+                    for j, buf in enumerate((self.rrows[k], self.rids[k], self.rcount[k])):
+                        if p == self.rank:
+                            base[(p, k, j)] = buf.data_ptr()
+                            continue
+                        h, off = every[p][k][j]
+                        if (p, h) not in opened:
+                            ptr = ctypes.c_void_p()
+                            N.check(self.L.oxc_ipc_import(
+                                (ctypes.c_uint8 * 64).from_buffer_copy(h), 0, ctypes.byref(ptr)),
+                                "ipc import")
+                            opened[(p, h)] = ptr.value
+                            self.mapped.append(ptr.value)
+                        base[(p, k, j)] = opened[(p, h)] + off
+        except RuntimeError as e:  # reported on every rank alike below
+            err = str(e)
+        ok = torch.tensor([0.0 if err else 1.0], device=device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if ok.item() < 1.0:
+            for ptr in self.mapped:
+                self.L.oxc_ipc_close(ptr, 0)
+            self.mapped = []
+            raise RuntimeError("peer memory could not be mapped on every rank"
+                               + (f": {err}" if err else ""))
+        self.push = []
+        for k in range(slots):
+            tab = N.EmbPush()
+            tab.world, tab.cap = G, cap
+            for p in range(G + 1):
+                tab.lo[p] = self.v * p // G
+            for p in range(G):
+                tab.rows[p] = base[(p, k, 0)] + self.rank * cap * d * 4
+                tab.ids[p] = base[(p, k, 1)] + self.rank * cap * 4
+                tab.count[p] = base[(p, k, 2)] + self.rank * 8
+            raw = bytes(tab)
+            dev_tab = t.tensor(list(raw), dtype=t.uint8).to(device)
+            self.push.append(dev_tab)
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)
+
+    def vjp(self, ids, dout, slot=0):
+        cur = torch.cuda.current_stream()
+        if self.passed is not None:
+            # Slot k was last written two exchanges ago; every owner's reduce of
+            # it precedes that owner's part in the last barrier.
+            cur.wait_event(self.passed)
+        self.N.check(self.L.oxc_embedding_bwd_push(
+            dout.data_ptr(), ids.data_ptr(), self.n, self.v, self.d, self.push[slot].data_ptr(),
+            self.flag.data_ptr(), self.ws[slot].data_ptr(), self.ws_bytes, cur.cuda_stream),
+            "embedding backward (push)")
+
+    def exchange(self, slot=0):
+        """Runs on the communication stream after the current stream's VJP, so
+        the next forward overlaps the barrier and the reduce."""
+        cur = torch.cuda.current_stream()
+        pushed = torch.cuda.Event()
+        pushed.record(cur)
+        with torch.cuda.stream(self.comm):
+            self.comm.wait_event(pushed)
+            # stream-ordered barrier: behind this stream's previous reduce here,
+            # behind every rank's VJP of this slot everywhere
+            dist.all_reduce(self.token, group=self.group)
+            self.passed = torch.cuda.Event()
+            self.passed.record(self.comm)
+            self.N.check(self.L.oxc_embedding_exchange_reduce_regions(
+                self.rids[slot].data_ptr(), self.rrows[slot].data_ptr(),
+                self.rcount[slot].data_ptr(), self.world, self.cap, self.lo, self.shard_rows,
+                self.d, self.dshard[slot].data_ptr(), self.flag.data_ptr(),
+                self.ws2[slot].data_ptr(), self.ws2_bytes, self.comm.cuda_stream),
+                "embedding gradient exchange")
+            done = torch.cuda.Event()
+            done.record(self.comm)
+        return self.dshard[slot], done
+
+    def close(self):
+        """Unmaps the other ranks' regions after every rank's last use, and
+        returns once every rank has unmapped this rank's (so its buffers may be
+        freed).  Collective: every rank calls it."""
+        torch.cuda.synchronize(self.dev)
+        dist.barrier(group=self.group)
+        for ptr in self.mapped:
+            self.N.check(self.L.oxc_ipc_close(ptr, 0), "ipc close")
+        self.mapped = []
+        dist.barrier(group=self.group)
+
+
 def embedding_grad(ids, dout, vocab_total, group=None):
     """Gradient of a replicated [vocab_total, cols] table from this rank's
     tokens (ids [n], dout [n, cols]), summed over every rank's tokens; each

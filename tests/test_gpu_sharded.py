@@ -277,6 +277,20 @@ def _nccl_body(rank, world, dev):
     voff, vrows = S.vocab_shard(v2, rank, world)
     assert_close(_host(dsh), _host(full2)[voff:voff + vrows], rtol=1e-4, atol=1e-4,
                  what="sparse-exchanged dtable shard")
+    # the fused exchange over peer memory: the same sums in the same order as
+    # the NCCL all-to-all exchange, so bit for bit the same shard, over three
+    # steps that alternate the two slots
+    ex = S.PeerGradExchange(hi2 - lo2, v2, d2, dev, slots=2)
+    ids_r = _dev(ids2[lo2:hi2], dev)
+    for step in range(3):
+        dout_k = _dev(dout2[lo2:hi2] * np.float32(step + 1), dev)
+        ex.vjp(ids_r, dout_k, step % 2)
+        got, done = ex.exchange(step % 2)
+        torch.cuda.current_stream().wait_event(done)
+        want_k = S.embedding_grad(ids_r, dout_k, v2)
+        assert_bitexact(_host(got), _host(want_k), f"peer-exchanged dtable shard, step {step}")
+    assert int(ex.flag.abs().sum().item()) == 0
+    ex.close()
     # the C-ABI communicator (oxc_comm_*), the route of a native host
     import ctypes
     from oxitorch_b200 import _native as N
