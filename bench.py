@@ -818,6 +818,41 @@ class Embedding(Workload):
         if self.world > 1 and self.exchange_kind == "peer":
             self.ex.close()
 
+    def check_exchange(self):
+        """After timing (N > 1): one more VJP through the workload's exchange,
+        against an independent route: every rank's dense single-GPU VJP of its
+        tokens (oxc_embedding_bwd over the whole table), summed over ranks in
+        f64 by a reduce-scatter onto the vocab shards.  Tolerance 1e-6 x the sum
+        over ranks of |partial|; rows touched by one rank only are that rank's
+        position-order sums, so they agree to the bit."""
+        t = self.torch
+        import torch.distributed as dist
+        from oxitorch_b200 import functional as F
+        self.begin(0)
+        self.bwd()
+        self.exchange()
+        self.drain()
+        got = self.ex.dshard[self.slot].double()
+        dense, flag = F.embedding_bwd(self.ids, self.dout, self.v)
+        part = dense.double()
+        del dense
+        lo, rows = self.ex.lo, self.ex.shard_rows
+        if self.v % self.world:
+            return {"ok": None, "what": "vocab not divisible by the ranks: not checked"}
+        want = t.empty(rows, self.d, dtype=t.float64, device=self.dev)
+        dist.reduce_scatter_tensor(want, part)
+        tol = t.empty_like(want)
+        dist.reduce_scatter_tensor(tol, part.abs_())
+        del part
+        tol.mul_(1e-6).add_(1e-30)
+        err = (got - want).abs_()
+        ok = bool((err <= tol).all().item()) and int(flag.abs().sum().item()) == 0 \
+            and int(self.ex.flag.abs().sum().item()) == 0
+        worst = float((err / tol).max().item())
+        return {"ok": ok, "worst_err_over_tolerance": worst, "shard_rows": [lo, lo + rows],
+                "what": "exchanged dtable shard vs the f64 reduce-scatter of every rank's dense "
+                        "single-GPU VJP, tolerance 1e-6 x sum over ranks of |partial|"}
+
     def _exchange_desc(self):
         if self.exchange_kind == "peer":
             return ("fused exchange: the VJP kernel stores each touched row into its vocab "
@@ -1238,8 +1273,16 @@ def time_steps(wl, steps, warmup, world, local_rank, exchange=True, solo=False):
     events on the launching stream around the whole loop, a barrier and a
     synchronize on both sides, the max over ranks.  The last step's exchange
     is inside the timed region (drain() before the end event).  `solo`: this
-    rank runs alone (no barrier, no max), the others wait.  Returns
-    (ms_per_step, fwd_ms, bwd_ms, clocks)."""
+    rank runs alone (no barrier, no max), the others wait.
+
+    A step is one replay of a graph holding the forward and the VJP (or their
+    eager launches); no event is recorded between the phases, because a timing
+    event between two kernels makes the GPU drain the first before the second
+    starts (on config 1 that cost 9 us of a 59 us step).  The phases' own
+    durations (the roofline's kernel time) come from two more loops right
+    after, timed the same way: `steps` forward launches back to back, then
+    `steps` VJP launches, on the same rotating buffers.
+    Returns (ms_per_step, fwd_ms, bwd_ms, clocks)."""
     torch = wl.torch
     stream = torch.cuda.current_stream()
     multi = world > 1 and not solo
@@ -1248,67 +1291,80 @@ def time_steps(wl, steps, warmup, world, local_rank, exchange=True, solo=False):
 
     graphs = capture_graphs(wl) if wl.GRAPHS else None
 
-    def one(i, ev):
-        wl.begin(i)
-        ev[0].record(stream)
+    def run(phase):
         if graphs:
-            key = wl.graph_key()
-            graphs[("fwd", key)].replay()
-            ev[1].record(stream)
-            graphs[("bwd", key)].replay()
+            graphs[(phase, wl.graph_key())].replay()
         else:
-            wl.fwd()
-            ev[1].record(stream)
-            wl.bwd()
-        ev[2].record(stream)
+            if phase in ("step", "fwd"):
+                wl.fwd()
+            if phase in ("step", "bwd"):
+                wl.bwd()
+
+    def one(i):
+        wl.begin(i)
+        run("step")
         if exchange:
             wl.exchange()
 
-    warm = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     for i in range(warmup):
-        one(i, warm)
+        one(i)
     wl.drain()
     torch.cuda.synchronize()
+
+    def timed(body, first):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if multi:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start.record(stream)
+        for i in range(steps):
+            body(first + i)
+        wl.drain()
+        end.record(stream)
+        torch.cuda.synchronize()
+        if multi:
+            dist.barrier()
+        ms = start.elapsed_time(end)
+        if multi:
+            ms = _max_over_ranks(torch, wl.dev, world, ms)
+        return ms / steps
+
     sampler = ClockSampler(local_rank)
     sampler.start()
     time.sleep(0.2)
-    events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if multi:
-        dist.barrier()
-    torch.cuda.synchronize()
-    start.record(stream)
-    for i in range(steps):
-        one(warmup + i, events[i])
-    wl.drain()
-    end.record(stream)
-    torch.cuda.synchronize()
-    if multi:
-        dist.barrier()
+    ms = timed(one, warmup)
     clocks = sampler.stop()
-    ms = start.elapsed_time(end)
-    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in events)
-    bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in events)
-    if multi:
-        ms = _max_over_ranks(torch, wl.dev, world, ms)
+
+    def phase_body(phase):
+        def body(i):
+            wl.begin(i)
+            run(phase)
+        return body
+
+    fwd_ms = timed(phase_body("fwd"), warmup + steps)
+    bwd_ms = timed(phase_body("bwd"), warmup + 2 * steps)
     wl.graphs_used = bool(graphs)
-    return ms / steps, fwd_ms, bwd_ms, clocks
+    return ms, fwd_ms, bwd_ms, clocks
 
 
 def capture_graphs(wl):
-    """One CUDA graph per phase (fwd, bwd) and step variant, so the timed loop
-    launches each phase with one replay instead of a Python call per kernel
-    (configs whose steps last tens of microseconds are otherwise bound by the
-    host).  The kernels and their launch geometry are exactly the eager ones.
-    Returns None (eager launches) if a capture fails."""
+    """One CUDA graph per phase (fwd, bwd, and the whole step) and step variant,
+    so the timed loops launch each with one replay instead of a Python call
+    per kernel (configs whose steps last tens of microseconds are otherwise
+    bound by the host).  The kernels and their launch geometry are exactly the
+    eager ones.  Returns None (eager launches) if a capture fails."""
     torch = wl.torch
     stream = torch.cuda.current_stream()
     graphs = {}
+
+    def both():
+        wl.fwd()
+        wl.bwd()
     try:
         for i in range(wl.VARIANTS):
             wl.begin(i)
             key = wl.graph_key()
-            for phase, fn in (("fwd", wl.fwd), ("bwd", wl.bwd)):
+            for phase, fn in (("fwd", wl.fwd), ("bwd", wl.bwd), ("step", both)):
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=stream, capture_error_mode="thread_local"):
                     fn()
@@ -1358,7 +1414,11 @@ def measure(name, args, rank, world, local_rank, inp, steps, warmup, mode="weak"
     cls = WORKLOADS[name]
     wl = cls(dev, rank, world, args, inp, mode)
     ms, fwd_ms, bwd_ms, clocks = time_steps(wl, steps, warmup, world, local_rank)
-    check = exchange_check(wl) if world > 1 and wl.partials() else None
+    check = None
+    if world > 1 and hasattr(wl, "check_exchange"):
+        check = wl.check_exchange()
+    elif world > 1 and wl.partials():
+        check = exchange_check(wl)
     total_bytes = world * (wl.fwd_bytes + wl.bwd_bytes)
     peak, peak_kind = measured_peak()
     dom_ms, dom_bytes = (bwd_ms, wl.bwd_bytes) if wl.dominant == "bwd" else (fwd_ms, wl.fwd_bytes)
@@ -1393,9 +1453,15 @@ def measure(name, args, rank, world, local_rank, inp, steps, warmup, mode="weak"
         "gpu_launches": wl.launches * steps,
         "clocks": clocks,
     }
-    rep["config"]["launch"] = ("each phase (forward, VJP) replayed as a CUDA graph of the same "
-                               "kernels, one per step variant" if wl.graphs_used
+    rep["config"]["launch"] = ("each step replayed as one CUDA graph of the same kernels (forward "
+                               "then VJP), one per step variant" if wl.graphs_used
                                else "eager launches through the C ABI")
+    rep["roofline"]["phase_timing"] = (
+        "fwd_ms / bwd_ms: each phase timed over its own loop of `steps` back-to-back launches "
+        "(CUDA events on the launching stream, max over ranks) right after the step loop, on "
+        "the same rotating buffers; the step loop itself records no event between the phases, "
+        "since a timing event between two kernels makes the GPU drain the first before the "
+        "second starts")
     if prof.get("fwd_dram_bytes_per_launch"):
         rep["roofline"]["fwd_dram_gbs"] = prof["fwd_dram_bytes_per_launch"] / (fwd_ms * 1e-3) / 1e9
     if check is not None:

@@ -462,7 +462,7 @@ oxc_status oxc_comm_alltoallv(oxc_comm* comm, const void* send, const int64_t* s
 #define OXC_PUSH_MAX_RANKS 16
 typedef struct oxc_emb_push {
   int32_t world;
-  int32_t reserved;
+  int32_t source;  /* this (source) rank: stores to its own region need no system-scope fence */
   int64_t cap;
   int64_t lo[OXC_PUSH_MAX_RANKS + 1];  /* owner p holds table rows [lo[p], lo[p+1]) */
   float* rows[OXC_PUSH_MAX_RANKS];

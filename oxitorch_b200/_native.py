@@ -53,7 +53,7 @@ class EmbPush(ctypes.Structure):
 
     _fields_ = [
         ("world", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("source", ctypes.c_int32),
         ("cap", ctypes.c_int64),
         ("lo", ctypes.c_int64 * (PUSH_MAX_RANKS + 1)),
         ("rows", ctypes.c_void_p * PUSH_MAX_RANKS),

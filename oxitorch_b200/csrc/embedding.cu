@@ -229,8 +229,6 @@ __global__ void __launch_bounds__(MAXT) emb_split_kernel(
   }
 }
 
-// With `slot` (the compact VJP, outer == 1), rows without occurrences are
-// skipped and row r is written at dtable + slot[r] * cols.
 // Owner of table row r under a push table, and r's index in the owner's
 // region for this source: the owner's rows come consecutively in the compact
 // order, so the index is r's slot minus the slot of the owner's first row.
@@ -241,10 +239,12 @@ __device__ __forceinline__ int push_owner(const oxc_emb_push* __restrict__ push,
 }
 
 // With `slot` (the compact VJP, outer == 1), rows without occurrences are
-// skipped and row r is written at dtable + slot[r] * cols; with `push` as
-// well, at its owner's region instead (peer memory), and the stores are
-// fenced at system scope before the grid completes.
-template <int VW, int VPT, int MAXT>
+// skipped and row r is written at dtable + slot[r] * cols; with PUSH (and
+// `slot`), at its owner's region instead (peer memory), and the stores are
+// fenced at system scope before the grid completes.  PUSH is a template
+// argument so that the plain VJP carries none of its registers (70 against
+// 54 per thread at float4 rows, which cost two CTAs per SM).
+template <int VW, int VPT, int MAXT, bool PUSH>
 __global__ void __launch_bounds__(MAXT) emb_rows_kernel(
     const float* __restrict__ dout_all, const int32_t* __restrict__ spos,
     const int32_t* __restrict__ offsets, const float* __restrict__ parts_all, int64_t rows,
@@ -257,15 +257,32 @@ __global__ void __launch_bounds__(MAXT) emb_rows_kernel(
   // so this grid never completes ahead of the split grid.
   const int nvec = cols / VW;
   const int64_t nblocks = (n + kSplitP - 1) / kSplitP;
+  bool remote = false;  // PUSH: this thread stored a row into another rank's memory
+  // PUSH walks the rows interleaved across their owners (row q of owner 0,
+  // of owner 1, ..., then row q + 1), so the stores into other ranks' memory
+  // spread over the whole launch instead of crowding NVLink while the rows
+  // of one shard pass.
+  int64_t span = rows;
+  if constexpr (PUSH) {
+    int64_t widest = 0;  // the largest shard: every row of every shard is visited
+    for (int q = 0; q < push->world; ++q) widest = max(widest, push->lo[q + 1] - push->lo[q]);
+    span = (int64_t)push->world * widest;
+  }
   for (int64_t o = blockIdx.z; o < outer; o += gridDim.z)
-  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+  for (int64_t j = blockIdx.x; j < span; j += gridDim.x) {
+    int64_t r = j;
+    int p = 0;
+    if constexpr (PUSH) {
+      p = (int)(j % push->world);
+      r = push->lo[p] + j / push->world;
+      if (r >= push->lo[p + 1] || r >= rows || r < 0) continue;
+    }
     const float* dout = dout_all + o * n * (int64_t)cols;
     const float* parts = parts_all + o * 2 * nblocks * (int64_t)cols;
     const int64_t s0 = offsets[r], s1 = offsets[r + 1];
     if (slot && s1 == s0) continue;
     float* dst = dtable + (slot ? (int64_t)slot[r] : o * rows + r) * (int64_t)cols;
-    if (push) {
-      const int p = push_owner(push, r);
+    if constexpr (PUSH) {
       const int64_t idx = (int64_t)slot[r] - slot[push->lo[p]];
       if (idx >= push->cap) {
         if (err && threadIdx.x == 0 && atomicCAS(err, 0, 1) == 0) {
@@ -276,6 +293,7 @@ __global__ void __launch_bounds__(MAXT) emb_rows_kernel(
         continue;
       }
       dst = push->rows[p] + idx * (int64_t)cols;
+      remote |= p != push->source;
     }
     for (int c_base = blockIdx.y * VPT * blockDim.x; c_base < nvec;
          c_base += gridDim.y * VPT * blockDim.x) {
@@ -328,7 +346,14 @@ __global__ void __launch_bounds__(MAXT) emb_rows_kernel(
     }
   }
   pdl_wait();
-  if (push) __threadfence_system();  // the peer stores are visible before the grid completes
+  if constexpr (PUSH) {
+    // The peer stores are visible at system scope before the grid completes:
+    // one fence per CTA that stored into another rank's memory, after a
+    // barrier that orders every thread's stores before it (a fence's release
+    // covers the writes that happen before it), instead of a fence in every
+    // thread, each waiting for its own stores.
+    if (__syncthreads_or(remote) && threadIdx.x == 0) __threadfence_system();
+  }
 }
 
 // ---- index_select along any dim (Tensor::index_select, lib.rs:665-703) ----------
@@ -494,7 +519,8 @@ __global__ void emb_push_meta_kernel(const int32_t* __restrict__ present,
     }
     *push->count[tid] = c < push->cap ? c : push->cap;
   }
-  __threadfence_system();
+  __syncthreads();  // one system-scope fence per CTA covers every thread's stores
+  if (threadIdx.x == 0) __threadfence_system();
 }
 
 // The owner's side of the fused exchange: region s of recv holds counts[s]
@@ -684,19 +710,22 @@ static oxc_status emb_sum_phase(const float* dout, int64_t n, int64_t rows, int6
       kEmbChunkThreads, std::max<int64_t>(32, ((cols / per_thread + 31) / 32) * 32));
   const int64_t chunks = std::min<int64_t>(65535, (cols + block * per_thread - 1) / (block * per_thread));
   const dim3 gsplit((unsigned)nblocks, (unsigned)chunks), grow(grows, (unsigned)chunks);
+#define OXC_EMB_ROWS(VW, VPT, PUSH)                                                          \
+  launch_dependent(emb_rows_kernel<VW, VPT, kEmbChunkThreads, PUSH>, grow, block, s, dout,   \
+                   vals_out, offsets, (const float*)parts, rows, (int)cols, dtable, n,       \
+                   (int64_t)1, slot, push, err)
   if (v4) {
     emb_split_kernel<4, 1, kEmbChunkThreads><<<gsplit, block, 0, s>>>(
         dout, keys_out, vals_out, offsets, n, rows, (int)cols, parts, (int64_t)1);
-    launch_dependent(emb_rows_kernel<4, 1, kEmbChunkThreads>, grow, block, s, dout, vals_out,
-                     offsets, (const float*)parts, rows, (int)cols, dtable, n, (int64_t)1,
-                     slot, push, err);
+    if (push) OXC_EMB_ROWS(4, 1, true);
+    else OXC_EMB_ROWS(4, 1, false);
   } else {
     emb_split_kernel<1, 4, kEmbChunkThreads><<<gsplit, block, 0, s>>>(
         dout, keys_out, vals_out, offsets, n, rows, (int)cols, parts, (int64_t)1);
-    launch_dependent(emb_rows_kernel<1, 4, kEmbChunkThreads>, grow, block, s, dout, vals_out,
-                     offsets, (const float*)parts, rows, (int)cols, dtable, n, (int64_t)1,
-                     slot, push, err);
+    if (push) OXC_EMB_ROWS(1, 4, true);
+    else OXC_EMB_ROWS(1, 4, false);
   }
+#undef OXC_EMB_ROWS
   return check_launch("oxc_embedding_bwd");
 }
 
@@ -1152,13 +1181,13 @@ oxc_status oxc_index_select_bwd(const float* g, const int64_t* ids, int64_t n,
   if (v4) {
     emb_split_kernel<4, 1, kEmbChunkThreads><<<gsplit, block, 0, s>>>(
         g, keys_out, vals_out, offsets, n, len, (int)inner, parts, outer);
-    launch_dependent(emb_rows_kernel<4, 1, kEmbChunkThreads>, grow, block, s, g, vals_out,
+    launch_dependent(emb_rows_kernel<4, 1, kEmbChunkThreads, false>, grow, block, s, g, vals_out,
                      offsets, (const float*)parts, len, (int)inner, gx, n, outer,
                      (const int32_t*)nullptr, (const oxc_emb_push*)nullptr, (int32_t*)nullptr);
   } else {
     emb_split_kernel<1, 4, kEmbChunkThreads><<<gsplit, block, 0, s>>>(
         g, keys_out, vals_out, offsets, n, len, (int)inner, parts, outer);
-    launch_dependent(emb_rows_kernel<1, 4, kEmbChunkThreads>, grow, block, s, g, vals_out,
+    launch_dependent(emb_rows_kernel<1, 4, kEmbChunkThreads, false>, grow, block, s, g, vals_out,
                      offsets, (const float*)parts, len, (int)inner, gx, n, outer,
                      (const int32_t*)nullptr, (const oxc_emb_push*)nullptr, (int32_t*)nullptr);
   }

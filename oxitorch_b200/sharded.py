@@ -407,7 +407,7 @@ class PeerGradExchange:
         self.push = []
         for k in range(slots):
             tab = N.EmbPush()
-            tab.world, tab.cap = G, cap
+            tab.world, tab.source, tab.cap = G, self.rank, cap
             for p in range(G + 1):
                 tab.lo[p] = self.v * p // G
             for p in range(G):
