@@ -178,6 +178,95 @@ def test_embedding_sparse_exchange_emulated(oracle):
         assert int(flag[0]) == 0
 
 
+def _push_table(N, world, source, cap, bounds, rrows, rids, rcount, d):
+    """The oxc_emb_push table of `source` (device memory): for every owner p,
+    this source's part of p's receive regions."""
+    import torch
+    tab = N.EmbPush()
+    tab.world, tab.source, tab.cap = world, source, cap
+    for p in range(world + 1):
+        tab.lo[p] = bounds[p]
+    for p in range(world):
+        tab.rows[p] = rrows[p].data_ptr() + source * cap * d * 4
+        tab.ids[p] = rids[p].data_ptr() + source * cap * 4
+        tab.count[p] = rcount[p].data_ptr() + source * 8
+    return torch.tensor(list(bytes(tab)), dtype=torch.uint8).to("cuda")
+
+
+@pytest.mark.parametrize("d", [512, 37])
+def test_embedding_push_exchange_emulated(d):
+    """The fused exchange (oxc_embedding_bwd_push + the owners'
+    oxc_embedding_exchange_reduce_regions) with three ranks emulated on one
+    GPU, every owner's receive regions in this GPU's memory: the regions hold
+    each source's touched ids of that owner's shard (ascending) and their
+    counts, and every owner's dense shard is bit for bit the one the NCCL route
+    gives (compact VJP, rows routed in source order,
+    oxc_embedding_exchange_reduce).  A vocabulary that does not split evenly
+    and odd rows (d = 37, the scalar path) included; two rounds over the same
+    regions, the second with other gradients."""
+    import torch
+    from oxitorch_b200 import _native as N
+    from oxitorch_b200 import functional as F
+    from oxitorch_b200 import sharded as S
+    L = N.load()
+    rng = np.random.default_rng(25)
+    V, n, G = 3001, 20000, 3
+    ids = np.minimum(rng.zipf(1.1, n) - 1, V - 1).astype(np.int64)
+    ids[::89] -= V  # negative ids count from the end
+    res = np.where(ids < 0, ids + V, ids)
+    bounds = [V * p // G for p in range(G + 1)]
+    cap = -(-V // G)
+    rrows = [torch.empty(G * cap * d, device="cuda") for _ in range(G)]
+    rids = [torch.full((G * cap,), -7, dtype=torch.int32, device="cuda") for _ in range(G)]
+    rcount = [torch.full((G,), -1, dtype=torch.int64, device="cuda") for _ in range(G)]
+    tabs = [_push_table(N, G, g, cap, bounds, rrows, rids, rcount, d) for g in range(G)]
+    flag = torch.zeros(4, dtype=torch.int32, device="cuda")
+    ws_bytes = L.oxc_embedding_bwd_compact_workspace_size(n, V, d)
+    ws = F._workspace(ws_bytes, torch.device("cuda"))
+    for rnd in range(2):
+        dout = (rng.standard_normal((n, d)) * (rnd + 1)).astype(np.float32)
+        shards = [S.shard_range(n, g, G) for g in range(G)]
+        d_in = [(_dev(ids[lo:hi]), _dev(dout[lo:hi])) for lo, hi in shards]
+        for g, (lo, hi) in enumerate(shards):
+            N.check(L.oxc_embedding_bwd_push(
+                d_in[g][1].data_ptr(), d_in[g][0].data_ptr(), hi - lo, V, d, tabs[g].data_ptr(),
+                flag.data_ptr(), ws.data_ptr(), ws_bytes, F._stream()), "push")
+        sends = [_compact(ids[lo:hi], dout[lo:hi], V, G) for lo, hi in shards]
+        for p in range(G):
+            lo_p, rows_p = S.vocab_shard(V, p, G)
+            assert (lo_p, lo_p + rows_p) == (bounds[p], bounds[p + 1])
+            cnt = _host(rcount[p])
+            rid_h = _host(rids[p]).reshape(G, cap)
+            for g, (glo, ghi) in enumerate(shards):
+                u = np.unique(res[glo:ghi])
+                u = u[(u >= bounds[p]) & (u < bounds[p + 1])]
+                assert cnt[g] == u.size, (p, g)
+                assert np.array_equal(rid_h[g, :u.size], u), (p, g)
+            ws2 = F._workspace(L.oxc_embedding_exchange_reduce_workspace_size(G, rows_p),
+                               torch.device("cuda"))
+            got = torch.empty(rows_p, d, device="cuda")
+            N.check(L.oxc_embedding_exchange_reduce_regions(
+                rids[p].data_ptr(), rrows[p].data_ptr(), rcount[p].data_ptr(), G, cap, lo_p,
+                rows_p, d, got.data_ptr(), flag.data_ptr(), ws2.data_ptr(), ws2.numel(),
+                F._stream()), "reduce regions")
+            # the NCCL route's owner reduce over the same rows in source order
+            rid, rrow, off = [], [], [0]
+            for oid, orow, k, sc in sends:
+                a = int(sc[:p].sum())
+                rid.append(oid[a:a + sc[p]])
+                rrow.append(orow[a:a + sc[p]])
+                off.append(off[-1] + int(sc[p]))
+            d_rid = _dev(np.concatenate(rid).astype(np.int32))
+            d_rrow = _dev(np.concatenate(rrow))
+            d_off = _dev(np.array(off, np.int64))
+            want = torch.empty(rows_p, d, device="cuda")
+            N.check(L.oxc_embedding_exchange_reduce(
+                d_rid.data_ptr(), d_rrow.data_ptr(), d_off.data_ptr(), G, lo_p, rows_p, d,
+                want.data_ptr(), flag.data_ptr(), ws2.data_ptr(), ws2.numel(), F._stream()))
+            assert_bitexact(_host(got), _host(want), f"owner {p} shard, round {rnd}")
+        assert int(flag.abs().sum().item()) == 0
+
+
 # ---- real NCCL ranks ---------------------------------------------------------------------
 
 def _free_port():
