@@ -576,7 +576,7 @@ class LnGelu(Workload):
 class Rms(Workload):
     DESC = "rms_norm fwd+bwd, fp32, x [4096, 4096] per GPU (BASELINE config 1)"
     CONFIG = 1
-    KERNEL = "rms_bwd_kernel (RMSNorm VJP) + dweight finisher"
+    KERNEL = "rms_bwd_stream_kernel (RMSNorm VJP) + dweight finisher"
     launches = 3
     SETS = 3  # rotating input/output sets: 3 x 268 MB, far more than the 126 MB L2
 
