@@ -839,6 +839,9 @@ class Embedding(Workload):
         lo, rows = self.ex.lo, self.ex.shard_rows
         if self.v % self.world:
             return {"ok": None, "what": "vocab not divisible by the ranks: not checked"}
+        cyclic = getattr(self.ex, "cyclic", False)
+        if cyclic:  # owner p's rows p, p + N, ...: order the table owner-major
+            part = part.view(self.v // self.world, self.world, self.d).transpose(0, 1).contiguous()
         want = t.empty(rows, self.d, dtype=t.float64, device=self.dev)
         dist.reduce_scatter_tensor(want, part)
         tol = t.empty_like(want)
@@ -849,15 +852,18 @@ class Embedding(Workload):
         ok = bool((err <= tol).all().item()) and int(flag.abs().sum().item()) == 0 \
             and int(self.ex.flag.abs().sum().item()) == 0
         worst = float((err / tol).max().item())
-        return {"ok": ok, "worst_err_over_tolerance": worst, "shard_rows": [lo, lo + rows],
+        return {"ok": ok, "worst_err_over_tolerance": worst,
+                "shard_rows": (f"{lo}, {lo} + {self.world}, ... ({rows} rows)" if cyclic
+                               else [lo, lo + rows]),
                 "what": "exchanged dtable shard vs the f64 reduce-scatter of every rank's dense "
                         "single-GPU VJP, tolerance 1e-6 x sum over ranks of |partial|"}
 
     def _exchange_desc(self):
         if self.exchange_kind == "peer":
-            return ("fused exchange: the VJP kernel stores each touched row into its vocab "
-                    "shard owner's memory over NVLink (CUDA IPC peer memory), a stream-ordered "
-                    "barrier, the owner's rank-order sum")
+            return ("fused exchange: the VJP kernel stores each touched row into its owner's "
+                    "memory over NVLink (CUDA IPC peer memory; rows owned cyclically, row r by "
+                    "rank r mod N, which spreads the Zipf-hot low ids), a stream-ordered barrier, "
+                    "the owner's rank-order sum")
         why = getattr(self, "exchange_fallback", None)
         return ("compact VJP + NCCL all-to-all of the touched rows to their vocab shard's owner "
                 "+ rank-order sum (sparse exchange)" + (f"; peer memory unavailable: {why}"

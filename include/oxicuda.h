@@ -448,23 +448,30 @@ oxc_status oxc_comm_alltoallv(oxc_comm* comm, const void* send, const int64_t* s
 /* ---- the fused exchange over peer memory --------------------------------------
  * No counterpart in the reference.  The VJP of a replicated table with
  * token-sharded ids that delivers its rows itself: each occurring row's sum is
- * stored straight into the receive region of the rank that owns the row's
- * vocab shard, over NVLink (peer memory mapped with oxc_ipc_import), so the
- * transfer overlaps the sums and nothing waits on the host.  oxc_emb_push
- * (device memory, built once by the host) names, for this source rank, every
- * owner's region: rows [cap][cols], ids [cap], and the owner's count slot for
- * this source.  After every rank's oxc_embedding_bwd_push, a stream-ordered
- * barrier across the ranks (any collective: its completion on a rank implies
- * every rank's earlier kernels, whose peer stores are fenced at system scope,
- * have completed), then each owner runs oxc_embedding_exchange_reduce_regions
- * over its own regions: source s at [s * cap, s * cap + counts[s]).  A row
+ * stored straight into the receive region of the rank that owns the row, over
+ * NVLink (peer memory mapped with oxc_ipc_import), so the transfer overlaps
+ * the sums and nothing waits on the host.  Ownership: cyclic = 0, owner p holds
+ * table rows [lo[p], lo[p+1]); cyclic = 1, owner p holds rows p, p + world,
+ * p + 2 world, ... (lo unused), which spreads Zipf-hot low ids over every
+ * owner.  oxc_emb_push (device memory, built once by the host) names, for this
+ * source rank, every owner's region: rows [cap][cols], ids [cap], and the
+ * owner's count slot for this source; cap is at least the largest shard's row
+ * count.  After every rank's oxc_embedding_bwd_push, a stream-ordered barrier
+ * across the ranks (any collective: its completion on a rank implies every
+ * rank's earlier kernels, whose peer stores are fenced at system scope, have
+ * completed), then each owner runs oxc_embedding_exchange_reduce_regions over
+ * its own regions (source s at [s * cap, s * cap + counts[s])) into its dense
+ * shard: row v of it is table row shard_lo + v * shard_stride (contiguous:
+ * shard_lo = lo[p], stride 1; cyclic: shard_lo = p, stride = world).  A row
  * beyond `cap` for one owner is recorded in err_flag and not sent. */
 #define OXC_PUSH_MAX_RANKS 16
 typedef struct oxc_emb_push {
   int32_t world;
   int32_t source;  /* this (source) rank: stores to its own region need no system-scope fence */
+  int32_t cyclic;  /* 1: owner p holds rows p, p + world, ...; 0: rows [lo[p], lo[p+1]) */
+  int32_t reserved;
   int64_t cap;
-  int64_t lo[OXC_PUSH_MAX_RANKS + 1];  /* owner p holds table rows [lo[p], lo[p+1]) */
+  int64_t lo[OXC_PUSH_MAX_RANKS + 1];  /* contiguous ownership: owner p's first row, lo[world] = rows */
   float* rows[OXC_PUSH_MAX_RANKS];
   int32_t* ids[OXC_PUSH_MAX_RANKS];
   int64_t* count[OXC_PUSH_MAX_RANKS];
@@ -476,9 +483,10 @@ oxc_status oxc_embedding_bwd_push(const float* dout, const int64_t* ids, int64_t
 oxc_status oxc_embedding_exchange_reduce_regions(const int32_t* recv_ids, const float* recv_rows,
                                                  const int64_t* counts, int32_t sources,
                                                  int64_t cap, int64_t shard_lo,
-                                                 int64_t shard_rows, int64_t cols, float* dshard,
-                                                 int32_t* err_flag, void* workspace,
-                                                 size_t workspace_bytes, void* stream);
+                                                 int64_t shard_stride, int64_t shard_rows,
+                                                 int64_t cols, float* dshard, int32_t* err_flag,
+                                                 void* workspace, size_t workspace_bytes,
+                                                 void* stream);
 /* Device memory shared between the processes of one node: oxc_ipc_export gives
  * the handle of the allocation holding dev_ptr and dev_ptr's byte offset in it;
  * oxc_ipc_import maps it into another process (peer access enabled) and

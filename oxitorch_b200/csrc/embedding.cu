@@ -229,13 +229,40 @@ __global__ void __launch_bounds__(MAXT) emb_split_kernel(
   }
 }
 
-// Owner of table row r under a push table, and r's index in the owner's
-// region for this source: the owner's rows come consecutively in the compact
-// order, so the index is r's slot minus the slot of the owner's first row.
+// Ownership under a push table.  Contiguous shards: owner p holds rows
+// [lo[p], lo[p+1]).  Cyclic: owner p holds rows p, p + world, p + 2 world, ...
+// The presence scan runs in owner-major order, so each owner's occurring rows
+// take consecutive slots: position push_pos(r) in that order, owner p's first
+// position push_base(p).  Contiguous: the order of the rows themselves.
+// Cyclic: p * span + r / world, span = ceil(rows / world) positions per owner,
+// the positions past the last row of an owner empty.  Every position is below
+// rows + OXC_PUSH_MAX_RANKS.  r's index in its owner's region for this source
+// is then slot[push_pos(r)] - slot[push_base(p)].
 __device__ __forceinline__ int push_owner(const oxc_emb_push* __restrict__ push, int64_t r) {
+  if (push->cyclic) return (int)(r % push->world);
   int p = 0;
   while (p + 1 < push->world && r >= push->lo[p + 1]) ++p;
   return p;
+}
+__device__ __forceinline__ int64_t push_span(const oxc_emb_push* __restrict__ push, int64_t rows) {
+  return (rows + push->world - 1) / push->world;
+}
+__device__ __forceinline__ int64_t push_pos(const oxc_emb_push* __restrict__ push, int64_t r,
+                                            int64_t rows) {
+  if (!push->cyclic) return r;
+  return (r % push->world) * push_span(push, rows) + r / push->world;
+}
+__device__ __forceinline__ int64_t push_base(const oxc_emb_push* __restrict__ push, int p,
+                                             int64_t rows) {
+  return push->cyclic ? (int64_t)p * push_span(push, rows) : push->lo[p];
+}
+// The table row at owner-major position q, or -1 (an empty cyclic position).
+__device__ __forceinline__ int64_t push_row_at(const oxc_emb_push* __restrict__ push, int64_t q,
+                                               int64_t rows) {
+  if (!push->cyclic) return q < rows ? q : -1;
+  const int64_t span = push_span(push, rows);
+  const int64_t r = (q % span) * push->world + q / span;
+  return q / span < push->world && r < rows ? r : -1;
 }
 
 // With `slot` (the compact VJP, outer == 1), rows without occurrences are
@@ -262,20 +289,27 @@ __global__ void __launch_bounds__(MAXT) emb_rows_kernel(
   // of owner 1, ..., then row q + 1), so the stores into other ranks' memory
   // spread over the whole launch instead of crowding NVLink while the rows
   // of one shard pass.
+  // (Cyclic ownership interleaves the owners in row order already.)
   int64_t span = rows;
   if constexpr (PUSH) {
-    int64_t widest = 0;  // the largest shard: every row of every shard is visited
-    for (int q = 0; q < push->world; ++q) widest = max(widest, push->lo[q + 1] - push->lo[q]);
-    span = (int64_t)push->world * widest;
+    if (!push->cyclic) {
+      int64_t widest = 0;  // the largest shard: every row of every shard is visited
+      for (int q = 0; q < push->world; ++q) widest = max(widest, push->lo[q + 1] - push->lo[q]);
+      span = (int64_t)push->world * widest;
+    }
   }
   for (int64_t o = blockIdx.z; o < outer; o += gridDim.z)
   for (int64_t j = blockIdx.x; j < span; j += gridDim.x) {
     int64_t r = j;
     int p = 0;
     if constexpr (PUSH) {
-      p = (int)(j % push->world);
-      r = push->lo[p] + j / push->world;
-      if (r >= push->lo[p + 1] || r >= rows || r < 0) continue;
+      if (push->cyclic) {
+        p = (int)(j % push->world);
+      } else {
+        p = (int)(j % push->world);
+        r = push->lo[p] + j / push->world;
+        if (r >= push->lo[p + 1] || r >= rows || r < 0) continue;
+      }
     }
     const float* dout = dout_all + o * n * (int64_t)cols;
     const float* parts = parts_all + o * 2 * nblocks * (int64_t)cols;
@@ -283,7 +317,8 @@ __global__ void __launch_bounds__(MAXT) emb_rows_kernel(
     if (slot && s1 == s0) continue;
     float* dst = dtable + (slot ? (int64_t)slot[r] : o * rows + r) * (int64_t)cols;
     if constexpr (PUSH) {
-      const int64_t idx = (int64_t)slot[r] - slot[push->lo[p]];
+      const int64_t idx =
+          (int64_t)slot[push_pos(push, r, rows)] - slot[push_base(push, p, rows)];
       if (idx >= push->cap) {
         if (err && threadIdx.x == 0 && atomicCAS(err, 0, 1) == 0) {
           err[1] = (int32_t)r;
@@ -495,47 +530,72 @@ __global__ void emb_compact_meta_kernel(const int32_t* __restrict__ present,
   }
 }
 
+// The push presence flags in owner-major order (push_pos): position q holds 1
+// if its table row occurs; the positions past the rows, up to rows +
+// OXC_PUSH_MAX_RANKS, hold 0, so the exclusive scan of all of them defines
+// slot[q] for every position an owner's bounds can name.
+__global__ void emb_push_present_kernel(const int32_t* __restrict__ offsets, int64_t rows,
+                                        const oxc_emb_push* __restrict__ push,
+                                        int32_t* __restrict__ present) {
+  const int64_t len = rows + OXC_PUSH_MAX_RANKS;
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < len;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = push_row_at(push, q, rows);
+    present[q] = r >= 0 && offsets[r + 1] > offsets[r] ? 1 : 0;
+  }
+}
+
 // The push meta: every occurring row's id into its owner's id region, and
-// each owner's count of this source's rows (prefix sums at the shard bounds).
+// each owner's count of this source's rows (differences of the owner-major
+// slots at the owners' bounds).
 __global__ void emb_push_meta_kernel(const int32_t* __restrict__ present,
                                      const int32_t* __restrict__ slot, int64_t rows,
                                      const oxc_emb_push* __restrict__ push, int32_t* err) {
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  auto pre = [&](int64_t r) -> int64_t {
-    return r >= rows ? (int64_t)slot[rows - 1] + present[rows - 1] : slot[r];
+  const int64_t len = rows + OXC_PUSH_MAX_RANKS;
+  auto pre = [&](int64_t q) -> int64_t {
+    q = q < 0 ? 0 : q;
+    return q >= len ? (int64_t)slot[len - 1] + present[len - 1] : slot[q];
   };
-  for (int64_t r = tid; r < rows; r += (int64_t)gridDim.x * blockDim.x) {
-    if (!present[r]) continue;
+  for (int64_t q = tid; q < len; q += (int64_t)gridDim.x * blockDim.x) {
+    if (!present[q]) continue;
+    const int64_t r = push_row_at(push, q, rows);
     const int p = push_owner(push, r);
-    const int64_t idx = (int64_t)slot[r] - pre(push->lo[p]);
+    const int64_t idx = (int64_t)slot[q] - pre(push_base(push, p, rows));
     if (idx < push->cap) push->ids[p][idx] = (int32_t)r;
   }
   if (tid < push->world) {
-    const int64_t c = pre(push->lo[tid + 1]) - pre(push->lo[tid]);
+    const int p = (int)tid;
+    const int64_t hi = p + 1 < push->world ? push_base(push, p + 1, rows)
+                       : (push->cyclic ? push->world * push_span(push, rows) : push->lo[p + 1]);
+    const int64_t c = pre(hi) - pre(push_base(push, p, rows));
     if (c > push->cap && err && atomicCAS(err, 0, 1) == 0) {
       err[1] = (int32_t)c;
       err[2] = 0;
       err[3] = (int32_t)push->cap;
     }
-    *push->count[tid] = c < push->cap ? c : push->cap;
+    *push->count[p] = c < push->cap ? c : push->cap;
   }
   __syncthreads();  // one system-scope fence per CTA covers every thread's stores
   if (threadIdx.x == 0) __threadfence_system();
 }
 
 // The owner's side of the fused exchange: region s of recv holds counts[s]
-// rows; map[s * shard_rows + v] = the region index of row shard_lo + v, or -1.
+// rows; map[s * shard_rows + v] = the region index of table row shard_lo +
+// v * shard_stride (the owner's shard row v), or -1.
 __global__ void emb_region_map_kernel(const int32_t* __restrict__ recv_ids,
                                       const int64_t* __restrict__ counts, int32_t sources,
-                                      int64_t cap, int64_t shard_lo, int64_t shard_rows,
-                                      int32_t* __restrict__ map, int32_t* err) {
+                                      int64_t cap, int64_t shard_lo, int64_t shard_stride,
+                                      int64_t shard_rows, int32_t* __restrict__ map,
+                                      int32_t* err) {
   const int64_t total = (int64_t)sources * cap;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t s = i / cap, k = i - s * cap;
     if (k >= counts[s]) continue;
-    const int64_t v = (int64_t)recv_ids[i] - shard_lo;
-    if (v < 0 || v >= shard_rows) {
+    const int64_t d = (int64_t)recv_ids[i] - shard_lo;
+    const int64_t v = d / shard_stride;
+    if (d < 0 || d % shard_stride != 0 || v >= shard_rows) {
       if (err && atomicCAS(err, 0, 1) == 0) {
         err[1] = recv_ids[i];
         err[2] = 0;
@@ -636,11 +696,14 @@ static oxc_status emb_layout(int64_t n, int64_t rows, int64_t cols, EmbLayout* L
   L->present = L->slot = L->scan = L->scan_bytes = 0;
   if (compact) {
     size_t scan_bytes = 0;
+    // rows + OXC_PUSH_MAX_RANKS positions: the owner-major order of the push
+    // VJP (cyclic ownership pads each owner's positions to the same span)
+    const int64_t positions = rows + OXC_PUSH_MAX_RANKS;
     e = cub::DeviceScan::ExclusiveSum(nullptr, scan_bytes, (const int32_t*)nullptr,
-                                      (int32_t*)nullptr, (int)std::max<int64_t>(rows, 1));
+                                      (int32_t*)nullptr, (int)positions);
     if (e != cudaSuccess) return cuda_fail(e, "embedding backward (scan workspace size)");
-    L->present = off; off += align256((size_t)(rows + 1) * 4);
-    L->slot = off; off += align256((size_t)(rows + 1) * 4);
+    L->present = off; off += align256((size_t)(positions + 1) * 4);
+    L->slot = off; off += align256((size_t)(positions + 1) * 4);
     L->scan = off; off += align256(scan_bytes);
     L->scan_bytes = scan_bytes;
   }
@@ -955,12 +1018,15 @@ oxc_status oxc_embedding_bwd_push(const float* dout, const int64_t* ids, int64_t
   int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
   int32_t* present = reinterpret_cast<int32_t*>(ws + L.present);
   int32_t* slot = reinterpret_cast<int32_t*>(ws + L.slot);
-  const unsigned gr = (unsigned)std::min<int64_t>((rows + 255) / 256, (int64_t)sm_count() * 8);
-  emb_present_kernel<<<gr, 256, 0, s>>>(offsets, rows, present);
+  const int64_t positions = rows + OXC_PUSH_MAX_RANKS;
+  const unsigned gr =
+      (unsigned)std::min<int64_t>((positions + 255) / 256, (int64_t)sm_count() * 8);
+  emb_push_present_kernel<<<gr, 256, 0, s>>>(offsets, rows, push, present);
   st = check_launch("oxc_embedding_bwd_push (present)");
   if (st) return st;
   size_t scan_bytes = L.scan_bytes;
-  cudaError_t e = cub::DeviceScan::ExclusiveSum(ws + L.scan, scan_bytes, present, slot, (int)rows, s);
+  cudaError_t e =
+      cub::DeviceScan::ExclusiveSum(ws + L.scan, scan_bytes, present, slot, (int)positions, s);
   if (e != cudaSuccess) return cuda_fail(e, "oxc_embedding_bwd_push (scan)");
   emb_push_meta_kernel<<<gr, 256, 0, s>>>(present, slot, rows, push, err_flag);
   st = check_launch("oxc_embedding_bwd_push (meta)");
@@ -972,11 +1038,12 @@ oxc_status oxc_embedding_bwd_push(const float* dout, const int64_t* ids, int64_t
 oxc_status oxc_embedding_exchange_reduce_regions(const int32_t* recv_ids, const float* recv_rows,
                                                  const int64_t* counts, int32_t sources,
                                                  int64_t cap, int64_t shard_lo,
-                                                 int64_t shard_rows, int64_t cols, float* dshard,
-                                                 int32_t* err_flag, void* workspace,
-                                                 size_t workspace_bytes, void* stream) {
+                                                 int64_t shard_stride, int64_t shard_rows,
+                                                 int64_t cols, float* dshard, int32_t* err_flag,
+                                                 void* workspace, size_t workspace_bytes,
+                                                 void* stream) {
   const char* fn = "embedding gradient exchange (regions)";
-  if (sources <= 0 || cap < 0 || shard_rows < 0 || cols < 0 || shard_lo < 0)
+  if (sources <= 0 || cap < 0 || shard_rows < 0 || cols < 0 || shard_lo < 0 || shard_stride < 1)
     return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: bad sizes", fn);
   if (shard_rows >= 0x7fffffff || cols > 0x7fffffff || (int64_t)sources * cap >= 0x7fffffff ||
       (int64_t)sources * shard_rows >= 0x7fffffff)
@@ -994,9 +1061,8 @@ oxc_status oxc_embedding_exchange_reduce_regions(const int32_t* recv_ids, const 
   cudaError_t e = cudaMemsetAsync(map, 0xff, (size_t)sources * shard_rows * sizeof(int32_t), s);
   if (e != cudaSuccess) return cuda_fail(e, "oxc_embedding_exchange_reduce_regions");
   if (cap > 0) {
-    emb_region_map_kernel<<<(unsigned)sm_count() * 4, 256, 0, s>>>(recv_ids, counts, sources, cap,
-                                                                   shard_lo, shard_rows, map,
-                                                                   err_flag);
+    emb_region_map_kernel<<<(unsigned)sm_count() * 4, 256, 0, s>>>(
+        recv_ids, counts, sources, cap, shard_lo, shard_stride, shard_rows, map, err_flag);
     oxc_status st = check_launch("oxc_embedding_exchange_reduce_regions (map)");
     if (st) return st;
   }

@@ -316,12 +316,18 @@ class PeerGradExchange:
     owner's rank-order sum (``oxc_embedding_exchange_reduce_regions``) on a
     communication stream; it returns the dense gradient shard and an event.
 
+    Ownership: ``cyclic`` (the default) gives rank p the table rows p, p + N,
+    p + 2N, ... (N ranks), so its dense shard's row v is table row p + v * N;
+    a Zipf id stream touches its low ids most, and cyclic ownership spreads
+    them, and the NVLink traffic they bring, over every owner.  ``cyclic=False``
+    gives rank p the contiguous ``vocab_shard`` rows.
+
     Ordering across steps: a source writes a slot's regions again two steps
     later, after the barrier of the step in between (``vjp`` waits for it),
     which every owner enters only after its reduce of that slot (both run in
     order on the owner's communication stream)."""
 
-    def __init__(self, n, vocab_total, cols, device, group=None, slots=2):
+    def __init__(self, n, vocab_total, cols, device, group=None, slots=2, cyclic=True):
         import ctypes
         import math
         from . import _native as N
@@ -337,7 +343,13 @@ class PeerGradExchange:
         self.n, self.v, self.d, self.dev, self.slots = int(n), int(vocab_total), int(cols), \
             device, slots
         self.cap = math.ceil(self.v / self.world)  # rows of the largest vocab shard
-        self.lo, self.shard_rows = vocab_shard(self.v, self.rank, self.world)
+        self.cyclic = bool(cyclic)
+        if self.cyclic:  # rows rank, rank + N, ...
+            self.lo, self.stride = self.rank, self.world
+            self.shard_rows = (self.v - self.rank + self.world - 1) // self.world
+        else:
+            self.lo, self.shard_rows = vocab_shard(self.v, self.rank, self.world)
+            self.stride = 1
         G, cap, d = self.world, self.cap, self.d
         t = torch
         self.rrows = [t.empty(G * cap * d, dtype=t.float32, device=device) for _ in range(slots)]
@@ -407,7 +419,7 @@ class PeerGradExchange:
         self.push = []
         for k in range(slots):
             tab = N.EmbPush()
-            tab.world, tab.source, tab.cap = G, self.rank, cap
+            tab.world, tab.source, tab.cyclic, tab.cap = G, self.rank, int(self.cyclic), cap
             for p in range(G + 1):
                 tab.lo[p] = self.v * p // G
             for p in range(G):
@@ -446,7 +458,8 @@ class PeerGradExchange:
             self.passed.record(self.comm)
             self.N.check(self.L.oxc_embedding_exchange_reduce_regions(
                 self.rids[slot].data_ptr(), self.rrows[slot].data_ptr(),
-                self.rcount[slot].data_ptr(), self.world, self.cap, self.lo, self.shard_rows,
+                self.rcount[slot].data_ptr(), self.world, self.cap, self.lo, self.stride,
+                self.shard_rows,
                 self.d, self.dshard[slot].data_ptr(), self.flag.data_ptr(),
                 self.ws2[slot].data_ptr(), self.ws2_bytes, self.comm.cuda_stream),
                 "embedding gradient exchange")

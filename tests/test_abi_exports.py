@@ -81,3 +81,39 @@ def test_cpu_tensors_are_rejected_before_any_launch():
     x = torch.zeros(2, 4)
     with pytest.raises(ValueError, match="CUDA"):
         F.rms_norm_fwd(x, torch.ones(4))
+
+
+def test_struct_mirrors_match_the_header(tmp_path):
+    """The ctypes mirrors of the ABI's structs have the header's size and
+    field offsets (compiled with gcc against include/oxicuda.h)."""
+    import shutil
+    import subprocess
+    from oxitorch_b200 import _native as N
+    if not shutil.which("gcc"):
+        pytest.skip("gcc not available")
+    checks = {
+        "oxc_view": (N.View, ["data", "ndim", "shape", "strides"]),
+        "oxc_emb_push": (N.EmbPush, ["world", "source", "cyclic", "cap", "lo", "rows", "ids",
+                                     "count"]),
+    }
+    lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "oxicuda.h"',
+             "int main(void) {"]
+    for cname, (_, fields) in checks.items():
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for f in fields:
+            lines.append(f'  printf("{cname} {f} %zu\\n", offsetof({cname}, {f}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    cuda_inc = "/usr/local/cuda/include"
+    subprocess.check_call(["gcc", "-I", os.path.join(ROOT, "include"), "-I", cuda_inc,
+                           str(src), "-o", str(exe)])
+    got = {}
+    for line in subprocess.check_output([str(exe)], text=True).splitlines():
+        cname, key, val = line.split()
+        got[(cname, key)] = int(val)
+    for cname, (cls, fields) in checks.items():
+        assert got[(cname, "size")] == ctypes.sizeof(cls), cname
+        for f in fields:
+            assert got[(cname, f)] == getattr(cls, f).offset, (cname, f)

@@ -178,12 +178,12 @@ def test_embedding_sparse_exchange_emulated(oracle):
         assert int(flag[0]) == 0
 
 
-def _push_table(N, world, source, cap, bounds, rrows, rids, rcount, d):
+def _push_table(N, world, source, cap, bounds, rrows, rids, rcount, d, cyclic):
     """The oxc_emb_push table of `source` (device memory): for every owner p,
     this source's part of p's receive regions."""
     import torch
     tab = N.EmbPush()
-    tab.world, tab.source, tab.cap = world, source, cap
+    tab.world, tab.source, tab.cyclic, tab.cap = world, source, int(cyclic), cap
     for p in range(world + 1):
         tab.lo[p] = bounds[p]
     for p in range(world):
@@ -193,17 +193,20 @@ def _push_table(N, world, source, cap, bounds, rrows, rids, rcount, d):
     return torch.tensor(list(bytes(tab)), dtype=torch.uint8).to("cuda")
 
 
+@pytest.mark.parametrize("cyclic", [False, True])
 @pytest.mark.parametrize("d", [512, 37])
-def test_embedding_push_exchange_emulated(d):
+def test_embedding_push_exchange_emulated(d, cyclic):
     """The fused exchange (oxc_embedding_bwd_push + the owners'
     oxc_embedding_exchange_reduce_regions) with three ranks emulated on one
-    GPU, every owner's receive regions in this GPU's memory: the regions hold
-    each source's touched ids of that owner's shard (ascending) and their
-    counts, and every owner's dense shard is bit for bit the one the NCCL route
-    gives (compact VJP, rows routed in source order,
-    oxc_embedding_exchange_reduce).  A vocabulary that does not split evenly
-    and odd rows (d = 37, the scalar path) included; two rounds over the same
-    regions, the second with other gradients."""
+    GPU, every owner's receive regions in this GPU's memory, for contiguous
+    and cyclic ownership: the regions hold each source's touched ids of that
+    owner (ascending) and their counts, and every owner's dense shard is, bit
+    for bit, the sum in source order from 0.0 of the sources' rows -- each
+    source's rows being its single-GPU dense VJP's.  With contiguous
+    ownership the shard is also the NCCL route's (compact VJP, rows routed in
+    source order, oxc_embedding_exchange_reduce).  A vocabulary that does not
+    split evenly and odd rows (d = 37, the scalar path) included; two rounds
+    over the same regions, the second with other gradients."""
     import torch
     from oxitorch_b200 import _native as N
     from oxitorch_b200 import functional as F
@@ -216,54 +219,68 @@ def test_embedding_push_exchange_emulated(d):
     res = np.where(ids < 0, ids + V, ids)
     bounds = [V * p // G for p in range(G + 1)]
     cap = -(-V // G)
+
+    def owned(p):  # table rows of owner p, ascending
+        return np.arange(p, V, G) if cyclic else np.arange(bounds[p], bounds[p + 1])
+
     rrows = [torch.empty(G * cap * d, device="cuda") for _ in range(G)]
     rids = [torch.full((G * cap,), -7, dtype=torch.int32, device="cuda") for _ in range(G)]
     rcount = [torch.full((G,), -1, dtype=torch.int64, device="cuda") for _ in range(G)]
-    tabs = [_push_table(N, G, g, cap, bounds, rrows, rids, rcount, d) for g in range(G)]
+    tabs = [_push_table(N, G, g, cap, bounds, rrows, rids, rcount, d, cyclic) for g in range(G)]
     flag = torch.zeros(4, dtype=torch.int32, device="cuda")
     ws_bytes = L.oxc_embedding_bwd_compact_workspace_size(n, V, d)
     ws = F._workspace(ws_bytes, torch.device("cuda"))
+    shards = [S.shard_range(n, g, G) for g in range(G)]
     for rnd in range(2):
         dout = (rng.standard_normal((n, d)) * (rnd + 1)).astype(np.float32)
-        shards = [S.shard_range(n, g, G) for g in range(G)]
         d_in = [(_dev(ids[lo:hi]), _dev(dout[lo:hi])) for lo, hi in shards]
         for g, (lo, hi) in enumerate(shards):
             N.check(L.oxc_embedding_bwd_push(
                 d_in[g][1].data_ptr(), d_in[g][0].data_ptr(), hi - lo, V, d, tabs[g].data_ptr(),
                 flag.data_ptr(), ws.data_ptr(), ws_bytes, F._stream()), "push")
-        sends = [_compact(ids[lo:hi], dout[lo:hi], V, G) for lo, hi in shards]
+        # the expected sums: every source's dense VJP rows, added in source order from 0.0
+        expect = np.zeros((V, d), np.float32)
+        touched = []
+        for g, (lo, hi) in enumerate(shards):
+            dense, _ = F.embedding_bwd(d_in[g][0], d_in[g][1], V)
+            u = np.unique(res[lo:hi])
+            touched.append(u)
+            expect[u] = expect[u] + _host(dense)[u]
         for p in range(G):
-            lo_p, rows_p = S.vocab_shard(V, p, G)
-            assert (lo_p, lo_p + rows_p) == (bounds[p], bounds[p + 1])
+            rows_p = owned(p)
             cnt = _host(rcount[p])
             rid_h = _host(rids[p]).reshape(G, cap)
-            for g, (glo, ghi) in enumerate(shards):
-                u = np.unique(res[glo:ghi])
-                u = u[(u >= bounds[p]) & (u < bounds[p + 1])]
+            for g in range(G):
+                u = np.intersect1d(touched[g], rows_p)
                 assert cnt[g] == u.size, (p, g)
                 assert np.array_equal(rid_h[g, :u.size], u), (p, g)
-            ws2 = F._workspace(L.oxc_embedding_exchange_reduce_workspace_size(G, rows_p),
+            lo_p, stride = (p, G) if cyclic else (bounds[p], 1)
+            ws2 = F._workspace(L.oxc_embedding_exchange_reduce_workspace_size(G, rows_p.size),
                                torch.device("cuda"))
-            got = torch.empty(rows_p, d, device="cuda")
+            got = torch.empty(rows_p.size, d, device="cuda")
             N.check(L.oxc_embedding_exchange_reduce_regions(
                 rids[p].data_ptr(), rrows[p].data_ptr(), rcount[p].data_ptr(), G, cap, lo_p,
-                rows_p, d, got.data_ptr(), flag.data_ptr(), ws2.data_ptr(), ws2.numel(),
-                F._stream()), "reduce regions")
-            # the NCCL route's owner reduce over the same rows in source order
-            rid, rrow, off = [], [], [0]
-            for oid, orow, k, sc in sends:
-                a = int(sc[:p].sum())
-                rid.append(oid[a:a + sc[p]])
-                rrow.append(orow[a:a + sc[p]])
-                off.append(off[-1] + int(sc[p]))
-            d_rid = _dev(np.concatenate(rid).astype(np.int32))
-            d_rrow = _dev(np.concatenate(rrow))
-            d_off = _dev(np.array(off, np.int64))
-            want = torch.empty(rows_p, d, device="cuda")
-            N.check(L.oxc_embedding_exchange_reduce(
-                d_rid.data_ptr(), d_rrow.data_ptr(), d_off.data_ptr(), G, lo_p, rows_p, d,
-                want.data_ptr(), flag.data_ptr(), ws2.data_ptr(), ws2.numel(), F._stream()))
-            assert_bitexact(_host(got), _host(want), f"owner {p} shard, round {rnd}")
+                stride, rows_p.size, d, got.data_ptr(), flag.data_ptr(), ws2.data_ptr(),
+                ws2.numel(), F._stream()), "reduce regions")
+            assert_bitexact(_host(got), expect[rows_p], f"owner {p} shard, round {rnd}")
+            if not cyclic:
+                # the NCCL route's owner reduce over the same rows in source order
+                sends = [_compact(ids[lo:hi], dout[lo:hi], V, G) for lo, hi in shards]
+                rid, rrow, off = [], [], [0]
+                for oid, orow, k, sc in sends:
+                    a = int(sc[:p].sum())
+                    rid.append(oid[a:a + sc[p]])
+                    rrow.append(orow[a:a + sc[p]])
+                    off.append(off[-1] + int(sc[p]))
+                d_rid = _dev(np.concatenate(rid).astype(np.int32))
+                d_rrow = _dev(np.concatenate(rrow))
+                d_off = _dev(np.array(off, np.int64))
+                want = torch.empty(rows_p.size, d, device="cuda")
+                N.check(L.oxc_embedding_exchange_reduce(
+                    d_rid.data_ptr(), d_rrow.data_ptr(), d_off.data_ptr(), G, bounds[p],
+                    rows_p.size, d, want.data_ptr(), flag.data_ptr(), ws2.data_ptr(),
+                    ws2.numel(), F._stream()))
+                assert_bitexact(_host(got), _host(want), f"owner {p} vs the NCCL route")
         assert int(flag.abs().sum().item()) == 0
 
 
@@ -367,19 +384,27 @@ def _nccl_body(rank, world, dev):
     assert_close(_host(dsh), _host(full2)[voff:voff + vrows], rtol=1e-4, atol=1e-4,
                  what="sparse-exchanged dtable shard")
     # the fused exchange over peer memory: the same sums in the same order as
-    # the NCCL all-to-all exchange, so bit for bit the same shard, over three
-    # steps that alternate the two slots
-    ex = S.PeerGradExchange(hi2 - lo2, v2, d2, dev, slots=2)
+    # the NCCL all-to-all exchange, so bit for bit the same rows, over three
+    # steps that alternate the two slots; contiguous ownership gives the NCCL
+    # route's shard, cyclic ownership its rows rank, rank + world, ...
     ids_r = _dev(ids2[lo2:hi2], dev)
-    for step in range(3):
-        dout_k = _dev(dout2[lo2:hi2] * np.float32(step + 1), dev)
-        ex.vjp(ids_r, dout_k, step % 2)
-        got, done = ex.exchange(step % 2)
-        torch.cuda.current_stream().wait_event(done)
-        want_k = S.embedding_grad(ids_r, dout_k, v2)
-        assert_bitexact(_host(got), _host(want_k), f"peer-exchanged dtable shard, step {step}")
-    assert int(ex.flag.abs().sum().item()) == 0
-    ex.close()
+    for cyclic in (False, True):
+        ex = S.PeerGradExchange(hi2 - lo2, v2, d2, dev, slots=2, cyclic=cyclic)
+        for step in range(3):
+            dout_k = _dev(dout2[lo2:hi2] * np.float32(step + 1), dev)
+            ex.vjp(ids_r, dout_k, step % 2)
+            got, done = ex.exchange(step % 2)
+            torch.cuda.current_stream().wait_event(done)
+            want_k = S.embedding_grad(ids_r, dout_k, v2)
+            if cyclic:
+                parts = [torch.empty(S.vocab_shard(v2, p, world)[1], d2, device=dev)
+                         for p in range(world)]
+                dist.all_gather(parts, want_k)
+                want_k = torch.cat(parts)[rank::world]
+            assert_bitexact(_host(got), _host(want_k),
+                            f"peer-exchanged dtable shard (cyclic={cyclic}), step {step}")
+        assert int(ex.flag.abs().sum().item()) == 0
+        ex.close()
     # the C-ABI communicator (oxc_comm_*), the route of a native host
     import ctypes
     from oxitorch_b200 import _native as N
