@@ -769,9 +769,10 @@ class Embedding(Workload):
             from oxitorch_b200.sharded import PeerGradExchange, SparseGradExchange
             self.GRAPHS = False  # the exchange holds a collective
             self.ex = None
-            if not getattr(args, "nccl_exchange", False):
+            kind = getattr(args, "exchange", "push")
+            if kind != "nccl":
                 try:
-                    self.ex = PeerGradExchange(n, self.v, self.d, dev, slots=2)
+                    self.ex = PeerGradExchange(n, self.v, self.d, dev, slots=2, mode=kind)
                     self.exchange_kind = "peer"
                     self.launches = 11  # + present, scan (2), meta, map, reduce (and NCCL's)
                 except RuntimeError as e:  # raised on every rank alike
@@ -860,10 +861,17 @@ class Embedding(Workload):
 
     def _exchange_desc(self):
         if self.exchange_kind == "peer":
-            return ("fused exchange: the VJP kernel stores each touched row into its owner's "
-                    "memory over NVLink (CUDA IPC peer memory; rows owned cyclically, row r by "
-                    "rank r mod N, which spreads the Zipf-hot low ids), a stream-ordered barrier, "
-                    "the owner's rank-order sum")
+            own = ("rows owned cyclically, row r by rank r mod N, which spreads the Zipf-hot "
+                   "low ids")
+            if self.ex.mode == "pull":
+                return ("exchange over NVLink peer memory (CUDA IPC), pull form: the VJP kernel "
+                        "writes each touched row into this GPU's region for the row's owner; after "
+                        "a stream-ordered barrier each owner's kernel reads its regions from every "
+                        "rank's memory and sums them in rank order, overlapping the next forward; "
+                        + own)
+            return ("exchange over NVLink peer memory (CUDA IPC), push form: the VJP kernel "
+                    "stores each touched row into its owner's memory; a stream-ordered barrier; "
+                    "the owner's rank-order sum; " + own)
         why = getattr(self, "exchange_fallback", None)
         return ("compact VJP + NCCL all-to-all of the touched rows to their vocab shard's owner "
                 "+ rank-order sum (sparse exchange)" + (f"; peer memory unavailable: {why}"
@@ -1719,8 +1727,9 @@ def main():
                     help="rows / tokens / ids per GPU (0 = the BASELINE config's; smaller only "
                          "for profiling: other shapes draw other arrays)")
     ap.add_argument("--skip-e2e", action="store_true", help="profiling runs: no host-buffer leg")
-    ap.add_argument("--nccl-exchange", action="store_true",
-                    help="embedding at N > 1: the NCCL all-to-all exchange, not the fused one")
+    ap.add_argument("--exchange", choices=("push", "pull", "nccl"), default="push",
+                    help="embedding at N > 1: the peer-memory exchange (pull or push form) or "
+                         "the NCCL all-to-all one")
     ap.add_argument("--e2e-large", action="store_true",
                     help="also run the host-buffer leg of the mlp_block workload")
     args = ap.parse_args()

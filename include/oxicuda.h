@@ -469,7 +469,7 @@ typedef struct oxc_emb_push {
   int32_t world;
   int32_t source;  /* this (source) rank: stores to its own region need no system-scope fence */
   int32_t cyclic;  /* 1: owner p holds rows p, p + world, ...; 0: rows [lo[p], lo[p+1]) */
-  int32_t reserved;
+  int32_t local;   /* 1: every region named here is in this GPU's own memory (the pull form) */
   int64_t cap;
   int64_t lo[OXC_PUSH_MAX_RANKS + 1];  /* contiguous ownership: owner p's first row, lo[world] = rows */
   float* rows[OXC_PUSH_MAX_RANKS];
@@ -487,6 +487,27 @@ oxc_status oxc_embedding_exchange_reduce_regions(const int32_t* recv_ids, const 
                                                  int64_t cols, float* dshard, int32_t* err_flag,
                                                  void* workspace, size_t workspace_bytes,
                                                  void* stream);
+/* The pull form of the same exchange.  Each source pushes into its OWN memory
+ * (an oxc_emb_push table with local = 1 naming, for every owner p, its send
+ * region p), so the VJP stores nothing over NVLink.  After the barrier, each
+ * owner's oxc_embedding_exchange_pull reads, for every source s in rank order,
+ * the region s holds for it -- peer memory mapped with oxc_ipc_import, or its
+ * own for s = this rank -- and sums the rows in source order from 0.0 into its
+ * dense shard (the same bits as oxc_embedding_exchange_reduce_regions), on a
+ * communication stream that overlaps the next forward.  oxc_emb_pull (device
+ * memory) lists the sources' regions for this owner; the workspace is
+ * oxc_embedding_exchange_reduce_workspace_size(sources, shard_rows). */
+typedef struct oxc_emb_pull {
+  const float* rows[OXC_PUSH_MAX_RANKS];    /* source s's region for this owner: [cap][cols] */
+  const int32_t* ids[OXC_PUSH_MAX_RANKS];   /* [cap] */
+  const int64_t* count[OXC_PUSH_MAX_RANKS]; /* one count */
+} oxc_emb_pull;
+oxc_status oxc_embedding_exchange_pull(const oxc_emb_pull* pull, int32_t sources, int64_t cap,
+                                       int64_t shard_lo, int64_t shard_stride,
+                                       int64_t shard_rows, int64_t cols, float* dshard,
+                                       int32_t* err_flag, void* workspace,
+                                       size_t workspace_bytes, void* stream);
+
 /* Device memory shared between the processes of one node: oxc_ipc_export gives
  * the handle of the allocation holding dev_ptr and dev_ptr's byte offset in it;
  * oxc_ipc_import maps it into another process (peer access enabled) and

@@ -55,9 +55,19 @@ class EmbPush(ctypes.Structure):
         ("world", ctypes.c_int32),
         ("source", ctypes.c_int32),
         ("cyclic", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("local", ctypes.c_int32),
         ("cap", ctypes.c_int64),
         ("lo", ctypes.c_int64 * (PUSH_MAX_RANKS + 1)),
+        ("rows", ctypes.c_void_p * PUSH_MAX_RANKS),
+        ("ids", ctypes.c_void_p * PUSH_MAX_RANKS),
+        ("count", ctypes.c_void_p * PUSH_MAX_RANKS),
+    ]
+
+
+class EmbPull(ctypes.Structure):
+    """struct oxc_emb_pull: every source's region for one owner (the pull form)."""
+
+    _fields_ = [
         ("rows", ctypes.c_void_p * PUSH_MAX_RANKS),
         ("ids", ctypes.c_void_p * PUSH_MAX_RANKS),
         ("count", ctypes.c_void_p * PUSH_MAX_RANKS),
@@ -156,6 +166,8 @@ SIGNATURES = {
     "oxc_embedding_bwd_push": (_I32, [_P, _P, _I64, _I64, _I64, _P, _P, _P, _SZ, _P]),
     "oxc_embedding_exchange_reduce_regions": (_I32, [_P, _P, _P, _I32, _I64, _I64, _I64, _I64,
                                                      _I64, _P, _P, _P, _SZ, _P]),
+    "oxc_embedding_exchange_pull": (_I32, [_P, _I32, _I64, _I64, _I64, _I64, _I64, _P, _P, _P,
+                                           _SZ, _P]),
     "oxc_ipc_export": (_I32, [_P, _P, ctypes.POINTER(_I64)]),
     "oxc_ipc_import": (_I32, [_P, _I64, ctypes.POINTER(_P)]),
     "oxc_ipc_close": (_I32, [_P, _I64]),

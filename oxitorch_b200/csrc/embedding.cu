@@ -328,7 +328,7 @@ __global__ void __launch_bounds__(MAXT) emb_rows_kernel(
         continue;
       }
       dst = push->rows[p] + idx * (int64_t)cols;
-      remote |= p != push->source;
+      remote |= p != push->source && !push->local;
     }
     for (int c_base = blockIdx.y * VPT * blockDim.x; c_base < nvec;
          c_base += gridDim.y * VPT * blockDim.x) {
@@ -578,6 +578,85 @@ __global__ void emb_push_meta_kernel(const int32_t* __restrict__ present,
   }
   __syncthreads();  // one system-scope fence per CTA covers every thread's stores
   if (threadIdx.x == 0) __threadfence_system();
+}
+
+// The pull form's owner side.  map[s * shard_rows + v] = the index in source
+// s's region of the owner's shard row v (table row shard_lo + v *
+// shard_stride), or -1.  The counts are read once per CTA.
+__global__ void emb_pull_map_kernel(const oxc_emb_pull* __restrict__ pull, int32_t sources,
+                                    int64_t cap, int64_t shard_lo, int64_t shard_stride,
+                                    int64_t shard_rows, int32_t* __restrict__ map, int32_t* err) {
+  __shared__ int64_t cnt[OXC_PUSH_MAX_RANKS];
+  if (threadIdx.x < sources) cnt[threadIdx.x] = *pull->count[threadIdx.x];
+  __syncthreads();
+  const int64_t total = (int64_t)sources * cap;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int s = (int)(i / cap);
+    const int64_t k = i - (int64_t)s * cap;
+    if (k >= cnt[s]) continue;
+    const int64_t id = pull->ids[s][k];
+    const int64_t d = id - shard_lo;
+    const int64_t v = d / shard_stride;
+    if (d < 0 || d % shard_stride != 0 || v >= shard_rows) {
+      if (err && atomicCAS(err, 0, 1) == 0) {
+        err[1] = (int32_t)id;
+        err[2] = 0;
+        err[3] = (int32_t)shard_rows;
+      }
+      continue;
+    }
+    map[(int64_t)s * shard_rows + v] = (int32_t)k;
+  }
+}
+
+// dshard[v] = sum over sources s in rank order, from 0.0, of row map[s][v] of
+// s's region (skipped where -1): the same sums as emb_exchange_reduce_kernel.
+// Every source's load is issued before the adds, so a thread keeps up to
+// `sources` NVLink reads in flight.
+template <int VW>
+__global__ void __launch_bounds__(128) emb_pull_reduce_kernel(
+    const oxc_emb_pull* __restrict__ pull, const int32_t* __restrict__ map, int32_t sources,
+    int64_t shard_rows, int cols, float* __restrict__ dshard) {
+  __shared__ const float* src[OXC_PUSH_MAX_RANKS];
+  if (threadIdx.x < sources) src[threadIdx.x] = pull->rows[threadIdx.x];
+  __syncthreads();
+  const int nvec = cols / VW;
+  for (int64_t v = blockIdx.x; v < shard_rows; v += gridDim.x) {
+    int32_t idx[OXC_PUSH_MAX_RANKS];
+#pragma unroll
+    for (int s = 0; s < OXC_PUSH_MAX_RANKS; ++s)
+      idx[s] = s < sources ? map[(int64_t)s * shard_rows + v] : -1;
+    for (int c = blockIdx.y * blockDim.x + threadIdx.x; c < nvec; c += gridDim.y * blockDim.x) {
+      float q[OXC_PUSH_MAX_RANKS][VW];
+#pragma unroll
+      for (int s = 0; s < OXC_PUSH_MAX_RANKS; ++s) {
+        if (idx[s] >= 0) {
+          if constexpr (VW == 4) {
+            const float4 a =
+                ld_stream(reinterpret_cast<const float4*>(src[s] + (int64_t)idx[s] * cols) + c);
+            q[s][0] = a.x; q[s][1] = a.y; q[s][2] = a.z; q[s][3] = a.w;
+          } else {
+            q[s][0] = ld_stream(src[s] + (int64_t)idx[s] * cols + c);
+          }
+        }
+      }
+      float acc[VW];
+#pragma unroll
+      for (int e = 0; e < VW; ++e) acc[e] = 0.0f;
+#pragma unroll
+      for (int s = 0; s < OXC_PUSH_MAX_RANKS; ++s)
+        if (idx[s] >= 0) {
+#pragma unroll
+          for (int e = 0; e < VW; ++e) acc[e] = __fadd_rn(acc[e], q[s][e]);
+        }
+      if constexpr (VW == 4)
+        st_stream(reinterpret_cast<float4*>(dshard + v * cols) + c,
+                  make_float4(acc[0], acc[1], acc[2], acc[3]));
+      else
+        st_stream(dshard + v * cols + c, acc[0]);
+    }
+  }
 }
 
 // The owner's side of the fused exchange: region s of recv holds counts[s]
@@ -1077,6 +1156,51 @@ oxc_status oxc_embedding_exchange_reduce_regions(const int32_t* recv_ids, const 
     emb_exchange_reduce_kernel<1><<<grid, 128, 0, s>>>(recv_rows, map, sources, shard_rows,
                                                        (int)cols, dshard);
   return check_launch("oxc_embedding_exchange_reduce_regions");
+}
+
+oxc_status oxc_embedding_exchange_pull(const oxc_emb_pull* pull, int32_t sources, int64_t cap,
+                                       int64_t shard_lo, int64_t shard_stride,
+                                       int64_t shard_rows, int64_t cols, float* dshard,
+                                       int32_t* err_flag, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+  const char* fn = "embedding gradient exchange (pull)";
+  if (sources <= 0 || sources > OXC_PUSH_MAX_RANKS || cap < 0 || shard_rows < 0 || cols < 0 ||
+      shard_lo < 0 || shard_stride < 1)
+    return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: bad sizes", fn);
+  if (shard_rows >= 0x7fffffff || cols > 0x7fffffff || (int64_t)sources * cap >= 0x7fffffff ||
+      (int64_t)sources * shard_rows >= 0x7fffffff)
+    return fail(OXC_ERR_NOT_IMPLEMENTED, "not implemented: %s: sizes beyond 2^31", fn);
+  if (shard_rows == 0 || cols == 0) return OXC_OK;
+  if (!pull || !dshard) return fail(OXC_ERR_INVALID_ARGUMENT, "invalid argument: %s: null pointer", fn);
+  const size_t need = oxc_embedding_exchange_reduce_workspace_size(sources, shard_rows);
+  if (!workspace || workspace_bytes < need)
+    return fail(OXC_ERR_INVALID_ARGUMENT,
+                "invalid argument: %s needs a %zu-byte workspace, got %zu", fn, need,
+                workspace_bytes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t* map = static_cast<int32_t*>(workspace);
+  cudaError_t e = cudaMemsetAsync(map, 0xff, (size_t)sources * shard_rows * sizeof(int32_t), s);
+  if (e != cudaSuccess) return cuda_fail(e, "oxc_embedding_exchange_pull");
+  if (cap > 0) {
+    emb_pull_map_kernel<<<(unsigned)sm_count() * 4, 256, 0, s>>>(
+        pull, sources, cap, shard_lo, shard_stride, shard_rows, map, err_flag);
+    oxc_status st = check_launch("oxc_embedding_exchange_pull (map)");
+    if (st) return st;
+  }
+  // the regions are the callers' buffers at cols-float strides: float4 rows
+  // when cols % 4 == 0 (the regions' bases are 256-byte aligned allocations
+  // plus multiples of 16 bytes)
+  const bool v4 = cols % 4 == 0 && aligned16(dshard);
+  const int64_t per = v4 ? cols / 4 : cols;
+  const unsigned chunks = (unsigned)std::min<int64_t>(65535, (per + 127) / 128);
+  const dim3 grid((unsigned)std::min<int64_t>(shard_rows, (int64_t)sm_count() * 32), chunks);
+  if (v4)
+    emb_pull_reduce_kernel<4><<<grid, 128, 0, s>>>(pull, map, sources, shard_rows, (int)cols,
+                                                   dshard);
+  else
+    emb_pull_reduce_kernel<1><<<grid, 128, 0, s>>>(pull, map, sources, shard_rows, (int)cols,
+                                                   dshard);
+  return check_launch("oxc_embedding_exchange_pull");
 }
 
 oxc_status oxc_index_select(const oxc_view* x, int64_t dim, const int64_t* ids, int64_t n,

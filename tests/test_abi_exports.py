@@ -93,8 +93,9 @@ def test_struct_mirrors_match_the_header(tmp_path):
         pytest.skip("gcc not available")
     checks = {
         "oxc_view": (N.View, ["data", "ndim", "shape", "strides"]),
-        "oxc_emb_push": (N.EmbPush, ["world", "source", "cyclic", "cap", "lo", "rows", "ids",
-                                     "count"]),
+        "oxc_emb_push": (N.EmbPush, ["world", "source", "cyclic", "local", "cap", "lo", "rows",
+                                     "ids", "count"]),
+        "oxc_emb_pull": (N.EmbPull, ["rows", "ids", "count"]),
     }
     lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "oxicuda.h"',
              "int main(void) {"]

@@ -178,35 +178,23 @@ def test_embedding_sparse_exchange_emulated(oracle):
         assert int(flag[0]) == 0
 
 
-def _push_table(N, world, source, cap, bounds, rrows, rids, rcount, d, cyclic):
-    """The oxc_emb_push table of `source` (device memory): for every owner p,
-    this source's part of p's receive regions."""
-    import torch
-    tab = N.EmbPush()
-    tab.world, tab.source, tab.cyclic, tab.cap = world, source, int(cyclic), cap
-    for p in range(world + 1):
-        tab.lo[p] = bounds[p]
-    for p in range(world):
-        tab.rows[p] = rrows[p].data_ptr() + source * cap * d * 4
-        tab.ids[p] = rids[p].data_ptr() + source * cap * 4
-        tab.count[p] = rcount[p].data_ptr() + source * 8
-    return torch.tensor(list(bytes(tab)), dtype=torch.uint8).to("cuda")
-
-
+@pytest.mark.parametrize("mode", ["push", "pull"])
 @pytest.mark.parametrize("cyclic", [False, True])
 @pytest.mark.parametrize("d", [512, 37])
-def test_embedding_push_exchange_emulated(d, cyclic):
-    """The fused exchange (oxc_embedding_bwd_push + the owners'
-    oxc_embedding_exchange_reduce_regions) with three ranks emulated on one
-    GPU, every owner's receive regions in this GPU's memory, for contiguous
-    and cyclic ownership: the regions hold each source's touched ids of that
-    owner (ascending) and their counts, and every owner's dense shard is, bit
-    for bit, the sum in source order from 0.0 of the sources' rows -- each
-    source's rows being its single-GPU dense VJP's.  With contiguous
-    ownership the shard is also the NCCL route's (compact VJP, rows routed in
-    source order, oxc_embedding_exchange_reduce).  A vocabulary that does not
-    split evenly and odd rows (d = 37, the scalar path) included; two rounds
-    over the same regions, the second with other gradients."""
+def test_embedding_push_exchange_emulated(d, cyclic, mode):
+    """The fused exchange with three ranks emulated on one GPU, every buffer in
+    this GPU's memory, for contiguous and cyclic ownership and both forms:
+    push (oxc_embedding_bwd_push into the owners' buffers, then each owner's
+    oxc_embedding_exchange_reduce_regions) and pull (the push kernel into the
+    sources' own buffers, then each owner's oxc_embedding_exchange_pull).  The
+    regions hold each source's touched ids of that owner (ascending) and their
+    counts, and every owner's dense shard is, bit for bit, the sum in source
+    order from 0.0 of the sources' rows -- each source's rows being its
+    single-GPU dense VJP's.  With contiguous ownership the shard is also the
+    NCCL route's (compact VJP, rows routed in source order,
+    oxc_embedding_exchange_reduce).  A vocabulary that does not split evenly
+    and odd rows (d = 37, the scalar path) included; two rounds over the same
+    regions, the second with other gradients."""
     import torch
     from oxitorch_b200 import _native as N
     from oxitorch_b200 import functional as F
@@ -223,10 +211,35 @@ def test_embedding_push_exchange_emulated(d, cyclic):
     def owned(p):  # table rows of owner p, ascending
         return np.arange(p, V, G) if cyclic else np.arange(bounds[p], bounds[p + 1])
 
-    rrows = [torch.empty(G * cap * d, device="cuda") for _ in range(G)]
-    rids = [torch.full((G * cap,), -7, dtype=torch.int32, device="cuda") for _ in range(G)]
-    rcount = [torch.full((G,), -1, dtype=torch.int64, device="cuda") for _ in range(G)]
-    tabs = [_push_table(N, G, g, cap, bounds, rrows, rids, rcount, d, cyclic) for g in range(G)]
+    # buffer h holds G regions; region (owner, source) is at index source of
+    # the owner's buffer (push) or index owner of the source's buffer (pull)
+    brows = [torch.empty(G * cap * d, device="cuda") for _ in range(G)]
+    bids = [torch.full((G * cap,), -7, dtype=torch.int32, device="cuda") for _ in range(G)]
+    bcount = [torch.full((G,), -1, dtype=torch.int64, device="cuda") for _ in range(G)]
+
+    def region(owner, source):
+        h, i = (owner, source) if mode == "push" else (source, owner)
+        return (brows[h].data_ptr() + i * cap * d * 4, bids[h].data_ptr() + i * cap * 4,
+                bcount[h].data_ptr() + i * 8, h, i)
+
+    def to_dev(tab):
+        return torch.tensor(list(bytes(tab)), dtype=torch.uint8).to("cuda")
+
+    tabs, pulls = [], []
+    for g in range(G):
+        tab = N.EmbPush()
+        tab.world, tab.source, tab.cyclic, tab.local, tab.cap = G, g, int(cyclic), \
+            int(mode == "pull"), cap
+        for p in range(G + 1):
+            tab.lo[p] = bounds[p]
+        for p in range(G):
+            tab.rows[p], tab.ids[p], tab.count[p] = region(p, g)[:3]
+        tabs.append(to_dev(tab))
+    for p in range(G):
+        pt = N.EmbPull()
+        for g in range(G):
+            pt.rows[g], pt.ids[g], pt.count[g] = region(p, g)[:3]
+        pulls.append(to_dev(pt))
     flag = torch.zeros(4, dtype=torch.int32, device="cuda")
     ws_bytes = L.oxc_embedding_bwd_compact_workspace_size(n, V, d)
     ws = F._workspace(ws_bytes, torch.device("cuda"))
@@ -248,20 +261,24 @@ def test_embedding_push_exchange_emulated(d, cyclic):
             expect[u] = expect[u] + _host(dense)[u]
         for p in range(G):
             rows_p = owned(p)
-            cnt = _host(rcount[p])
-            rid_h = _host(rids[p]).reshape(G, cap)
             for g in range(G):
+                h, i = region(p, g)[3:]
                 u = np.intersect1d(touched[g], rows_p)
-                assert cnt[g] == u.size, (p, g)
-                assert np.array_equal(rid_h[g, :u.size], u), (p, g)
+                assert int(_host(bcount[h])[i]) == u.size, (p, g)
+                assert np.array_equal(_host(bids[h]).reshape(G, cap)[i, :u.size], u), (p, g)
             lo_p, stride = (p, G) if cyclic else (bounds[p], 1)
             ws2 = F._workspace(L.oxc_embedding_exchange_reduce_workspace_size(G, rows_p.size),
                                torch.device("cuda"))
             got = torch.empty(rows_p.size, d, device="cuda")
-            N.check(L.oxc_embedding_exchange_reduce_regions(
-                rids[p].data_ptr(), rrows[p].data_ptr(), rcount[p].data_ptr(), G, cap, lo_p,
-                stride, rows_p.size, d, got.data_ptr(), flag.data_ptr(), ws2.data_ptr(),
-                ws2.numel(), F._stream()), "reduce regions")
+            if mode == "push":
+                N.check(L.oxc_embedding_exchange_reduce_regions(
+                    bids[p].data_ptr(), brows[p].data_ptr(), bcount[p].data_ptr(), G, cap, lo_p,
+                    stride, rows_p.size, d, got.data_ptr(), flag.data_ptr(), ws2.data_ptr(),
+                    ws2.numel(), F._stream()), "reduce regions")
+            else:
+                N.check(L.oxc_embedding_exchange_pull(
+                    pulls[p].data_ptr(), G, cap, lo_p, stride, rows_p.size, d, got.data_ptr(),
+                    flag.data_ptr(), ws2.data_ptr(), ws2.numel(), F._stream()), "pull")
             assert_bitexact(_host(got), expect[rows_p], f"owner {p} shard, round {rnd}")
             if not cyclic:
                 # the NCCL route's owner reduce over the same rows in source order
@@ -388,8 +405,8 @@ def _nccl_body(rank, world, dev):
     # steps that alternate the two slots; contiguous ownership gives the NCCL
     # route's shard, cyclic ownership its rows rank, rank + world, ...
     ids_r = _dev(ids2[lo2:hi2], dev)
-    for cyclic in (False, True):
-        ex = S.PeerGradExchange(hi2 - lo2, v2, d2, dev, slots=2, cyclic=cyclic)
+    for mode, cyclic in (("push", False), ("push", True), ("pull", False), ("pull", True)):
+        ex = S.PeerGradExchange(hi2 - lo2, v2, d2, dev, slots=2, cyclic=cyclic, mode=mode)
         for step in range(3):
             dout_k = _dev(dout2[lo2:hi2] * np.float32(step + 1), dev)
             ex.vjp(ids_r, dout_k, step % 2)
@@ -402,7 +419,7 @@ def _nccl_body(rank, world, dev):
                 dist.all_gather(parts, want_k)
                 want_k = torch.cat(parts)[rank::world]
             assert_bitexact(_host(got), _host(want_k),
-                            f"peer-exchanged dtable shard (cyclic={cyclic}), step {step}")
+                            f"peer-exchanged dtable shard ({mode}, cyclic={cyclic}), step {step}")
         assert int(ex.flag.abs().sum().item()) == 0
         ex.close()
     # the C-ABI communicator (oxc_comm_*), the route of a native host
