@@ -180,9 +180,9 @@ def test_embedding_sparse_exchange_emulated(oracle):
 
 @pytest.mark.parametrize("mode", ["push", "pull"])
 @pytest.mark.parametrize("cyclic", [False, True])
-@pytest.mark.parametrize("d", [512, 37])
-def test_embedding_push_exchange_emulated(d, cyclic, mode):
-    """The fused exchange with three ranks emulated on one GPU, every buffer in
+@pytest.mark.parametrize("d,G", [(512, 3), (37, 3), (512, 8)])
+def test_embedding_push_exchange_emulated(d, G, cyclic, mode):
+    """The fused exchange with three (or eight) ranks emulated on one GPU, every buffer in
     this GPU's memory, for contiguous and cyclic ownership and both forms:
     push (oxc_embedding_bwd_push into the owners' buffers, then each owner's
     oxc_embedding_exchange_reduce_regions) and pull (the push kernel into the
@@ -201,7 +201,7 @@ def test_embedding_push_exchange_emulated(d, cyclic, mode):
     from oxitorch_b200 import sharded as S
     L = N.load()
     rng = np.random.default_rng(25)
-    V, n, G = 3001, 20000, 3
+    V, n = 3001, 20000
     ids = np.minimum(rng.zipf(1.1, n) - 1, V - 1).astype(np.int64)
     ids[::89] -= V  # negative ids count from the end
     res = np.where(ids < 0, ids + V, ids)
