@@ -57,6 +57,28 @@ __device__ __forceinline__ float gelu_grad(float y, float g, const GeluConst& gc
   return g * fmaf(y * s * oms, dv, s);
 }
 
+// gelu_grad for two lanes at once on the packed f32x2 pipe of sm_100
+// (__ffma2_rn / __fadd2_rn / __fmul2_rn round each lane exactly like the
+// scalar fmaf / __fadd_rn / __fmul_rn).  The operations and their order are
+// those of gelu_grad, which has no multiply-add pair the compiler could
+// contract, so both forms give the same bits; this one issues half the FP
+// instructions (the two MUFU operations and the clamp stay per lane).
+__device__ __forceinline__ float2 bcast2(float a) { return make_float2(a, a); }
+
+__device__ __forceinline__ float2 gelu_grad2(float2 y, float2 g, const GeluConst& gc) {
+  const float2 y2 = __fmul2_rn(y, y);
+  const float2 v = __ffma2_rn(__fmul2_rn(bcast2(gc.k), y2), y, y);
+  const float2 t = __fmul2_rn(v, bcast2(gc.e2));
+  const float2 E = make_float2(ex2_approx(t.x), ex2_approx(t.y));
+  const float2 d = __fadd2_rn(bcast2(1.0f), E);
+  const float2 s = make_float2(rcp_approx(d.x), rcp_approx(d.y));
+  const float2 es = __fmul2_rn(E, s);
+  const float2 oms = make_float2(fminf(es.x, 1.0f), fminf(es.y, 1.0f));
+  const float2 dv = __fmul2_rn(bcast2(gc.c2), __ffma2_rn(bcast2(gc.k3), y2, bcast2(1.0f)));
+  const float2 q = __fmul2_rn(__fmul2_rn(y, s), oms);
+  return __fmul2_rn(g, __ffma2_rn(q, dv, s));
+}
+
 // The constants as f32, computed on the host once per launch.
 inline GeluConst gelu_const() {
   GeluConst gc;

@@ -378,39 +378,45 @@ __global__ void __launch_bounds__((NG * NWG + 1) * 32, 1) ln_bwd_pipe_kernel(
       gv[k] = valid ? gs[slot] : make_float4(0, 0, 0, 0);
     }
     consumer_release<2>(ring, i);
-    float s1 = 0.0f, s2 = 0.0f;
+    // Element pairs on the packed f32x2 pipe: every lane rounds as the scalar
+    // operations would, and the row sums run as two interleaved partials.
+    const float2 nmu2 = bcast2(-mu), inv2 = bcast2(inv);
+    float2 s1p = make_float2(0.0f, 0.0f), s2p = make_float2(0.0f, 0.0f);
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
       const int slot = k * T + gt;
-      const float4 wv = slot < nvec ? w4[slot] : make_float4(0, 0, 0, 0);
-      const float4 bv = slot < nvec ? b4[slot] : make_float4(0, 0, 0, 0);
-      float* xe = reinterpret_cast<float*>(&xv[k]);
-      float* ge = reinterpret_cast<float*>(&gv[k]);
-      const float* we = reinterpret_cast<const float*>(&wv);
-      const float* be = reinterpret_cast<const float*>(&bv);
+      float4 wv = make_float4(0, 0, 0, 0), bv = make_float4(0, 0, 0, 0);
+      if (slot < nvec) {
+        wv = w4[slot];
+        bv = b4[slot];
+      }
+      float2* xe = reinterpret_cast<float2*>(&xv[k]);
+      float2* ge = reinterpret_cast<float2*>(&gv[k]);
+      const float2* we = reinterpret_cast<const float2*>(&wv);
+      const float2* be = reinterpret_cast<const float2*>(&bv);
       float4 dw4, db4;
       if constexpr (SACC) {
         dw4 = slot < nvec ? gdw[slot] : make_float4(0, 0, 0, 0);
         db4 = slot < nvec ? gdb[slot] : make_float4(0, 0, 0, 0);
       }
-      float* dwe = SACC ? reinterpret_cast<float*>(&dw4) : reinterpret_cast<float*>(&adw[SACC ? 0 : k]);
-      float* dbe = SACC ? reinterpret_cast<float*>(&db4) : reinterpret_cast<float*>(&adb[SACC ? 0 : k]);
+      float2* dwe = SACC ? reinterpret_cast<float2*>(&dw4) : reinterpret_cast<float2*>(&adw[SACC ? 0 : k]);
+      float2* dbe = SACC ? reinterpret_cast<float2*>(&db4) : reinterpret_cast<float2*>(&adb[SACC ? 0 : k]);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float t1 = (xe[e] - mu) * inv;
-        float gg = ge[e];
-        if constexpr (ACT == OXC_ACT_GELU_TANH) gg = gelu_grad(fmaf(t1, we[e], be[e]), gg, gc);
-        dwe[e] = fmaf(gg, t1, dwe[e]);
-        dbe[e] += gg;
-        const float gw = gg * we[e];
+      for (int e = 0; e < 2; ++e) {
+        const float2 t1 = __fmul2_rn(__fadd2_rn(xe[e], nmu2), inv2);  // (x - mu) * inv
+        float2 gg = ge[e];
+        if constexpr (ACT == OXC_ACT_GELU_TANH) gg = gelu_grad2(__ffma2_rn(t1, we[e], be[e]), gg, gc);
+        dwe[e] = __ffma2_rn(gg, t1, dwe[e]);
+        dbe[e] = __fadd2_rn(dbe[e], gg);
+        const float2 gw = __fmul2_rn(gg, we[e]);
         if constexpr (MODE == OXC_GRAD_REF) {
-          ge[e] = gw * inv;
-          s1 += ge[e];
+          ge[e] = __fmul2_rn(gw, inv2);
+          s1p = __fadd2_rn(s1p, ge[e]);
         } else {
           ge[e] = gw;
           xe[e] = t1;
-          s1 += gw;
-          s2 = fmaf(gw, t1, s2);
+          s1p = __fadd2_rn(s1p, gw);
+          s2p = __ffma2_rn(gw, t1, s2p);
         }
       }
       if constexpr (SACC) {
@@ -420,6 +426,7 @@ __global__ void __launch_bounds__((NG * NWG + 1) * 32, 1) ln_bwd_pipe_kernel(
         }
       }
     }
+    float s1 = s1p.x + s1p.y, s2 = s2p.x + s2p.y;
     s1 = group_sum<NWG>(s1, gred, bar);
     if constexpr (MODE == OXC_GRAD_EXACT) s2 = group_sum<NWG>(s2, gred, bar);
     float4* dxr = reinterpret_cast<float4*>(dx + row * (int64_t)cols);
@@ -430,13 +437,16 @@ __global__ void __launch_bounds__((NG * NWG + 1) * 32, 1) ln_bwd_pipe_kernel(
       const int slot = k * T + gt;
       if (ok && slot < nvec) {
         float4 o;
-        float* oe = reinterpret_cast<float*>(&o);
-        const float* xe = reinterpret_cast<const float*>(&xv[k]);
-        const float* ge = reinterpret_cast<const float*>(&gv[k]);
+        float2* oe = reinterpret_cast<float2*>(&o);
+        const float2* xe = reinterpret_cast<const float2*>(&xv[k]);
+        const float2* ge = reinterpret_cast<const float2*>(&gv[k]);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          if constexpr (MODE == OXC_GRAD_REF) oe[e] = ge[e] + shift;
-          else oe[e] = inv * ((ge[e] - m1) - xe[e] * m2);
+        for (int e = 0; e < 2; ++e) {
+          if constexpr (MODE == OXC_GRAD_REF) {
+            oe[e] = __fadd2_rn(ge[e], bcast2(shift));
+          } else {  // inv * ((g - m1) - x * m2), the last two as one fused step
+            oe[e] = __fmul2_rn(inv2, __ffma2_rn(xe[e], bcast2(-m2), __fadd2_rn(ge[e], bcast2(-m1))));
+          }
         }
         st_stream(dxr + slot, o);
       }
