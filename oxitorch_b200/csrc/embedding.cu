@@ -185,6 +185,19 @@ __device__ __forceinline__ void store_acc(float* dst, int cols, int c_base,
   }
 }
 
+// The split and row kernels run on a linear grid: CTA b takes column chunk
+// b % chunks of row slot b / chunks, so the chunks of one row (or one block of
+// positions) run side by side and each dout row is read whole at about the
+// same time, instead of in chunk-sized pieces far apart in time.
+struct ChunkGrid {
+  int64_t slot, slots;
+  int chunk, chunks;
+};
+__device__ __forceinline__ ChunkGrid chunk_grid(int chunks) {
+  return ChunkGrid{(int64_t)(blockIdx.x / (unsigned)chunks), (int64_t)(gridDim.x / (unsigned)chunks),
+                   (int)(blockIdx.x % (unsigned)chunks), chunks};
+}
+
 // Block j of the sorted array: partial sums of the (at most two) pieces of
 // rows that occur more than kSplitP times.  Slot 2j: the row covering
 // position j*P (if split); slot 2j+1: a split row that starts inside block j.
@@ -195,16 +208,16 @@ template <int VW, int VPT, int MAXT>
 __global__ void __launch_bounds__(MAXT) emb_split_kernel(
     const float* __restrict__ dout, const int32_t* __restrict__ skeys,
     const int32_t* __restrict__ spos, const int32_t* __restrict__ offsets, int64_t n,
-    int64_t rows, int cols, float* __restrict__ parts, int64_t outer) {
+    int64_t rows, int cols, float* __restrict__ parts, int64_t outer, int chunks) {
   // emb_rows_kernel may start on the rows that need no pieces while this grid
   // runs (it was launched after the sort and offsets had completed)
   pdl_launch_dependents();
-  const int64_t j = blockIdx.x;
-  const int64_t b0 = j * kSplitP, b1 = min(n, b0 + kSplitP);
-  if (b0 >= n) return;
-  const int64_t keys2[2] = {skeys[b0], skeys[b1 - 1]};
+  const ChunkGrid cg = chunk_grid(chunks);
   const int nvec = cols / VW;
   const int64_t nblocks = (n + kSplitP - 1) / kSplitP;
+  for (int64_t j = cg.slot; j < nblocks; j += cg.slots) {
+  const int64_t b0 = j * kSplitP, b1 = min(n, b0 + kSplitP);
+  const int64_t keys2[2] = {skeys[b0], skeys[b1 - 1]};
   for (int64_t o = blockIdx.z; o < outer; o += gridDim.z) {
     const float* od = dout + o * n * (int64_t)cols;
     for (int side = 0; side < 2; ++side) {
@@ -215,8 +228,8 @@ __global__ void __launch_bounds__(MAXT) emb_split_kernel(
       if (s1 - s0 <= kSplitP) continue;
       const int64_t p0 = max(s0, b0), p1 = min(s1, b1);
       float* dst = parts + (o * 2 * nblocks + 2 * j + side) * (int64_t)cols;
-      for (int c_base = blockIdx.y * VPT * blockDim.x; c_base < nvec;
-           c_base += gridDim.y * VPT * blockDim.x) {
+      for (int c_base = cg.chunk * VPT * blockDim.x; c_base < nvec;
+           c_base += cg.chunks * VPT * blockDim.x) {
         float acc[VPT][VW];
 #pragma unroll
         for (int i = 0; i < VPT; ++i)
@@ -226,6 +239,7 @@ __global__ void __launch_bounds__(MAXT) emb_split_kernel(
         store_acc<VW, VPT>(dst, cols, c_base, acc, false);
       }
     }
+  }
   }
 }
 
@@ -276,12 +290,14 @@ __global__ void __launch_bounds__(MAXT) emb_rows_kernel(
     const float* __restrict__ dout_all, const int32_t* __restrict__ spos,
     const int32_t* __restrict__ offsets, const float* __restrict__ parts_all, int64_t rows,
     int cols, float* __restrict__ dtable, int64_t n, int64_t outer,
-    const int32_t* __restrict__ slot, const oxc_emb_push* __restrict__ push, int32_t* err) {
+    const int32_t* __restrict__ slot, const oxc_emb_push* __restrict__ push, int32_t* err,
+    int chunks) {
   // Launched as a programmatic dependent of emb_split_kernel: rows with at
   // most kSplitP occurrences read only the sort's output and run while the
   // split grid is still working; rows made of pieces wait for it (pdl_wait)
   // before reading `parts`, and every CTA waits once more before it exits,
   // so this grid never completes ahead of the split grid.
+  const ChunkGrid cg = chunk_grid(chunks);
   const int nvec = cols / VW;
   const int64_t nblocks = (n + kSplitP - 1) / kSplitP;
   bool remote = false;  // PUSH: this thread stored a row into another rank's memory
@@ -299,7 +315,7 @@ __global__ void __launch_bounds__(MAXT) emb_rows_kernel(
     }
   }
   for (int64_t o = blockIdx.z; o < outer; o += gridDim.z)
-  for (int64_t j = blockIdx.x; j < span; j += gridDim.x) {
+  for (int64_t j = cg.slot; j < span; j += cg.slots) {
     int64_t r = j;
     int p = 0;
     if constexpr (PUSH) {
@@ -330,8 +346,8 @@ __global__ void __launch_bounds__(MAXT) emb_rows_kernel(
       dst = push->rows[p] + idx * (int64_t)cols;
       remote |= p != push->source && !push->local;
     }
-    for (int c_base = blockIdx.y * VPT * blockDim.x; c_base < nvec;
-         c_base += gridDim.y * VPT * blockDim.x) {
+    for (int c_base = cg.chunk * VPT * blockDim.x; c_base < nvec;
+         c_base += cg.chunks * VPT * blockDim.x) {
       float acc[VPT][VW];
 #pragma unroll
       for (int i = 0; i < VPT; ++i)
@@ -828,6 +844,14 @@ static oxc_status emb_sort_phase(const int64_t* ids, int64_t n, int64_t vocab_to
   return check_launch("oxc_embedding_bwd (offsets)");
 }
 
+// gridDim.x of a chunk grid: `slots` row slots (or position blocks) of
+// `chunks` CTAs each, fewer slots if that would pass 2^31 - 1 CTAs (the
+// kernels loop over their slots).
+static unsigned chunk_grid_size(int64_t slots, int chunks) {
+  const int64_t most = (int64_t)0x7fffffff / chunks;
+  return (unsigned)(std::max<int64_t>(1, std::min<int64_t>(slots, most)) * chunks);
+}
+
 // hot-row pieces -> per-row sums in position order, into dtable (every row)
 // or, with `slot`, into the compact rows of the occurring ids.
 static oxc_status emb_sum_phase(const float* dout, int64_t n, int64_t rows, int64_t cols,
@@ -841,7 +865,7 @@ static oxc_status emb_sum_phase(const float* dout, int64_t n, int64_t rows, int6
   const bool v4 = cols % 4 == 0 && aligned16(dout) && aligned16(dtable);
   const int64_t nblocks = (n + kSplitP - 1) / kSplitP;
   const unsigned grows = (unsigned)std::min<int64_t>(rows, (int64_t)sm_count() * 32);
-  // Each CTA takes one column chunk of a row (blockIdx.y): kEmbChunkThreads
+  // Each CTA takes one column chunk of a row (chunk_grid): kEmbChunkThreads
   // threads with one float4 (or four floats) each.  Small CTAs keep many rows'
   // gathers in flight on every SM: on B200 at [32000, 4096] the VJP ran at
   // 4.7 / 4.9 / 5.0 / 5.1 / 5.0 / 4.8 TB/s with 1024 / 512 / 256 / 128 / 64 / 32
@@ -850,20 +874,20 @@ static oxc_status emb_sum_phase(const float* dout, int64_t n, int64_t rows, int6
   const int64_t per_thread = (int64_t)vpt * vw;
   const int block = (int)std::min<int64_t>(
       kEmbChunkThreads, std::max<int64_t>(32, ((cols / per_thread + 31) / 32) * 32));
-  const int64_t chunks = std::min<int64_t>(65535, (cols + block * per_thread - 1) / (block * per_thread));
-  const dim3 gsplit((unsigned)nblocks, (unsigned)chunks), grow(grows, (unsigned)chunks);
+  const int chunks = (int)std::min<int64_t>(65535, (cols + block * per_thread - 1) / (block * per_thread));
+  const dim3 gsplit(chunk_grid_size(nblocks, chunks)), grow(chunk_grid_size(grows, chunks));
 #define OXC_EMB_ROWS(VW, VPT, PUSH)                                                          \
   launch_dependent(emb_rows_kernel<VW, VPT, kEmbChunkThreads, PUSH>, grow, block, s, dout,   \
                    vals_out, offsets, (const float*)parts, rows, (int)cols, dtable, n,       \
-                   (int64_t)1, slot, push, err)
+                   (int64_t)1, slot, push, err, chunks)
   if (v4) {
     emb_split_kernel<4, 1, kEmbChunkThreads><<<gsplit, block, 0, s>>>(
-        dout, keys_out, vals_out, offsets, n, rows, (int)cols, parts, (int64_t)1);
+        dout, keys_out, vals_out, offsets, n, rows, (int)cols, parts, (int64_t)1, chunks);
     if (push) OXC_EMB_ROWS(4, 1, true);
     else OXC_EMB_ROWS(4, 1, false);
   } else {
     emb_split_kernel<1, 4, kEmbChunkThreads><<<gsplit, block, 0, s>>>(
-        dout, keys_out, vals_out, offsets, n, rows, (int)cols, parts, (int64_t)1);
+        dout, keys_out, vals_out, offsets, n, rows, (int)cols, parts, (int64_t)1, chunks);
     if (push) OXC_EMB_ROWS(1, 4, true);
     else OXC_EMB_ROWS(1, 4, false);
   }
@@ -1366,20 +1390,22 @@ oxc_status oxc_index_select_bwd(const float* g, const int64_t* ids, int64_t n,
   const int64_t per_thread = (int64_t)vpt * vw;
   const int block = (int)std::min<int64_t>(
       kEmbChunkThreads, std::max<int64_t>(32, ((inner / per_thread + 31) / 32) * 32));
-  const int64_t chunks = std::min<int64_t>(65535, (inner + block * per_thread - 1) / (block * per_thread));
-  const dim3 gsplit((unsigned)nblocks, (unsigned)chunks, zs), grow(grows, (unsigned)chunks, zs);
+  const int chunks = (int)std::min<int64_t>(65535, (inner + block * per_thread - 1) / (block * per_thread));
+  const dim3 gsplit(chunk_grid_size(nblocks, chunks), 1, zs), grow(chunk_grid_size(grows, chunks), 1, zs);
   if (v4) {
     emb_split_kernel<4, 1, kEmbChunkThreads><<<gsplit, block, 0, s>>>(
-        g, keys_out, vals_out, offsets, n, len, (int)inner, parts, outer);
+        g, keys_out, vals_out, offsets, n, len, (int)inner, parts, outer, chunks);
     launch_dependent(emb_rows_kernel<4, 1, kEmbChunkThreads, false>, grow, block, s, g, vals_out,
                      offsets, (const float*)parts, len, (int)inner, gx, n, outer,
-                     (const int32_t*)nullptr, (const oxc_emb_push*)nullptr, (int32_t*)nullptr);
+                     (const int32_t*)nullptr, (const oxc_emb_push*)nullptr, (int32_t*)nullptr,
+                     chunks);
   } else {
     emb_split_kernel<1, 4, kEmbChunkThreads><<<gsplit, block, 0, s>>>(
-        g, keys_out, vals_out, offsets, n, len, (int)inner, parts, outer);
+        g, keys_out, vals_out, offsets, n, len, (int)inner, parts, outer, chunks);
     launch_dependent(emb_rows_kernel<1, 4, kEmbChunkThreads, false>, grow, block, s, g, vals_out,
                      offsets, (const float*)parts, len, (int)inner, gx, n, outer,
-                     (const int32_t*)nullptr, (const oxc_emb_push*)nullptr, (int32_t*)nullptr);
+                     (const int32_t*)nullptr, (const oxc_emb_push*)nullptr, (int32_t*)nullptr,
+                     chunks);
   }
   return check_launch("oxc_index_select_bwd");
 }
